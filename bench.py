@@ -1,0 +1,511 @@
+"""Benchmark of the B200 hybrid-attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
+
+Default workload (the configuration the headline metric is quoted on):
+paged GQA decode, bf16, 128 requests, 32 q heads / 4 kv heads, head_dim 256, seq_lens ~ U[512, 8192],
+token-granular pages: each request's slots are a random draw from a 1.2M-slot pool (slot 0 reserved),
+q and K/V ~ N(0,1), sigmoid output gate from N(0,1) logits, scale 1/16.  One step = the decode
+step of one full-attention layer: KV store of the new token (a1) + paged decode with fused gate
+(a2, a4).  With N GPUs the heads are sharded exactly like the reference's tensor-parallel split
+(qwen3_8/full_attention.py:43-52, kv heads replicated once N > 4) and every rank decodes the whole
+batch for its heads: total work is fixed, so scaling is "strong".
+--config 3: Gated DeltaNet recurrent decode (B=256, Hk=16, Hv=48, dk=dv=128, fp32 state).
+
+Timing: W warm-up steps, then K steps between CUDA events on the launching stream, bracketed by a
+barrier and synchronize; the max over ranks is reported.  The K/V read per step (2.3 GB) is far
+larger than L2, so no flush is needed.  `e2e` repeats the measurement through the public API with
+the step's inputs copied from pinned host memory and its output copied back inside the timed
+region.  `cpu_baseline` times the CPU oracle (a restatement of the reference's torch algorithm) on a
+bounded sample on this host; `--impl reference` times only that.
+"""
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode attn tok/s/GPU + % of 8 TB/s HBM; extend attn TFLOP/s; 1/2/4/8 GPU"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------------------------
+# environment
+# ---------------------------------------------------------------------------------------------
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 4:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+                bits = int(parts[3], 16)
+            except ValueError:
+                continue
+            for bit, name in _REASONS.items():
+                if bits & bit and name != "gpu_idle":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _profile_traffic(name: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name> (or None)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------------------------
+# config 2: paged GQA decode
+# ---------------------------------------------------------------------------------------------
+C2 = dict(B=128, Hq=32, Hkv=4, D=256, Lmin=512, Lmax=8192, slots=1_200_000)
+
+
+def _tp_heads(hq, hkv, rank, world):
+    """Local q heads and the kv heads they read under the reference's TP split
+    (qwen3_8/full_attention.py:43-52, qwen3_8/hybrid_cache_pool.py:48)."""
+    lq = hq // world
+    if hkv >= world:
+        return lq, hkv // world
+    return lq, 1
+
+
+def _decode_inputs(seed: int, rank: int, world: int, dev):
+    B, Hq, Hkv, D, S = C2["B"], C2["Hq"], C2["Hkv"], C2["D"], C2["slots"]
+    gen = torch.Generator().manual_seed(seed)
+    lens = torch.randint(C2["Lmin"], C2["Lmax"] + 1, (B,), generator=gen)
+    perm = torch.randperm(S - 1, generator=gen)[: int(lens.sum())] + 1
+    r2t = torch.full((B, C2["Lmax"]), -1, dtype=torch.int64)
+    off = 0
+    for b in range(B):
+        n = int(lens[b])
+        r2t[b, :n] = perm[off:off + n]
+        off += n
+    lq, lkv = _tp_heads(Hq, Hkv, rank, world)
+    g = torch.Generator(device=dev).manual_seed(seed + 1 + rank)
+    kb = torch.randn((S, lkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    vb = torch.randn((S, lkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    q = torch.randn((B, lq, D), generator=g, device=dev, dtype=torch.bfloat16)
+    gate = torch.randn((B, lq, D), generator=g, device=dev, dtype=torch.bfloat16)
+    knew = torch.randn((B, lkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    vnew = torch.randn((B, lkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    out_loc = r2t[torch.arange(B), lens - 1].clone()
+    return dict(lens=lens, r2t=r2t, kb=kb, vb=vb, q=q, gate=gate, knew=knew, vnew=vnew,
+                out_loc=out_loc, lq=lq, lkv=lkv)
+
+
+def _decode_bytes(lens, lq, lkv, D):
+    """Algorithmic HBM bytes of one decode launch: K+V rows of every visible token, the int64
+    req_to_token entries, and q, gate, out."""
+    sl = int(lens.sum())
+    return sl * lkv * D * 2 * 2 + sl * 8 + 3 * len(lens) * lq * D * 2
+
+
+def bench_decode(args, rank, world, dev):
+    from tokenfactory_b200 import ops
+
+    inp = _decode_inputs(0, rank, world, dev)
+    B, D = C2["B"], C2["D"]
+    lens_d = inp["lens"].to(dev)
+    r2t_d = inp["r2t"].to(dev)
+    rpi_d = torch.arange(B, dtype=torch.int64, device=dev)
+    loc_d = inp["out_loc"].to(dev)
+    scale = D ** -0.5
+    maxL = int(inp["lens"].max())
+    out = torch.empty_like(inp["q"])
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ops.kv_store(inp["kb"], inp["vb"], loc_d, inp["knew"], inp["vnew"])
+        ops.paged_decode(inp["q"], inp["kb"], inp["vb"], r2t_d, rpi_d, lens_d, scale, maxL,
+                         gate=inp["gate"], gate_mode="sigmoid", out=out)
+
+    for _ in range(args.warmup):
+        step()
+    # device time of the whole step, plus of the decode call alone (roofline)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            e_a, e_b, e_c = ev[i]
+            e_a.record(stream)
+            ops.kv_store(inp["kb"], inp["vb"], loc_d, inp["knew"], inp["vnew"])
+            e_b.record(stream)
+            ops.paged_decode(inp["q"], inp["kb"], inp["vb"], r2t_d, rpi_d, lens_d, scale, maxL,
+                             gate=inp["gate"], gate_mode="sigmoid", out=out)
+            e_c.record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    _barrier(world)
+    elapsed = _max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
+    dec_s = sum(e_b.elapsed_time(e_c) for _, e_b, e_c in ev) / 1e3 / args.steps
+    dec_s = _max_over_ranks(dec_s, world)
+
+    # e2e through the public API: per-step inputs from pinned host memory, output back to host
+    h_q = inp["q"].cpu().pin_memory()
+    h_gate = inp["gate"].cpu().pin_memory()
+    h_k, h_v = inp["knew"].cpu().pin_memory(), inp["vnew"].cpu().pin_memory()
+    h_loc = inp["out_loc"].pin_memory()
+    h_rpi = torch.arange(B, dtype=torch.int64).pin_memory()
+    h_lens = inp["lens"].pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_q, d_gate = torch.empty_like(inp["q"]), torch.empty_like(inp["gate"])
+    d_k, d_v = torch.empty_like(inp["knew"]), torch.empty_like(inp["vnew"])
+    d_loc, d_rpi, d_lens = torch.empty_like(loc_d), torch.empty_like(rpi_d), torch.empty_like(lens_d)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_gate, h_k, h_v, h_loc, h_rpi, h_lens))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        for d, h in ((d_q, h_q), (d_gate, h_gate), (d_k, h_k), (d_v, h_v), (d_loc, h_loc),
+                     (d_rpi, h_rpi), (d_lens, h_lens)):
+            d.copy_(h, non_blocking=True)
+        ops.kv_store(inp["kb"], inp["vb"], d_loc, d_k, d_v)
+        ops.paged_decode(d_q, inp["kb"], inp["vb"], r2t_d, d_rpi, d_lens, scale, maxL,
+                         gate=d_gate, gate_mode="sigmoid", out=out)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    _barrier(world)
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_s = _max_over_ranks(s0.elapsed_time(s1) / 1e3, world)
+
+    hbm, peak_kind = _peaks()
+    nbytes = _decode_bytes(inp["lens"], inp["lq"], inp["lkv"], D)
+    achieved = nbytes / dec_s / 1e9
+    traffic = _profile_traffic("paged_decode_config2.md")
+    res = {
+        "metric": METRIC, "value": B * args.steps / elapsed, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2 paged GQA decode (one full-attention layer step)",
+                   "batch": B, "q_heads": C2["Hq"], "kv_heads": C2["Hkv"], "head_dim": D,
+                   "seq_len": f"U[{C2['Lmin']},{C2['Lmax']}]", "sum_seq_len": int(inp["lens"].sum()),
+                   "pool_slots": C2["slots"], "page_size": 1, "gate": "sigmoid",
+                   "parallelism": f"tp{world}", "local_q_heads": inp["lq"],
+                   "local_kv_heads": inp["lkv"],
+                   "l2": "no flush: each step reads 2.3 GB of K/V, far above the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_kind": peak_kind,
+                     "kernel": "tf_paged_decode_attn (plan + decode + combine)",
+                     "bytes_per_launch": nbytes,
+                     "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
+                     "traffic": traffic},
+        "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clk.summary(),
+    }
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
+# config 3: GDN recurrent decode
+# ---------------------------------------------------------------------------------------------
+C3 = dict(B=256, Hk=16, Hv=48, dk=128, dv=128, K=4, slots=512)
+
+
+def bench_gdn_decode(args, rank, world, dev):
+    from tokenfactory_b200 import ops
+
+    B, dk, dv, K = C3["B"], C3["dk"], C3["dv"], C3["K"]
+    hk, hv = C3["Hk"] // world, C3["Hv"] // world
+    conv_dim = 2 * hk * dk + hv * dv
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    bf = torch.bfloat16
+    S = C3["slots"]
+    ssm = torch.randn((S, hv, dk, dv), generator=g, device=dev) * 0.02
+    conv = torch.randn((S, conv_dim, K - 1), generator=g, device=dev, dtype=bf)
+    rpi = torch.randperm(S, generator=torch.Generator().manual_seed(4))[:B].to(dev)
+    qkv = torch.randn((B, conv_dim), generator=g, device=dev, dtype=bf)
+    bb = torch.randn((B, hv), generator=g, device=dev, dtype=bf)
+    aa = torch.randn((B, hv), generator=g, device=dev, dtype=bf)
+    z = torch.randn((B, hv * dv), generator=g, device=dev, dtype=bf)
+    w = torch.randn((conv_dim, 1, K), generator=g, device=dev, dtype=bf) * 0.5
+    A_log = (torch.rand((hv,), generator=g, device=dev) * 1.5).to(bf)
+    dt_bias = torch.randn((hv,), generator=g, device=dev, dtype=bf) * 0.5
+    nw = torch.ones((hv * dv,), device=dev, dtype=bf)
+    out = torch.empty((B, hv * dv), device=dev, dtype=bf)
+
+    def step():
+        ops.gdn_decode(qkv, bb, aa, w, A_log, dt_bias, conv, ssm, rpi, num_k_heads=hk,
+                       head_k_dim=dk, head_v_dim=dv, z=z, norm_weight=nw, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.current_stream()
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    _barrier(world)
+    el = _max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
+    nbytes = (B * hv * dk * dv * 4 * 2 + B * conv_dim * (K - 1) * 2 * 2 + B * conv_dim * 2 +
+              B * hv * dv * 2 * 2 + 2 * B * hv * 2)
+    hbm, peak_kind = _peaks()
+    achieved = nbytes / (el / args.steps) / 1e9
+    return {
+        "metric": "GDN recurrent decode tok/s", "value": B * args.steps / el, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config3 GDN recurrent decode", "batch": B, "k_heads": C3["Hk"],
+                   "v_heads": C3["Hv"], "dk": dk, "dv": dv, "parallelism": f"tp{world}",
+                   "l2": "no flush: each step streams 1.6 GB of fp32 state"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_kind": peak_kind,
+                     "kernel": "tf_gdn_decode", "bytes_per_launch": nbytes,
+                     "traffic": _profile_traffic("gdn_decode_config3.md")},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the oracle (restatement of the reference's torch algorithm) on this host
+# ---------------------------------------------------------------------------------------------
+def _cpu_decode_sample(n_requests: int, seed: int = 0):
+    """A bounded CPU sample of config 2: requests with the config's length distribution over a
+    200K-slot host pool (the GPU pool's 1.2M slots would take 5 GB of host memory)."""
+    rng = np.random.default_rng(seed)
+    S = 200_000
+    D, Hkv, Hq = C2["D"], C2["Hkv"], C2["Hq"]
+    lens = rng.integers(C2["Lmin"], C2["Lmax"] + 1, n_requests)
+    kb = rng.integers(0x3C00, 0x4000, (S, Hkv, D), dtype=np.uint16)  # finite bf16 patterns
+    vb = rng.integers(0x3C00, 0x4000, (S, Hkv, D), dtype=np.uint16)
+    r2t = np.full((n_requests, C2["Lmax"]), -1, dtype=np.int64)
+    for b in range(n_requests):
+        r2t[b, :lens[b]] = rng.integers(1, S, lens[b])
+    q = rng.integers(0x3C00, 0x4000, (n_requests, Hq, D), dtype=np.uint16)
+    return lens, kb, vb, r2t, q
+
+
+def cpu_decode_baseline(budget_s: float, threads: int):
+    """Time the oracle's slot_based_attention (one decode request per call, `threads` in
+    parallel) for about `budget_s` seconds; returns (tok/s, requests timed)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    sys.path.insert(0, ROOT)
+    from oracle import attention as OA
+
+    n = 32
+    lens, kb, vb, r2t, q = _cpu_decode_sample(n)
+    scale = C2["D"] ** -0.5
+
+    def one(b):
+        OA.slot_based_attention(q[b:b + 1], kb, vb, r2t, [b], [int(lens[b])], [1], scale,
+                                "bf16", max_seq_len=int(lens[b]))
+        return 1
+
+    one(0)  # warm
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        while time.perf_counter() - t0 < budget_s:
+            done += sum(ex.map(one, [(done + i) % n for i in range(threads)]))
+    el = time.perf_counter() - t0
+    return done / el, done
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference algorithm (oracle port) on the host CPU, rank 0 only."""
+    if rank != 0:
+        return None
+    from concurrent.futures import ThreadPoolExecutor
+
+    sys.path.insert(0, ROOT)
+    from oracle import attention as OA
+
+    threads = os.cpu_count() or 1
+    n = 32
+    lens, kb, vb, r2t, q = _cpu_decode_sample(n)
+    scale = C2["D"] ** -0.5
+
+    def one(b):
+        OA.slot_based_attention(q[b:b + 1], kb, vb, r2t, [b], [int(lens[b])], [1], scale,
+                                "bf16", max_seq_len=int(lens[b]))
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        for w in range(args.warmup):
+            list(ex.map(one, [(w * threads + i) % n for i in range(threads)]))
+        t0 = time.perf_counter()
+        for s in range(args.steps):
+            list(ex.map(one, [(s * threads + i) % n for i in range(threads)]))
+        el = time.perf_counter() - t0
+    v = threads * args.steps / el
+    sample = (f"{threads} decode requests per step (one per thread) of config 2's length "
+              f"distribution over a 200K-slot host pool")
+    return {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config2 paged GQA decode (one full-attention layer step)",
+                   "batch": C2["B"], "q_heads": C2["Hq"], "kv_heads": C2["Hkv"],
+                   "head_dim": C2["D"], "seq_len": f"U[{C2['Lmin']},{C2['Lmax']}]",
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    rank, world, local = _dist()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = bench_decode(args, rank, world, dev) if args.config == 2 else \
+        bench_gdn_decode(args, rank, world, dev)
+    if rank == 0 and world == 1 and args.config == 2:
+        threads = os.cpu_count() or 1
+        v, n = cpu_decode_baseline(args.cpu_baseline_seconds, threads)
+        res["cpu_baseline"] = {
+            "value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode requests of config 2's length distribution "
+                      f"({args.cpu_baseline_seconds:.0f} s budget, {threads} threads)"}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

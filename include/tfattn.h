@@ -1,0 +1,213 @@
+/*
+ * tfattn.h - C ABI of the B200 (sm_100a) hybrid-attention hot path of tokenFactory.
+ *
+ * The reference (yz29528/tokenFactory) is pure Python/torch and has no FFI of its own: its hot path
+ * is a handful of module methods.  Each entry point below replaces one of those methods (cited as
+ * path:line inside the reference project) and is what a ctypes binding of the reference would call.
+ *
+ * Conventions
+ *  - Every pointer is a DEVICE pointer unless stated otherwise; every stride is in ELEMENTS.
+ *  - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).  No entry point
+ *    synchronises the host, allocates device memory, or keeps per-call global state; scratch memory
+ *    is passed in by the caller (`workspace`), sized by the matching *_workspace_size() query.
+ *  - Tensors keep the reference's layouts (qwen3_8/hybrid_cache_pool.py:51-61,
+ *    req_to_state_pool.py:80-103, qwen3_8/forward_batch.py:19-31): K/V pool layer views
+ *    [num_slots, Hkv, D]; req_to_token [max_reqs, max_ctx] int64 with -1 = empty; conv_state layer
+ *    view [slots, conv_dim, K-1] in the pool dtype; ssm_state layer view [slots, Hv, dk, dv] fp32.
+ *  - Errors are returned as tf_status; tf_last_error() gives a message for the calling thread.
+ *    Optional `err` words receive in-kernel index violations (a slot or request index outside its
+ *    table); the kernel records the first violation and skips the access, it never traps.
+ */
+#ifndef TFATTN_H
+#define TFATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TFATTN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TF_API __attribute__((visibility("default")))
+#else
+#define TF_API
+#endif
+
+typedef int32_t tf_status;
+enum {
+  TF_OK = 0,
+  TF_ERR_INVALID_ARG = 1,   /* null pointer, bad shape, negative size            */
+  TF_ERR_UNSUPPORTED = 2,   /* dtype / head_dim combination not compiled         */
+  TF_ERR_ALIGNMENT = 3,     /* pointer or stride not aligned for vector access   */
+  TF_ERR_WORKSPACE = 4,     /* workspace missing or smaller than *_workspace_size */
+  TF_ERR_CUDA = 5           /* a CUDA runtime call or kernel launch failed       */
+};
+
+/* Element types of activations, pools and parameters. */
+enum { TF_DTYPE_F32 = 0, TF_DTYPE_BF16 = 1, TF_DTYPE_F16 = 2 };
+
+/* Output gate applied as out = attn * act(gate) (qwen3_8/full_attention.py:157-158 uses SiLU). */
+enum { TF_GATE_NONE = 0, TF_GATE_SILU = 1, TF_GATE_SIGMOID = 2 };
+
+/* How a negative req_to_token entry inside [0, seq_len) is read:
+ *  CLAMP: as slot 0, like the batched path's .clamp(min=0) (qwen3_8/full_attention.py:216-218);
+ *  WRAP : as num_slots + s, like torch indexing in the bsz==1 path (qwen3_8/full_attention.py:188). */
+enum { TF_SLOT_CLAMP = 0, TF_SLOT_WRAP = 1 };
+
+/* In-kernel index violations recorded in an `err` word (first one wins). */
+enum { TF_KERR_NONE = 0, TF_KERR_SLOT_RANGE = 1, TF_KERR_REQ_RANGE = 2, TF_KERR_TIMEOUT = 3 };
+
+TF_API int tf_abi_version(void);
+TF_API const char* tf_status_string(tf_status s);
+/* Message of the last failing call made by this thread ("" when none). */
+TF_API const char* tf_last_error(void);
+
+/* ------------------------------------------------------------------------------------------------
+ * a1. KV-pool store.  Replaces `layer_k_buffer[out_cache_loc] = k; layer_v_buffer[...] = v`
+ *     (qwen3_8/full_attention.py:147-149).  Bit-exact copy; negative locations wrap like torch
+ *     indexing, locations outside [-num_slots, num_slots) are recorded in `err` and skipped.
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_kv_store_args {
+  void* k_buffer;              /* [num_slots, Hkv, D] layer view                         */
+  void* v_buffer;              /* same shape and strides as k_buffer                     */
+  int64_t buf_stride_slot;     /* elements between consecutive slots                     */
+  int64_t buf_stride_head;     /* elements between consecutive kv heads                 */
+  int64_t num_slots;
+  const void* k;               /* [T, Hkv, D]                                            */
+  const void* v;               /* [T, Hkv, D]                                            */
+  int64_t k_stride_tok, k_stride_head;
+  int64_t v_stride_tok, v_stride_head;
+  const int64_t* out_cache_loc;/* [T]                                                    */
+  int64_t num_tokens;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t dtype;
+  int32_t* err;                /* optional device word                                   */
+} tf_kv_store_args;
+
+TF_API tf_status tf_kv_store(const tf_kv_store_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * a2-a4. Paged (token-granular) GQA attention through req_to_token, with the fused output gate.
+ *
+ * Query token t of request b sits at absolute position P_b + i (P_b = seq_len_b - extend_len_b,
+ * i = t - q_start_b) and attends to positions j <= P_b + i of that request, the K/V rows being
+ * k_buffer[req_to_token[req_pool_indices[b], j]].  Query head h reads kv head h / (Hq/Hkv)
+ * (repeat_interleave in qwen3_8/full_attention.py:191-193,221-227).  out = softmax(q.K^T*scale).V,
+ * then out *= act(gate) when gate_mode != NONE (qwen3_8/full_attention.py:157-158).
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_paged_attn_args {
+  const void* q;               /* [T, Hq, D]                                             */
+  int64_t q_stride_tok, q_stride_head;
+  const void* k_buffer;        /* [num_slots, Hkv, D] layer view                         */
+  const void* v_buffer;
+  int64_t kv_stride_slot, kv_stride_head;
+  int64_t num_slots;
+  const int64_t* req_to_token; /* [r2t_rows, r2t_cols]                                   */
+  int64_t r2t_stride;          /* elements between rows                                  */
+  int64_t r2t_rows, r2t_cols;
+  const int64_t* req_pool_indices; /* [B]                                                */
+  const int64_t* seq_lens;     /* [B] total length after this step                      */
+  const int64_t* extend_lens;  /* [B] new tokens per request; NULL = all 1 (decode)      */
+  const void* gate;            /* [T, Hq, D] view (head h at gate + h*gate_stride_head) or NULL */
+  int64_t gate_stride_tok, gate_stride_head;
+  void* out;                   /* [T, Hq, D]                                             */
+  int64_t out_stride_tok, out_stride_head;
+  int32_t batch_size;          /* B                                                      */
+  int32_t num_tokens;          /* T = sum(extend_lens) (= B for decode)                  */
+  int32_t num_q_heads, num_kv_heads, head_dim;
+  int32_t max_seq_len;         /* host-known max(seq_lens)   (ForwardBatch.max_seq_len)  */
+  int32_t max_extend_len;      /* host-known max(extend_lens) (ForwardBatch.max_extend_len) */
+  float scale;                 /* softmax scale, head_dim**-0.5 in the reference         */
+  int32_t dtype;               /* q, pool, gate and out dtype                            */
+  int32_t gate_mode;
+  int32_t slot_mode;           /* TF_SLOT_CLAMP or TF_SLOT_WRAP                          */
+  int32_t* err;                /* optional device word                                   */
+} tf_paged_attn_args;
+
+/* a2: pure decode batch (every extend_len == 1; qwen3_8/full_attention.py:215-242).  Split-KV with
+ * a balanced schedule over all SMs; `workspace` holds the schedule and the split partials. */
+TF_API size_t tf_paged_decode_workspace_size(const tf_paged_attn_args* args);
+TF_API tf_status tf_paged_decode_attn(const tf_paged_attn_args* args, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* a3: extend / mixed batch over a radix-cached prefix (qwen3_8/full_attention.py:179-213 for one
+ * request, :244-283 for the padded batched path).  Padded query rows do not exist here: only the
+ * T real rows are computed and written. */
+TF_API size_t tf_paged_extend_workspace_size(const tf_paged_attn_args* args);
+TF_API tf_status tf_paged_extend_attn(const tf_paged_attn_args* args, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * a5-a9. Gated DeltaNet (GDN) linear attention against req_to_state_pool.
+ *
+ * Per token: conv = causal depthwise conv1d(K taps) over [conv_state(K-1) | x] then SiLU, rounded to
+ * the pool dtype twice like the reference (conv in pool dtype, silu in pool dtype); q,k = L2-normalised
+ * (eps 1e-12), q *= dk**-0.5; v-head h reads k-head h / (Hv/Hk); g = -exp(A_log)*softplus(a+dt_bias),
+ * beta = sigmoid(b); S = exp(g)*S; S += k (beta*(v - S^T k))^T; o = S^T q
+ * (qwen3_8/linear_attention.py:133-152,154-242,244-298).  When `z` is given the gated RMSNorm
+ * epilogue out = w * o/rms_head(o) * silu(z) of qwen3_8/rms_norm_gated.py:26-40 is fused, applied to
+ * o rounded to the activation dtype as the reference does (:298 then rms_norm_gated.py:28).
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_gdn_args {
+  const void* qkv;             /* [T, conv_dim] projected q|k|v channels (pre-conv)      */
+  int64_t qkv_stride_tok;
+  const void* b;               /* [T, Hv] beta logits                                    */
+  int64_t b_stride_tok;
+  const void* a;               /* [T, Hv] decay logits                                   */
+  int64_t a_stride_tok;
+  const void* conv_weight;     /* [conv_dim, K] (nn.Conv1d weight [conv_dim,1,K], contiguous) */
+  const void* conv_bias;       /* [conv_dim] or NULL                                     */
+  const void* A_log;           /* [Hv]                                                   */
+  const void* dt_bias;         /* [Hv]                                                   */
+  void* conv_state;            /* [num_slots, conv_dim, K-1] layer view, pool dtype      */
+  int64_t conv_stride_slot;    /* channel stride must be K-1, tap stride 1               */
+  float* ssm_state;            /* [num_slots, Hv, dk, dv] layer view, fp32               */
+  int64_t ssm_stride_slot;     /* head/row strides must be dk*dv / dv                    */
+  int64_t num_slots;
+  const int64_t* req_pool_indices; /* [B]                                                */
+  const int64_t* extend_lens;  /* [B]; NULL = all 1 (tf_gdn_decode ignores it)           */
+  const void* z;               /* [T, Hv*dv] gate of the fused norm, or NULL (no norm)   */
+  int64_t z_stride_tok;
+  const void* norm_weight;     /* [norm_weight_len]: Hv*dv per channel, or dv shared     */
+  int32_t norm_weight_len;
+  float norm_eps;
+  void* out;                   /* [T, Hv*dv]                                             */
+  int64_t out_stride_tok;
+  int32_t batch_size;          /* B                                                      */
+  int32_t num_tokens;          /* T                                                      */
+  int32_t max_extend_len;      /* host-known max(extend_lens)                            */
+  int32_t num_k_heads, num_v_heads, head_k_dim, head_v_dim, conv_kernel;
+  int32_t dtype;               /* activations, conv_state and parameters                 */
+  int32_t* err;                /* optional device word                                   */
+} tf_gdn_args;
+
+/* a5 (+a9): pure decode batch, one token per request (qwen3_8/linear_attention.py:244-298). */
+TF_API tf_status tf_gdn_decode(const tf_gdn_args* args, void* stream);
+
+/* a6-a8 (+a9): varlen extend / mixed batch in one launch sequence, replacing the per-request loop
+ * (qwen3_8/linear_attention.py:329-358) of _causal_conv1d_step + _gated_delta_rule_step. */
+TF_API size_t tf_gdn_extend_workspace_size(const tf_gdn_args* args);
+TF_API tf_status tf_gdn_extend(const tf_gdn_args* args, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* a9 standalone: out = w * x/rms_head(x) * silu(z) (qwen3_8/rms_norm_gated.py:26-40). */
+typedef struct tf_gated_rmsnorm_args {
+  const void* x;  int64_t x_stride_tok;   /* [T, H*hd]                                   */
+  const void* z;  int64_t z_stride_tok;   /* [T, H*hd]                                   */
+  const void* weight; int32_t weight_len; /* H*hd per channel, or hd shared              */
+  void* out;      int64_t out_stride_tok;
+  int32_t num_tokens, num_heads, head_dim;
+  float eps;
+  int32_t dtype;
+} tf_gated_rmsnorm_args;
+
+TF_API tf_status tf_gated_rmsnorm(const tf_gated_rmsnorm_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TFATTN_H */

@@ -1,0 +1,135 @@
+"""Seeded case definitions shared by the golden-vector generator and the tests.
+
+Inputs are regenerated from these specs with numpy's PCG64 generator (stable across machines and
+numpy versions), so the committed fixtures (tests/golden/*.npz) hold only the reference's outputs
+plus a checksum of the inputs they were computed from.  Shapes follow the reference's own test
+dimensions (heads 4/1, head_dim 32, GDN 2/6 heads with dk=dv=16; tests/test_hybrid_radix_cache.py
+:127-146) and slices of the 27B shapes (head_dim 256, GQA 8, dk=dv=128).
+"""
+
+import hashlib
+from typing import Dict
+
+import numpy as np
+
+from oracle import bf16 as _bf
+
+ATTN_CASES: Dict[str, dict] = {
+    # batched decode (qwen3_8/full_attention.py:215-242)
+    "decode_bf16": dict(dtype="bf16", hq=8, hkv=2, d=64, seq=[1, 17, 64, 100], ext=[1, 1, 1, 1],
+                        req=[3, 0, 5, 1], slots=300, rows=6, cols=128, seed=11),
+    "decode_f32": dict(dtype="f32", hq=8, hkv=2, d=64, seq=[33, 2, 90], ext=[1, 1, 1],
+                       req=[1, 2, 0], slots=200, rows=4, cols=96, seed=12),
+    "decode_d256_bf16": dict(dtype="bf16", hq=8, hkv=1, d=256, seq=[5, 300, 129], ext=[1, 1, 1],
+                             req=[0, 2, 1], slots=480, rows=3, cols=320, seed=13),
+    "decode_d32_mha_bf16": dict(dtype="bf16", hq=4, hkv=4, d=32, seq=[7, 40], ext=[1, 1],
+                                req=[1, 0], slots=64, rows=2, cols=48, seed=14),
+    # -1 entries inside seq_len read padding slot 0 (clamp, :216-218)
+    "decode_negslot_bf16": dict(dtype="bf16", hq=4, hkv=1, d=32, seq=[20, 9], ext=[1, 1],
+                                req=[0, 1], slots=64, rows=2, cols=32, seed=15, neg=[(0, 3), (1, 8)]),
+    # varlen extend / mixed (qwen3_8/full_attention.py:244-283)
+    "extend_mixed_bf16": dict(dtype="bf16", hq=4, hkv=1, d=32, seq=[21, 9, 103], ext=[1, 9, 70],
+                              req=[2, 0, 1], slots=256, rows=3, cols=128, seed=21),
+    "extend_mixed_f32": dict(dtype="f32", hq=8, hkv=2, d=64, seq=[40, 66, 5], ext=[17, 66, 1],
+                             req=[0, 1, 2], slots=160, rows=3, cols=80, seed=22),
+    "extend_d256_gqa4_bf16": dict(dtype="bf16", hq=4, hkv=1, d=256, seq=[140, 10], ext=[40, 3],
+                                  req=[1, 0], slots=200, rows=2, cols=160, seed=23),
+    "extend_d128_bf16": dict(dtype="bf16", hq=4, hkv=2, d=128, seq=[150, 66], ext=[70, 66],
+                             req=[0, 1], slots=256, rows=2, cols=160, seed=24),
+    # single-request path (qwen3_8/full_attention.py:179-213)
+    "bsz1_extend_bf16": dict(dtype="bf16", hq=8, hkv=2, d=128, seq=[53], ext=[13], req=[1],
+                             slots=64, rows=2, cols=64, seed=31),
+    "bsz1_decode_f32": dict(dtype="f32", hq=8, hkv=2, d=64, seq=[77], ext=[1], req=[0],
+                            slots=100, rows=1, cols=80, seed=32),
+    # a -1 inside seq_len wraps to the last slot on the single-request path (:188)
+    "bsz1_negslot_f32": dict(dtype="f32", hq=4, hkv=2, d=32, seq=[12], ext=[1], req=[0],
+                             slots=40, rows=1, cols=16, seed=33, neg=[(0, 5)]),
+}
+
+GDN_CASES: Dict[str, dict] = {
+    # batched decode (qwen3_8/linear_attention.py:244-298)
+    "gdn_decode_bf16": dict(dtype="bf16", nk=2, nv=6, dk=16, dv=16, kc=4, ext=[1, 1, 1],
+                            req=[2, 0, 3], slots=5, seed=41),
+    "gdn_decode_f32_d64": dict(dtype="f32", nk=2, nv=4, dk=64, dv=64, kc=4, ext=[1, 1],
+                               req=[1, 0], slots=3, seed=42),
+    "gdn_decode_bf16_d128": dict(dtype="bf16", nk=1, nv=2, dk=128, dv=128, kc=4, ext=[1, 1],
+                                 req=[0, 2], slots=3, seed=43),
+    # per-request extend loop (qwen3_8/linear_attention.py:329-363)
+    "gdn_extend_bf16_mixed": dict(dtype="bf16", nk=2, nv=6, dk=16, dv=16, kc=4,
+                                  ext=[1, 5, 70, 64], req=[3, 1, 0, 2], slots=5, seed=51),
+    "gdn_extend_f32_mixed": dict(dtype="f32", nk=2, nv=4, dk=64, dv=64, kc=4, ext=[3, 1, 130],
+                                 req=[2, 0, 1], slots=4, seed=52),
+    "gdn_extend_bf16_d128": dict(dtype="bf16", nk=1, nv=3, dk=128, dv=128, kc=4, ext=[129, 2],
+                                 req=[1, 0], slots=2, seed=53),
+}
+
+
+def _normal(rng, shape, scale=1.0):
+    return (rng.standard_normal(shape, dtype=np.float32) * np.float32(scale)).astype(np.float32)
+
+
+def attn_inputs(spec: dict) -> dict:
+    """Pools, req_to_token, q and gate of an attention case (storage form of spec['dtype'])."""
+    rng = np.random.default_rng(spec["seed"])
+    dt = spec["dtype"]
+    hq, hkv, d = spec["hq"], spec["hkv"], spec["d"]
+    s = spec["slots"]
+    seq, ext, req = spec["seq"], spec["ext"], spec["req"]
+    t = int(sum(ext))
+    k_buf = _bf.store(_normal(rng, (s, hkv, d)), dt)
+    v_buf = _bf.store(_normal(rng, (s, hkv, d)), dt)
+    q = _bf.store(_normal(rng, (t, hq, d)), dt)
+    gate = _bf.store(_normal(rng, (t, hq, d)), dt)
+    r2t = np.full((spec["rows"], spec["cols"]), -1, dtype=np.int64)
+    perm = rng.permutation(np.arange(1, s, dtype=np.int64))
+    off = 0
+    for b, L in enumerate(seq):
+        r2t[req[b], :L] = perm[off:off + L]
+        off += L
+    for (b, pos) in spec.get("neg", []):
+        r2t[req[b], pos] = -1
+    out_loc = np.concatenate([r2t[req[b], seq[b] - ext[b]:seq[b]] for b in range(len(seq))])
+    return dict(q=q, k_buf=k_buf, v_buf=v_buf, gate=gate, req_to_token=r2t,
+                req_pool_indices=np.asarray(req, np.int64), seq_lens=np.asarray(seq, np.int64),
+                extend_lens=np.asarray(ext, np.int64), out_cache_loc=out_loc.astype(np.int64))
+
+
+def gdn_inputs(spec: dict) -> dict:
+    """Projected activations, parameters and the state pools of a GDN case."""
+    rng = np.random.default_rng(spec["seed"])
+    dt = spec["dtype"]
+    nk, nv, dk, dv, kc = spec["nk"], spec["nv"], spec["dk"], spec["dv"], spec["kc"]
+    conv_dim = 2 * nk * dk + nv * dv
+    t = int(sum(spec["ext"]))
+    slots = spec["slots"]
+    return dict(
+        qkv=_bf.store(_normal(rng, (t, conv_dim)), dt),
+        b=_bf.store(_normal(rng, (t, nv)), dt),
+        a=_bf.store(_normal(rng, (t, nv)), dt),
+        z=_bf.store(_normal(rng, (t, nv * dv)), dt),
+        conv_weight=_bf.store(_normal(rng, (conv_dim, kc), 0.5), dt),
+        A_log=_bf.store(rng.uniform(0.0, 1.5, nv).astype(np.float32), dt),
+        dt_bias=_bf.store(_normal(rng, (nv,), 0.5), dt),
+        norm_weight=_bf.store((1.0 + _normal(rng, (nv * dv,), 0.1)).astype(np.float32), dt),
+        conv_state=_bf.store(_normal(rng, (slots, conv_dim, kc - 1)), dt),
+        ssm_state=_normal(rng, (slots, nv, dk, dv), 0.02),
+        req_pool_indices=np.asarray(spec["req"], np.int64),
+        extend_lens=np.asarray(spec["ext"], np.int64),
+    )
+
+
+def gdn_dims(spec: dict) -> dict:
+    return dict(num_k_heads=spec["nk"], num_v_heads=spec["nv"], head_k_dim=spec["dk"],
+                head_v_dim=spec["dv"])
+
+
+def checksum(arrays: dict) -> str:
+    """sha256 over the inputs (sorted by name) - detects drift between generator and tests."""
+    h = hashlib.sha256()
+    for k in sorted(arrays):
+        a = np.ascontiguousarray(arrays[k])
+        h.update(k.encode())
+        h.update(str(a.dtype).encode())
+        h.update(str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()

@@ -1,0 +1,162 @@
+"""Generate the golden vectors of the hot path by running the REFERENCE's own torch functions.
+
+    python tests/golden/make_golden.py --reference <path to a yz29528/tokenFactory checkout>
+
+Needs the reference's Python package importable on the CPU (torch only); writes
+tests/golden/attention_golden.npz and tests/golden/gdn_golden.npz.  Inputs come from
+tests/golden/cases.py (seeded numpy), so the fixtures store outputs and an input checksum only.
+
+Reference functions exercised (paths inside the reference project):
+  Qwen3_8FullAttention._slot_based_attention   qwen3_8/full_attention.py:163-283
+  output gate attn * F.silu(gate)              qwen3_8/full_attention.py:157-158
+  Qwen3_8LinearAttention._batched_decode_step  qwen3_8/linear_attention.py:244-298
+  Qwen3_8LinearAttention._causal_conv1d_step   qwen3_8/linear_attention.py:133-152
+  Qwen3_8LinearAttention._gated_delta_rule_step qwen3_8/linear_attention.py:154-242
+  the extend loop of forward()                 qwen3_8/linear_attention.py:329-358
+  Qwen3_8RMSNormGated.forward                  qwen3_8/rms_norm_gated.py:26-40
+"""
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from tests.golden import cases as C  # noqa: E402
+
+
+# the gated outputs are recorded for the smaller cases only, to keep the fixtures small
+GATED_MAX_ELEMS = 40000
+
+
+def _t(x: np.ndarray, dtype: str) -> torch.Tensor:
+    """numpy storage (uint16 bits for bf16) -> torch tensor of the case dtype."""
+    if dtype == "bf16" and x.dtype == np.uint16:
+        return torch.from_numpy(x.view(np.int16).copy()).view(torch.bfloat16)
+    if x.dtype == np.int64:
+        return torch.from_numpy(x.copy())
+    return torch.from_numpy(np.asarray(x, np.float32).copy())
+
+
+def _np(x: torch.Tensor) -> np.ndarray:
+    """torch tensor -> numpy storage (bf16 -> uint16 bits)."""
+    x = x.detach().contiguous()
+    if x.dtype == torch.bfloat16:
+        return x.view(torch.int16).numpy().view(np.uint16).copy()
+    return x.numpy().copy()
+
+
+def _tdt(dtype: str):
+    return torch.bfloat16 if dtype == "bf16" else torch.float32
+
+
+def attention_golden(ref) -> dict:
+    from qwen3_8 import ForwardBatch, Qwen3_8Config
+    from qwen3_8.full_attention import Qwen3_8FullAttention
+
+    out = {}
+    for name, spec in C.ATTN_CASES.items():
+        inp = C.attn_inputs(spec)
+        dt = spec["dtype"]
+        cfg = Qwen3_8Config(hidden_size=64, intermediate_size=64, num_hidden_layers=1,
+                            layer_types=["full_attention"], num_attention_heads=spec["hq"],
+                            num_key_value_heads=spec["hkv"], head_dim=spec["d"])
+        fa = Qwen3_8FullAttention(cfg, 0).eval()
+        q = _t(inp["q"], dt)
+        kb, vb = _t(inp["k_buf"], dt), _t(inp["v_buf"], dt)
+        seq, ext = spec["seq"], spec["ext"]
+        fb = ForwardBatch(batch_size=len(seq), req_pool_indices=_t(inp["req_pool_indices"], dt),
+                          seq_lens=_t(inp["seq_lens"], dt),
+                          prefix_lens=_t(inp["seq_lens"] - inp["extend_lens"], dt),
+                          extend_lens=list(ext), out_cache_loc=_t(inp["out_cache_loc"], dt),
+                          req_to_token=_t(inp["req_to_token"], dt), is_prefill=max(ext) > 1,
+                          max_seq_len=max(seq), max_extend_len=max(ext),
+                          extend_lens_tensor=_t(inp["extend_lens"], dt),
+                          req_pool_indices_list=list(spec["req"]))
+        with torch.inference_mode():
+            attn = fa._slot_based_attention(q, kb, vb, fb)
+            t = attn.shape[0]
+            flat = attn.reshape(t, spec["hq"] * spec["d"])
+            gate = _t(inp["gate"], dt).reshape(t, -1)
+            silu = flat * F.silu(gate)
+            sig = flat * torch.sigmoid(gate)
+        out[f"{name}/out"] = _np(attn)
+        if attn.numel() <= GATED_MAX_ELEMS:
+            out[f"{name}/out_silu"] = _np(silu)
+            out[f"{name}/out_sigmoid"] = _np(sig)
+        out[f"{name}/checksum"] = np.frombuffer(C.checksum(inp).encode(), dtype=np.uint8)
+    return out
+
+
+def gdn_golden(ref) -> dict:
+    from qwen3_8 import Qwen3_8Config
+    from qwen3_8.linear_attention import Qwen3_8LinearAttention
+
+    out = {}
+    for name, spec in C.GDN_CASES.items():
+        inp = C.gdn_inputs(spec)
+        dt = spec["dtype"]
+        tdt = _tdt(dt)
+        cfg = Qwen3_8Config(hidden_size=64, intermediate_size=64, num_hidden_layers=1,
+                            layer_types=["linear_attention"],
+                            linear_num_key_heads=spec["nk"], linear_num_value_heads=spec["nv"],
+                            linear_key_head_dim=spec["dk"], linear_value_head_dim=spec["dv"],
+                            linear_conv_kernel_dim=spec["kc"])
+        la = Qwen3_8LinearAttention(cfg, 0).eval().to(tdt)
+        with torch.no_grad():
+            la.conv1d.weight.copy_(_t(inp["conv_weight"], dt).unsqueeze(1))
+            la.A_log.copy_(_t(inp["A_log"], dt))
+            la.dt_bias.copy_(_t(inp["dt_bias"], dt))
+            la.norm.weight.copy_(_t(inp["norm_weight"], dt))
+        qkv, b, a, z = (_t(inp[k], dt) for k in ("qkv", "b", "a", "z"))
+        conv_state = _t(inp["conv_state"], dt)
+        ssm_state = torch.from_numpy(inp["ssm_state"].copy())
+        req = spec["req"]
+        ext = spec["ext"]
+        with torch.inference_mode():
+            if all(e == 1 for e in ext):
+                raw = la._batched_decode_step(qkv, b, a, conv_state, ssm_state,
+                                              torch.tensor(req, dtype=torch.long))
+            else:
+                outs, off = [], 0
+                for i, e in enumerate(ext):
+                    r = req[i]
+                    co = la._causal_conv1d_step(qkv[off:off + e], conv_state[r])
+                    qi, ki, vi = co.split([la.key_dim, la.key_dim, la.value_dim], dim=-1)
+                    oi = la._gated_delta_rule_step(
+                        qi.reshape(e, la.num_k_heads, la.head_k_dim),
+                        ki.reshape(e, la.num_k_heads, la.head_k_dim),
+                        vi.reshape(e, la.num_v_heads, la.head_v_dim),
+                        b[off:off + e], a[off:off + e], ssm_state[r])
+                    outs.append(oi.reshape(e, la.value_dim))
+                    off += e
+                raw = torch.cat(outs, dim=0)
+            normed = la.norm(raw, z)
+        out[f"{name}/raw"] = _np(raw)
+        out[f"{name}/normed"] = _np(normed)
+        out[f"{name}/conv_state"] = _np(conv_state[req])
+        out[f"{name}/ssm_state"] = _np(ssm_state[req])
+        out[f"{name}/checksum"] = np.frombuffer(C.checksum(inp).encode(), dtype=np.uint8)
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--reference", required=True,
+                    help="root of a yz29528/tokenFactory checkout (its qwen3_8 package)")
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    torch.manual_seed(0)
+    np.savez_compressed(os.path.join(HERE, "attention_golden.npz"), **attention_golden(args))
+    np.savez_compressed(os.path.join(HERE, "gdn_golden.npz"), **gdn_golden(args))
+    for f in ("attention_golden.npz", "gdn_golden.npz"):
+        print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,49 @@
+"""Conversions between the oracle's numpy storage and torch tensors, and parity checks."""
+
+import numpy as np
+
+from oracle import bf16 as BF
+
+try:
+    import torch
+except ImportError:  # pragma: no cover
+    torch = None
+
+
+def to_torch(x: np.ndarray, dtype: str, device="cuda"):
+    """numpy storage (uint16 bits for bf16, float32, int64) -> torch tensor on `device`."""
+    if x.dtype == np.int64:
+        return torch.from_numpy(np.ascontiguousarray(x)).to(device)
+    if dtype == "bf16":
+        t = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16)
+        return t.to(device)
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(device)
+
+
+def to_numpy(t) -> np.ndarray:
+    """torch tensor -> numpy storage (bf16 -> uint16 bits)."""
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16).copy()
+    return t.numpy().copy()
+
+
+def values(t, dtype: str) -> np.ndarray:
+    """float32 values of a torch tensor of the case dtype."""
+    return BF.as_f32(to_numpy(t), dtype)
+
+
+def assert_close_bf16(got: np.ndarray, ref: np.ndarray, max_abs=2e-2, mean_abs=2e-3, what=""):
+    """The hot path's bf16 tolerance against an fp32 evaluation: max-abs 2e-2, mean-abs 2e-3."""
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    assert d.max() <= max_abs, f"{what}: max-abs {d.max():.3g} > {max_abs}"
+    assert d.mean() <= mean_abs, f"{what}: mean-abs {d.mean():.3g} > {mean_abs}"
+
+
+def assert_close(got, ref, dtype: str, what="", f32_rtol=1e-4, f32_atol=1e-5):
+    if dtype == "f32":
+        np.testing.assert_allclose(got, ref, rtol=f32_rtol, atol=f32_atol, err_msg=what)
+    else:
+        assert_close_bf16(got, ref, what=what)

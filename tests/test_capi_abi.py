@@ -1,0 +1,81 @@
+"""CPU checks of the C ABI: the library loads, exports exactly what include/tfattn.h declares, and
+the ctypes structures match the C layout (sizes and offsets from the host C compiler)."""
+
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "tfattn.h")
+
+
+def _declared_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^TF_API [^;(]*?\b(tf_\w+)\(", src, re.M)))
+
+
+def test_header_declares_every_bound_function():
+    from tokenfactory_b200 import _capi
+    assert _declared_functions() == sorted(n for n, _, _ in _capi.SIGNATURES)
+
+
+def test_library_loads_and_exports_every_declared_symbol(tmp_path):
+    from tokenfactory_b200 import _capi
+    lib = _capi.load()
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.tf_abi_version() == _capi.ABI_VERSION
+    assert lib.tf_status_string(4).decode() == "workspace missing or too small"
+    nm = shutil.which("nm")
+    if nm:
+        out = subprocess.run([nm, "-D", "--defined-only", _capi.LIB_PATH], capture_output=True,
+                             text=True).stdout
+        exported = sorted(l.split()[-1] for l in out.splitlines() if " T " in l)
+        assert exported == _declared_functions(), "only the C ABI may be exported"
+
+
+def test_invalid_arguments_fail_without_a_gpu():
+    """Validation runs before any CUDA call: a NULL pointer is rejected with a message."""
+    from tokenfactory_b200 import _capi
+    lib = _capi.load()
+    a = _capi.PagedAttnArgs(batch_size=2, num_tokens=2, num_q_heads=8, num_kv_heads=2,
+                            head_dim=64, dtype=1)
+    st = lib.tf_paged_decode_attn(ctypes.byref(a), None, 0, None)
+    assert st == _capi.TF_ERR_INVALID_ARG
+    assert b"NULL" in lib.tf_last_error()
+    g = _capi.GdnArgs(batch_size=1, num_tokens=1)
+    assert lib.tf_gdn_decode(ctypes.byref(g), None) == _capi.TF_ERR_INVALID_ARG
+
+
+_STRUCTS = {
+    "tf_kv_store_args": "KVStoreArgs",
+    "tf_paged_attn_args": "PagedAttnArgs",
+    "tf_gdn_args": "GdnArgs",
+    "tf_gated_rmsnorm_args": "GatedRMSNormArgs",
+}
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs a host C compiler")
+def test_ctypes_layout_matches_c(tmp_path):
+    from tokenfactory_b200 import _capi
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "tfattn.h"', 'int main(void){']
+    for cname, pyname in _STRUCTS.items():
+        st = getattr(_capi, pyname)
+        lines.append(f'printf("{pyname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in st._fields_:
+            lines.append(f'printf("{pyname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0;}")
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(c), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    for line in out.splitlines():
+        pyname, field, value = line.split()
+        st = getattr(_capi, pyname)
+        got = ctypes.sizeof(st) if field == "size" else getattr(st, field).offset
+        assert got == int(value), f"{pyname}.{field}: ctypes {got} != C {value}"

@@ -1,0 +1,153 @@
+"""GPU parity of the Gated DeltaNet hot path (a5-a9) through the C ABI.
+
+Compared against the golden outputs of the reference's own functions and against the oracle.
+conv_state rolls are copies and must be bit-exact; the fp32 recurrent state within rtol 1e-4 per
+step and within 1e-3 relative after 256 sequential steps; outputs within the bf16 tolerance.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import bf16 as BF
+from oracle import gdn as OG
+from tests.golden import cases as C
+from tests.golden.load import gdn_case
+from tests.helpers import assert_close, to_numpy, to_torch, values
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _tensors(inp, dt):
+    return {k: to_torch(v, "f32" if k == "ssm_state" else dt) for k, v in inp.items()}
+
+
+def _run(spec, t, fused_norm: bool, force_extend=False):
+    from tokenfactory_b200 import ops
+    ext = spec["ext"]
+    kw = dict(num_k_heads=spec["nk"], head_k_dim=spec["dk"], head_v_dim=spec["dv"])
+    z = t["z"] if fused_norm else None
+    nw = t["norm_weight"] if fused_norm else None
+    if all(e == 1 for e in ext) and not force_extend:
+        out = ops.gdn_decode(t["qkv"], t["b"], t["a"], t["conv_weight"], t["A_log"], t["dt_bias"],
+                             t["conv_state"], t["ssm_state"], t["req_pool_indices"], z=z,
+                             norm_weight=nw, **kw)
+    else:
+        out = ops.gdn_extend(t["qkv"], t["b"], t["a"], t["conv_weight"], t["A_log"],
+                             t["dt_bias"], t["conv_state"], t["ssm_state"], t["req_pool_indices"],
+                             t["extend_lens"], max_extend_len=max(ext), z=z, norm_weight=nw, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle(spec, inp, with_norm):
+    cs, ss = inp["conv_state"].copy(), inp["ssm_state"].copy()
+    params = dict(conv_weight=inp["conv_weight"], conv_bias=None, A_log=inp["A_log"],
+                  dt_bias=inp["dt_bias"], norm_weight=inp["norm_weight"])
+    out = OG.linear_attention_core(inp["qkv"], inp["b"], inp["a"],
+                                   inp["z"] if with_norm else None, params, cs, ss, spec["req"],
+                                   spec["ext"], C.gdn_dims(spec), spec["dtype"])
+    return out, cs, ss
+
+
+@pytest.mark.parametrize("name", sorted(C.GDN_CASES))
+@pytest.mark.parametrize("fused_norm", [False, True])
+def test_gdn_matches_golden_and_oracle(name, fused_norm):
+    spec, inp, gold = gdn_case(name)
+    dt = spec["dtype"]
+    t = _tensors(inp, dt)
+    out = values(_run(spec, t, fused_norm), dt)
+    orc, cs, ss = _oracle(spec, inp, fused_norm)
+    req = spec["req"]
+    np.testing.assert_array_equal(to_numpy(t["conv_state"])[req], gold["conv_state"])
+    np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+    got_ss = to_numpy(t["ssm_state"])
+    np.testing.assert_allclose(got_ss[req], gold["ssm_state"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(got_ss, ss, rtol=1e-4, atol=1e-5)
+    ref = BF.as_f32(gold["normed" if fused_norm else "raw"], dt)
+    assert_close(out, orc, dt, what=f"{name} vs oracle")
+    assert_close(out, ref, dt, what=f"{name} vs golden", f32_rtol=2e-4, f32_atol=2e-5)
+
+
+@pytest.mark.parametrize("name", ["gdn_decode_bf16", "gdn_decode_bf16_d128", "gdn_decode_f32_d64"])
+def test_decode_batch_through_extend_path(name):
+    """An all-decode batch through tf_gdn_extend equals tf_gdn_decode (same state updates)."""
+    spec, inp, _ = gdn_case(name)
+    dt = spec["dtype"]
+    t1, t2 = _tensors(inp, dt), _tensors(inp, dt)
+    a = values(_run(spec, t1, True), dt)
+    b = values(_run(spec, t2, True, force_extend=True), dt)
+    assert_close(a, b, dt, what="decode vs extend")
+    np.testing.assert_array_equal(to_numpy(t1["conv_state"]), to_numpy(t2["conv_state"]))
+    np.testing.assert_allclose(to_numpy(t1["ssm_state"]), to_numpy(t2["ssm_state"]), rtol=1e-5,
+                               atol=1e-7)
+
+
+def test_state_after_256_decode_steps_within_1e3():
+    """the recurrent state after 256 sequential decode steps stays within 1e-3
+    relative of the fp32 oracle (27B head shapes, GVA 3:1)."""
+    from tokenfactory_b200 import ops
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=[1] * 3, req=[4, 0, 2],
+                slots=5, seed=77)
+    inp = C.gdn_inputs(spec)
+    t = _tensors(inp, "bf16")
+    cs, ss = inp["conv_state"].copy(), inp["ssm_state"].copy()
+    params = dict(conv_weight=inp["conv_weight"], conv_bias=None, A_log=inp["A_log"],
+                  dt_bias=inp["dt_bias"], norm_weight=inp["norm_weight"])
+    rng = np.random.default_rng(78)
+    conv_dim = inp["qkv"].shape[1]
+    for step in range(256):
+        qkv = BF.from_f32(rng.standard_normal((3, conv_dim)).astype(np.float32))
+        b = BF.from_f32(rng.standard_normal((3, 6)).astype(np.float32))
+        a = BF.from_f32(rng.standard_normal((3, 6)).astype(np.float32))
+        OG.linear_attention_core(qkv, b, a, None, params, cs, ss, spec["req"], [1, 1, 1],
+                                 C.gdn_dims(spec), "bf16")
+        ops.gdn_decode(to_torch(qkv, "bf16"), to_torch(b, "bf16"), to_torch(a, "bf16"),
+                       t["conv_weight"], t["A_log"], t["dt_bias"], t["conv_state"],
+                       t["ssm_state"], t["req_pool_indices"], num_k_heads=2, head_k_dim=128,
+                       head_v_dim=128)
+    torch.cuda.synchronize()
+    got = to_numpy(t["ssm_state"])[spec["req"]].astype(np.float64)
+    want = ss[spec["req"]].astype(np.float64)
+    rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert rel < 1e-3, rel
+    np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+
+
+@pytest.mark.parametrize("ext", [[1, 300, 7, 64], [65, 1, 1, 129]])
+def test_extend_random_27b_heads_vs_oracle(ext):
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext,
+                req=[3, 0, 5, 1][:len(ext)], slots=6, seed=sum(ext))
+    inp = C.gdn_inputs(spec)
+    t = _tensors(inp, "bf16")
+    out = values(_run(spec, t, True), "bf16")
+    orc, cs, ss = _oracle(spec, inp, True)
+    assert_close(out, orc, "bf16", what=f"extend {ext}")
+    np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+    np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
+
+
+def test_gated_rmsnorm_standalone():
+    from tokenfactory_b200 import ops
+    rng = np.random.default_rng(3)
+    x = BF.from_f32(rng.standard_normal((37, 6 * 128)).astype(np.float32))
+    z = BF.from_f32(rng.standard_normal((37, 6 * 128)).astype(np.float32))
+    for wlen in (6 * 128, 128):
+        w = BF.from_f32((1 + 0.1 * rng.standard_normal(wlen)).astype(np.float32))
+        got = values(ops.gated_rmsnorm(to_torch(x, "bf16"), to_torch(z, "bf16"),
+                                       to_torch(w, "bf16"), 128), "bf16")
+        want = OG.rms_norm_gated(BF.to_f32(x), BF.to_f32(z), BF.to_f32(w), 128, 1e-6, "bf16")
+        assert_close(got, want, "bf16", what=f"gated rmsnorm w{wlen}")
+
+
+def test_bad_request_index_is_recorded():
+    from tokenfactory_b200 import ops
+    spec, inp, _ = gdn_case("gdn_decode_bf16")
+    t = _tensors(inp, "bf16")
+    t["req_pool_indices"][1] = 99
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.gdn_decode(t["qkv"], t["b"], t["a"], t["conv_weight"], t["A_log"], t["dt_bias"],
+                   t["conv_state"], t["ssm_state"], t["req_pool_indices"], num_k_heads=2,
+                   head_k_dim=16, head_v_dim=16, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 2  # TF_KERR_REQ_RANGE

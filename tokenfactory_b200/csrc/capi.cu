@@ -1,0 +1,274 @@
+// C ABI of libtfattn (include/tfattn.h): argument validation, device selection and dispatch.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <atomic>
+#include <string>
+
+#include "launch.h"
+#include "tfattn.h"
+
+namespace tf {
+namespace {
+
+thread_local std::string g_last_error;
+
+tf_status fail(tf_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+tf_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return TF_OK;
+  if (e == cudaErrorNotSupported)
+    return fail(TF_ERR_UNSUPPORTED, "%s: dimension combination not compiled", what);
+  return fail(TF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Runs the launch on the stream's device, restoring the caller's current device afterwards.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(cudaStream_t s) {
+    ok_ = cudaGetDevice(&prev_) == cudaSuccess;
+    int dev = prev_;
+    if (ok_ && s != nullptr && cudaStreamGetDevice(s, &dev) == cudaSuccess && dev != prev_) {
+      ok_ = cudaSetDevice(dev) == cudaSuccess;
+      switched_ = ok_;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool ok_ = false, switched_ = false;
+};
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+
+bool dtype_ok(int d) { return d == TF_DTYPE_F32 || d == TF_DTYPE_BF16 || d == TF_DTYPE_F16; }
+
+}  // namespace
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  g_sm_count[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+static tf_status check_paged(const tf_paged_attn_args* a, bool decode) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->batch_size < 0 || a->num_tokens < 0)
+    return fail(TF_ERR_INVALID_ARG, "negative batch_size (%d) or num_tokens (%d)", a->batch_size,
+                a->num_tokens);
+  if (a->batch_size == 0 || a->num_tokens == 0) return TF_OK;
+  if (!a->q || !a->k_buffer || !a->v_buffer || !a->req_to_token || !a->req_pool_indices ||
+      !a->seq_lens || !a->out)
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->num_q_heads % a->num_kv_heads != 0)
+    return fail(TF_ERR_INVALID_ARG, "num_q_heads %d is not a multiple of num_kv_heads %d",
+                a->num_q_heads, a->num_kv_heads);
+  if (a->num_q_heads / a->num_kv_heads > 64)
+    return fail(TF_ERR_UNSUPPORTED, "more than 64 query heads per kv head");
+  if (a->head_dim <= 0 || a->head_dim > 256)
+    return fail(TF_ERR_UNSUPPORTED, "head_dim %d outside [1, 256]", a->head_dim);
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  if (a->gate_mode < TF_GATE_NONE || a->gate_mode > TF_GATE_SIGMOID)
+    return fail(TF_ERR_INVALID_ARG, "unknown gate_mode %d", a->gate_mode);
+  if (a->gate_mode != TF_GATE_NONE && a->gate == nullptr)
+    return fail(TF_ERR_INVALID_ARG, "gate_mode %d needs a gate tensor", a->gate_mode);
+  if (a->slot_mode != TF_SLOT_CLAMP && a->slot_mode != TF_SLOT_WRAP)
+    return fail(TF_ERR_INVALID_ARG, "unknown slot_mode %d", a->slot_mode);
+  if (a->num_slots <= 0 || a->r2t_rows <= 0 || a->r2t_cols <= 0)
+    return fail(TF_ERR_INVALID_ARG, "empty pool or req_to_token table");
+  if (a->max_seq_len > a->r2t_cols)
+    return fail(TF_ERR_INVALID_ARG, "max_seq_len %d exceeds req_to_token columns %lld",
+                a->max_seq_len, (long long)a->r2t_cols);
+  if (decode && a->num_tokens != a->batch_size)
+    return fail(TF_ERR_INVALID_ARG, "decode batch needs num_tokens == batch_size (%d vs %d)",
+                a->num_tokens, a->batch_size);
+  if (!decode && a->extend_lens == nullptr && a->num_tokens != a->batch_size)
+    return fail(TF_ERR_INVALID_ARG, "extend batch needs extend_lens");
+  return TF_OK;
+}
+
+static tf_status check_gdn(const tf_gdn_args* a, bool decode) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->batch_size < 0 || a->num_tokens < 0) return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->batch_size == 0 || a->num_tokens == 0) return TF_OK;
+  if (!a->qkv || !a->b || !a->a || !a->conv_weight || !a->A_log || !a->dt_bias || !a->conv_state ||
+      !a->ssm_state || !a->req_pool_indices || !a->out)
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  if (a->num_k_heads <= 0 || a->num_v_heads <= 0 || a->num_v_heads % a->num_k_heads != 0)
+    return fail(TF_ERR_INVALID_ARG, "num_v_heads %d is not a multiple of num_k_heads %d",
+                a->num_v_heads, a->num_k_heads);
+  if (!gdn_dims_supported(a->head_k_dim, a->head_v_dim))
+    return fail(TF_ERR_UNSUPPORTED, "head dims dk=%d dv=%d not compiled (16/32/64/128, dk == dv)",
+                a->head_k_dim, a->head_v_dim);
+  if (a->conv_kernel < 2 || a->conv_kernel > 9)
+    return fail(TF_ERR_UNSUPPORTED, "conv_kernel %d outside [2, 9]", a->conv_kernel);
+  const int64_t conv_dim = 2LL * a->num_k_heads * a->head_k_dim + (int64_t)a->num_v_heads * a->head_v_dim;
+  if (a->conv_stride_slot < conv_dim * (a->conv_kernel - 1))
+    return fail(TF_ERR_INVALID_ARG, "conv_stride_slot %lld smaller than conv_dim*(K-1)",
+                (long long)a->conv_stride_slot);
+  if (a->ssm_stride_slot < (int64_t)a->num_v_heads * a->head_k_dim * a->head_v_dim)
+    return fail(TF_ERR_INVALID_ARG, "ssm_stride_slot %lld smaller than Hv*dk*dv",
+                (long long)a->ssm_stride_slot);
+  if ((reinterpret_cast<uintptr_t>(a->ssm_state) & 15) != 0 || (a->ssm_stride_slot & 3) != 0)
+    return fail(TF_ERR_ALIGNMENT, "ssm_state must be 16-byte aligned with a stride multiple of 4");
+  if (a->qkv_stride_tok < conv_dim)
+    return fail(TF_ERR_INVALID_ARG, "qkv_stride_tok smaller than conv_dim");
+  if (a->z != nullptr &&
+      (a->norm_weight == nullptr ||
+       (a->norm_weight_len != a->head_v_dim && a->norm_weight_len != a->num_v_heads * a->head_v_dim)))
+    return fail(TF_ERR_INVALID_ARG, "fused norm needs norm_weight of length dv or Hv*dv");
+  if (a->num_slots <= 0) return fail(TF_ERR_INVALID_ARG, "empty state pool");
+  if (decode && a->num_tokens != a->batch_size)
+    return fail(TF_ERR_INVALID_ARG, "decode batch needs num_tokens == batch_size");
+  if (!decode && a->extend_lens == nullptr)
+    return fail(TF_ERR_INVALID_ARG, "extend batch needs extend_lens");
+  return TF_OK;
+}
+
+}  // namespace tf
+
+using namespace tf;
+
+extern "C" {
+
+int tf_abi_version(void) { return TFATTN_ABI_VERSION; }
+
+const char* tf_status_string(tf_status s) {
+  switch (s) {
+    case TF_OK: return "ok";
+    case TF_ERR_INVALID_ARG: return "invalid argument";
+    case TF_ERR_UNSUPPORTED: return "unsupported configuration";
+    case TF_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case TF_ERR_WORKSPACE: return "workspace missing or too small";
+    case TF_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+const char* tf_last_error(void) { return g_last_error.c_str(); }
+
+tf_status tf_kv_store(const tf_kv_store_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->num_tokens < 0 || a->num_kv_heads < 0 || a->head_dim < 0)
+    return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->num_tokens == 0) return TF_OK;
+  if (!a->k_buffer || !a->v_buffer || !a->k || !a->v || !a->out_cache_loc)
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  if (a->num_slots <= 0) return fail(TF_ERR_INVALID_ARG, "empty pool");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_kv_store(*a, s), "tf_kv_store");
+}
+
+size_t tf_paged_decode_workspace_size(const tf_paged_attn_args* a) {
+  if (a == nullptr || a->batch_size <= 0) return 0;
+  if (!paged_decode_mma_supported(*a)) return 0;
+  return paged_decode_mma_workspace(*a, device_sm_count());
+}
+
+tf_status tf_paged_decode_attn(const tf_paged_attn_args* a, void* ws, size_t ws_bytes,
+                               void* stream) {
+  tf_status st = check_paged(a, true);
+  if (st != TF_OK || a->batch_size == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  if (paged_decode_mma_supported(*a)) {
+    const int nsm = device_sm_count();
+    const size_t need = paged_decode_mma_workspace(*a, nsm);
+    if (ws == nullptr || ws_bytes < need)
+      return fail(TF_ERR_WORKSPACE, "decode workspace of %zu bytes needed, %zu given", need,
+                  ws_bytes);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+      return fail(TF_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    return cuda_status(launch_paged_decode_mma(*a, ws, ws_bytes, nsm, s), "tf_paged_decode_attn");
+  }
+  tf_paged_attn_args d = *a;
+  d.extend_lens = nullptr;
+  return cuda_status(launch_paged_attn_simt(d, s), "tf_paged_decode_attn");
+}
+
+size_t tf_paged_extend_workspace_size(const tf_paged_attn_args* a) {
+  (void)a;
+  return 0;
+}
+
+tf_status tf_paged_extend_attn(const tf_paged_attn_args* a, void* ws, size_t ws_bytes,
+                               void* stream) {
+  (void)ws;
+  (void)ws_bytes;
+  tf_status st = check_paged(a, false);
+  if (st != TF_OK || a->batch_size == 0 || a->num_tokens == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_paged_attn_simt(*a, s), "tf_paged_extend_attn");
+}
+
+tf_status tf_gdn_decode(const tf_gdn_args* a, void* stream) {
+  tf_status st = check_gdn(a, true);
+  if (st != TF_OK || a->batch_size == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_gdn_decode(*a, s), "tf_gdn_decode");
+}
+
+size_t tf_gdn_extend_workspace_size(const tf_gdn_args* a) {
+  if (a == nullptr || a->batch_size <= 0 || a->num_tokens <= 0) return 0;
+  return gdn_extend_workspace(*a);
+}
+
+tf_status tf_gdn_extend(const tf_gdn_args* a, void* ws, size_t ws_bytes, void* stream) {
+  tf_status st = check_gdn(a, false);
+  if (st != TF_OK || a->batch_size == 0 || a->num_tokens == 0) return st;
+  const size_t need = gdn_extend_workspace(*a);
+  if (ws == nullptr || ws_bytes < need)
+    return fail(TF_ERR_WORKSPACE, "extend workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return fail(TF_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_gdn_extend(*a, ws, ws_bytes, s), "tf_gdn_extend");
+}
+
+tf_status tf_gated_rmsnorm(const tf_gated_rmsnorm_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->num_tokens < 0 || a->num_heads < 0 || a->head_dim < 0)
+    return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->num_tokens == 0 || a->num_heads == 0) return TF_OK;
+  if (!a->x || !a->z || !a->weight || !a->out)
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (a->weight_len != a->head_dim && a->weight_len != a->num_heads * a->head_dim)
+    return fail(TF_ERR_INVALID_ARG, "weight length %d is neither head_dim nor heads*head_dim",
+                a->weight_len);
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_gated_rmsnorm(*a, s), "tf_gated_rmsnorm");
+}
+
+}  // extern "C"

@@ -1,0 +1,508 @@
+// a5-a9: Gated DeltaNet (GDN) linear attention against req_to_state_pool (qwen3_8/linear_attention.py,
+// qwen3_8/rms_norm_gated.py).  HBM-bound on the fp32 recurrent state.
+//
+// State tile layout in registers: a CTA of 2*DV threads holds one [DK x DV] fp32 state; thread
+// (rg, cg) = (tid / (DV/4), tid % (DV/4)) owns rows [rg*DK/8, (rg+1)*DK/8) and the 4 columns
+// [4cg, 4cg+4), so a warp reads/writes whole 512-byte row segments (float4, coalesced).  One token
+// step is then
+//   a_j = sum_i S_ij k_i,  c_j = sum_i S_ij q_i      (row partials in registers, 8-way smem reduce)
+//   delta_j = beta (v_j - alpha a_j),  o_j = alpha c_j + delta_j (k.q)
+//   S_ij <- alpha S_ij + k_i delta_j
+// which is the reference's S = alpha S; v^ = S^T k; S += k (beta (v - v^))^T; o = S^T q
+// (linear_attention.py:184-192, 285-297) with the products regrouped, all in fp32.
+//
+// decode (tf_gdn_decode): one CTA per (request, k-head) does the causal conv of the k-head's q/k
+//   channels and of its v-heads' v channels (so it alone rolls those conv_state rows), then runs the
+//   step for each of the Hv/Hk v-heads; the state is read once and written once per token.
+// extend (tf_gdn_extend): a varlen conv kernel writes the conv outputs of every token to the
+//   workspace and a second kernel rolls conv_state; the recurrent kernel then runs one CTA per
+//   (request, v-head) over the request's tokens with the state resident in registers, so the state
+//   costs one read and one write per request instead of per token.
+#include "common.cuh"
+#include "launch.h"
+
+namespace tf {
+namespace gdn {
+
+template <int DK, int DV>
+struct Lay {
+  static constexpr int kThreads = 2 * DV;
+  static constexpr int kCG = DV / 4;   // column groups (float4 each)
+  static constexpr int kRG = 8;        // row groups
+  static constexpr int kRPT = DK / 8;  // rows per thread
+  static_assert(DK % 8 == 0 && DV % 4 == 0, "state tile");
+};
+
+// Scalars of one token for one v-head, prepared by the caller.
+struct TokenScalars {
+  float alpha, beta, inv_nq, inv_nk, kq;  // inv_nq includes the dk**-0.5 scale
+};
+
+// One recurrent step on the register-resident state.  q_s/k_s hold RAW conv outputs (the 1/||.||
+// factors are applied here), v_s the v row.  Writes o (unrounded, fp32) to o_s.
+template <int DK, int DV>
+__device__ __forceinline__ void state_step(float4 (&S)[DK / 8], const float* q_s, const float* k_s,
+                                           const float* v_s, const TokenScalars& ts, float* red_s,
+                                           float* delta_s, float* o_s) {
+  using Y = Lay<DK, DV>;
+  const int tid = threadIdx.x;
+  const int cg = tid % Y::kCG, rg = tid / Y::kCG;
+  float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int r = 0; r < Y::kRPT; ++r) {
+    const int i = rg * Y::kRPT + r;
+    const float ki = k_s[i] * ts.inv_nk, qi = q_s[i] * ts.inv_nq;
+    pa.x = fmaf(S[r].x, ki, pa.x); pa.y = fmaf(S[r].y, ki, pa.y);
+    pa.z = fmaf(S[r].z, ki, pa.z); pa.w = fmaf(S[r].w, ki, pa.w);
+    pc.x = fmaf(S[r].x, qi, pc.x); pc.y = fmaf(S[r].y, qi, pc.y);
+    pc.z = fmaf(S[r].z, qi, pc.z); pc.w = fmaf(S[r].w, qi, pc.w);
+  }
+  reinterpret_cast<float4*>(red_s + (rg * 2 + 0) * DV)[cg] = pa;
+  reinterpret_cast<float4*>(red_s + (rg * 2 + 1) * DV)[cg] = pc;
+  __syncthreads();
+  if (tid < DV) {
+    float sa = 0.f, sc = 0.f;
+#pragma unroll
+    for (int g = 0; g < Y::kRG; ++g) {
+      sa += red_s[(g * 2 + 0) * DV + tid];
+      sc += red_s[(g * 2 + 1) * DV + tid];
+    }
+    const float d = ts.beta * (v_s[tid] - ts.alpha * sa);
+    delta_s[tid] = d;
+    o_s[tid] = fmaf(ts.alpha, sc, d * ts.kq);
+  }
+  __syncthreads();
+  const float4 dl = reinterpret_cast<const float4*>(delta_s)[cg];
+#pragma unroll
+  for (int r = 0; r < Y::kRPT; ++r) {
+    const int i = rg * Y::kRPT + r;
+    const float ki = k_s[i] * ts.inv_nk;
+    S[r].x = fmaf(ts.alpha, S[r].x, ki * dl.x);
+    S[r].y = fmaf(ts.alpha, S[r].y, ki * dl.y);
+    S[r].z = fmaf(ts.alpha, S[r].z, ki * dl.z);
+    S[r].w = fmaf(ts.alpha, S[r].w, ki * dl.w);
+  }
+}
+
+template <int DK, int DV>
+__device__ __forceinline__ void load_state(float4 (&S)[DK / 8], const float* st) {
+  using Y = Lay<DK, DV>;
+  const int cg = threadIdx.x % Y::kCG, rg = threadIdx.x / Y::kCG;
+#pragma unroll
+  for (int r = 0; r < Y::kRPT; ++r)
+    S[r] = __ldcs(reinterpret_cast<const float4*>(st + (size_t)(rg * Y::kRPT + r) * DV) + cg);
+}
+
+template <int DK, int DV>
+__device__ __forceinline__ void store_state(const float4 (&S)[DK / 8], float* st) {
+  using Y = Lay<DK, DV>;
+  const int cg = threadIdx.x % Y::kCG, rg = threadIdx.x / Y::kCG;
+#pragma unroll
+  for (int r = 0; r < Y::kRPT; ++r)
+    __stcs(reinterpret_cast<float4*>(st + (size_t)(rg * Y::kRPT + r) * DV) + cg, S[r]);
+}
+
+// ||q||^2, ||k||^2 and q.k of the raw rows, one quantity per warp (round-robin); to sc_s[0..2].
+template <int DK>
+__device__ __forceinline__ void qk_norms(const float* q_s, const float* k_s, float* sc_s) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  for (int w = warp; w < 3; w += nwarps) {
+    float acc = 0.f;
+    for (int i = lane; i < DK; i += 32) {
+      const float qv = q_s[i], kv = k_s[i];
+      acc = w == 0 ? fmaf(qv, qv, acc) : (w == 1 ? fmaf(kv, kv, acc) : fmaf(qv, kv, acc));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) sc_s[w] = acc;
+  }
+}
+
+__device__ __forceinline__ TokenScalars make_scalars(const float* sc_s, float scale, float g,
+                                                     float beta) {
+  TokenScalars ts;
+  const float nq = fmaxf(sqrtf(sc_s[0]), 1e-12f), nk = fmaxf(sqrtf(sc_s[1]), 1e-12f);
+  ts.inv_nq = scale / nq;
+  ts.inv_nk = 1.0f / nk;
+  ts.kq = sc_s[2] * ts.inv_nq * ts.inv_nk;
+  ts.alpha = expf(g);
+  ts.beta = beta;
+  return ts;
+}
+
+// g = -exp(A_log) * softplus(a + dt_bias), beta = sigmoid(b)  (linear_attention.py:178-181)
+template <typename T>
+__device__ __forceinline__ void gate_values(const tf_gdn_args& a, int64_t t, int vh, float* g,
+                                            float* beta) {
+  const float av = to_f(reinterpret_cast<const T*>(a.a)[t * a.a_stride_tok + vh]);
+  const float bv = to_f(reinterpret_cast<const T*>(a.b)[t * a.b_stride_tok + vh]);
+  const float al = to_f(reinterpret_cast<const T*>(a.A_log)[vh]);
+  const float db = to_f(reinterpret_cast<const T*>(a.dt_bias)[vh]);
+  *g = -expf(al) * softplus_f(av + db);
+  *beta = 1.0f / (1.0f + expf(-bv));
+}
+
+// Output row of one v-head: o rounded to T (linear_attention.py:298), then optionally the gated
+// RMSNorm w * x/rms(x) * silu(z) (rms_norm_gated.py:26-40), by warp 0.
+template <typename T, int DV>
+__device__ __forceinline__ void write_output(const tf_gdn_args& a, int64_t t, int vh,
+                                             const float* o_s) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp != 0) return;
+  T* out = reinterpret_cast<T*>(a.out) + t * a.out_stride_tok + (int64_t)vh * DV;
+  constexpr int PER = (DV + 31) / 32;
+  float x[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int j = lane + 32 * k;
+    x[k] = j < DV ? round_to<T>(o_s[j]) : 0.f;
+    ss = fmaf(x[k], x[k], ss);
+  }
+  if (a.z == nullptr) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k)
+      if (lane + 32 * k < DV) out[lane + 32 * k] = from_f<T>(x[k]);
+    return;
+  }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / (float)DV + a.norm_eps);
+  const T* z = reinterpret_cast<const T*>(a.z) + t * a.z_stride_tok + (int64_t)vh * DV;
+  const T* w = reinterpret_cast<const T*>(a.norm_weight) +
+               (a.norm_weight_len == DV ? 0 : (int64_t)vh * DV);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int j = lane + 32 * k;
+    if (j < DV) out[j] = from_f<T>(to_f(w[j]) * (x[k] * rs) * silu_f(to_f(z[j])));
+  }
+}
+
+// depthwise causal conv of one channel at in-request position i, then SiLU, with the reference's
+// double rounding to T.  window(p) = p >= 0 ? x[p] : state[K-1+p].
+template <typename T>
+__device__ __forceinline__ float conv_channel(const tf_gdn_args& a, const T* xrow0, int64_t i,
+                                              const T* st, int c) {
+  const int K = a.conv_kernel;
+  const T* w = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * K;
+  float acc = 0.f;
+  for (int j = 0; j < K; ++j) {
+    const int64_t p = i - (K - 1) + j;
+    const float v = p >= 0 ? to_f(xrow0[p * a.qkv_stride_tok + c]) : to_f(st[c * (K - 1) + (K - 1) + p]);
+    acc = fmaf(to_f(w[j]), v, acc);
+  }
+  if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
+  return round_to<T>(silu_f(round_to<T>(acc)));
+}
+
+// ---------------------------------------------------------------------------------------------
+// decode: one CTA per (request, k-head)
+// ---------------------------------------------------------------------------------------------
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(2 * DV) decode_kernel(tf_gdn_args a) {
+  using Y = Lay<DK, DV>;
+  const int b = blockIdx.x / a.num_k_heads;
+  const int kh = blockIdx.x - b * a.num_k_heads;
+  const int vpk = a.num_v_heads / a.num_k_heads;
+  const int tid = threadIdx.x;
+  const int key_dim = a.num_k_heads * DK;
+  const int K = a.conv_kernel;
+
+  extern __shared__ float sm[];
+  float* q_s = sm;                       // [DK]
+  float* k_s = q_s + DK;                 // [DK]
+  float* v_s = k_s + DK;                 // [vpk][DV]
+  float* red_s = v_s + vpk * DV;         // [8][2][DV]
+  float* delta_s = red_s + 16 * DV;      // [DV]
+  float* o_s = delta_s + DV;             // [DV]
+  float* sc_s = o_s + DV;                // [4]
+  float* gb_s = sc_s + 4;                // [vpk][2]
+
+  const int64_t slot = a.req_pool_indices[b];
+  if (slot < 0 || slot >= a.num_slots) {
+    if (tid == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+    return;
+  }
+  float* st_base = a.ssm_state + slot * a.ssm_stride_slot;
+  float4 S[DK / 8];
+  load_state<DK, DV>(S, st_base + (size_t)(kh * vpk) * DK * DV);  // in flight during the conv
+
+  // causal conv of this CTA's channels; the CTA owns these conv_state rows
+  const T* x = reinterpret_cast<const T*>(a.qkv) + (int64_t)b * a.qkv_stride_tok;
+  T* cst = reinterpret_cast<T*>(a.conv_state) + slot * a.conv_stride_slot;
+  const int nch = 2 * DK + vpk * DV;
+  for (int e = tid; e < nch; e += blockDim.x) {
+    int c;
+    if (e < DK) c = kh * DK + e;
+    else if (e < 2 * DK) c = key_dim + kh * DK + (e - DK);
+    else c = 2 * key_dim + kh * vpk * DV + (e - 2 * DK);
+    float win[8];
+    for (int j = 0; j < K - 1; ++j) win[j] = to_f(cst[(int64_t)c * (K - 1) + j]);
+    const float xv = to_f(x[c]);
+    const T* w = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * K;
+    float acc = 0.f;
+    for (int j = 0; j < K - 1; ++j) acc = fmaf(to_f(w[j]), win[j], acc);
+    acc = fmaf(to_f(w[K - 1]), xv, acc);
+    if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
+    const float y = round_to<T>(silu_f(round_to<T>(acc)));
+    for (int j = 0; j + 1 < K - 1; ++j) cst[(int64_t)c * (K - 1) + j] = from_f<T>(win[j + 1]);
+    if (K > 1) cst[(int64_t)c * (K - 1) + K - 2] = x[c];
+    sm[e] = y;  // q_s | k_s | v_s are contiguous
+  }
+  if (tid < vpk) {
+    float g, be;
+    gate_values<T>(a, b, kh * vpk + tid, &g, &be);
+    gb_s[2 * tid] = g;
+    gb_s[2 * tid + 1] = be;
+  }
+  __syncthreads();
+  qk_norms<DK>(q_s, k_s, sc_s);
+  __syncthreads();
+  const float scale = rsqrtf((float)DK);
+  for (int j = 0; j < vpk; ++j) {
+    const int vh = kh * vpk + j;
+    if (j > 0) load_state<DK, DV>(S, st_base + (size_t)vh * DK * DV);
+    const TokenScalars ts = make_scalars(sc_s, scale, gb_s[2 * j], gb_s[2 * j + 1]);
+    state_step<DK, DV>(S, q_s, k_s, v_s + j * DV, ts, red_s, delta_s, o_s);
+    store_state<DK, DV>(S, st_base + (size_t)vh * DK * DV);
+    write_output<T, DV>(a, b, vh, o_s);
+    __syncthreads();  // o_s / delta_s reuse
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// extend: conv over every token (varlen), conv_state roll, recurrent kernel per (request, v-head)
+// ---------------------------------------------------------------------------------------------
+// token t -> request b and its first token, by one warp
+__device__ void find_request(int64_t t, const int64_t* ext, int B, int* b_out, int64_t* start_out) {
+  const int lane = threadIdx.x & 31;
+  int64_t base = 0;
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + lane;
+    const int64_t e = b < B ? ext[b] : 0;
+    int64_t incl = e;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, b < B && base + incl > t);
+    if (hit) {
+      const int l = __ffs(hit) - 1;
+      *b_out = b0 + l;
+      *start_out = base + __shfl_sync(0xffffffffu, incl - e, l);
+      return;
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  *b_out = -1;
+  *start_out = 0;
+}
+
+// token offsets of every request (exclusive prefix of extend_lens), one CTA
+__global__ void offsets_kernel(const int64_t* ext, int B, int64_t* start) {
+  if (threadIdx.x == 0) {
+    int64_t s = 0;
+    for (int b = 0; b < B; ++b) { start[b] = s; s += ext[b]; }
+    start[B] = s;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) conv_extend_kernel(tf_gdn_args a, const int64_t* start,
+                                                          T* conv_out) {
+  const int64_t t = blockIdx.x;
+  __shared__ int sb;
+  if (threadIdx.x < 32) {
+    int b; int64_t st;
+    find_request(t, a.extend_lens, a.batch_size, &b, &st);
+    if (threadIdx.x == 0) sb = b;
+  }
+  __syncthreads();
+  const int b = sb;
+  if (b < 0) return;
+  const int64_t slot = a.req_pool_indices[b];
+  if (slot < 0 || slot >= a.num_slots) {
+    if (threadIdx.x == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+    return;
+  }
+  const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
+  const T* x0 = reinterpret_cast<const T*>(a.qkv) + start[b] * a.qkv_stride_tok;
+  const T* st = reinterpret_cast<const T*>(a.conv_state) + slot * a.conv_stride_slot;
+  const int64_t i = t - start[b];
+  for (int c = threadIdx.x; c < conv_dim; c += blockDim.x)
+    conv_out[t * conv_dim + c] = from_f<T>(conv_channel<T>(a, x0, i, st, c));
+}
+
+// conv_state <- last K-1 columns of [state | x] per (request, channel)  (linear_attention.py:142-143)
+template <typename T>
+__global__ void conv_state_roll_kernel(tf_gdn_args a, const int64_t* start) {
+  const int b = blockIdx.y;
+  const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= conv_dim) return;
+  const int64_t slot = a.req_pool_indices[b];
+  if (slot < 0 || slot >= a.num_slots) return;
+  const int K = a.conv_kernel;
+  const int64_t E = a.extend_lens[b];
+  T* st = reinterpret_cast<T*>(a.conv_state) + slot * a.conv_stride_slot + (int64_t)c * (K - 1);
+  const T* x0 = reinterpret_cast<const T*>(a.qkv) + start[b] * a.qkv_stride_tok + c;
+  T nw[8];
+  for (int k = 0; k < K - 1; ++k) {
+    const int64_t p = E + k;  // index into padded = [state(K-1) | x(E)]
+    nw[k] = p < K - 1 ? st[p] : x0[(p - (K - 1)) * a.qkv_stride_tok];
+  }
+  for (int k = 0; k < K - 1; ++k) st[k] = nw[k];
+}
+
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(2 * DV) recurrent_extend_kernel(tf_gdn_args a,
+                                                                  const int64_t* start,
+                                                                  const T* conv_out) {
+  const int b = blockIdx.x / a.num_v_heads;
+  const int vh = blockIdx.x - b * a.num_v_heads;
+  const int vpk = a.num_v_heads / a.num_k_heads;
+  const int kh = vh / vpk;
+  const int tid = threadIdx.x;
+  const int key_dim = a.num_k_heads * DK;
+  const int conv_dim = 2 * key_dim + a.num_v_heads * DV;
+
+  extern __shared__ float sm[];
+  float* q_s = sm;                  // [DK]
+  float* k_s = q_s + DK;            // [DK]
+  float* v_s = k_s + DK;            // [DV]
+  float* red_s = v_s + DV;          // [8][2][DV]
+  float* delta_s = red_s + 16 * DV; // [DV]
+  float* o_s = delta_s + DV;        // [DV]
+  float* sc_s = o_s + DV;           // [4]
+  float* gb_s = sc_s + 4;           // [2]
+
+  const int64_t slot = a.req_pool_indices[b];
+  if (slot < 0 || slot >= a.num_slots) return;  // recorded by the conv kernel
+  const int64_t E = a.extend_lens[b];
+  if (E <= 0) return;
+  const int64_t t0 = start[b];
+  float* st = a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * DK * DV;
+  float4 S[DK / 8];
+  load_state<DK, DV>(S, st);
+  const float scale = rsqrtf((float)DK);
+  for (int64_t i = 0; i < E; ++i) {
+    const int64_t t = t0 + i;
+    const T* row = conv_out + t * conv_dim;
+    for (int e = tid; e < 2 * DK + DV; e += blockDim.x) {
+      int c;
+      if (e < DK) c = kh * DK + e;
+      else if (e < 2 * DK) c = key_dim + kh * DK + (e - DK);
+      else c = 2 * key_dim + vh * DV + (e - 2 * DK);
+      sm[e] = to_f(row[c]);
+    }
+    if (tid == 0) gate_values<T>(a, t, vh, &gb_s[0], &gb_s[1]);
+    __syncthreads();
+    qk_norms<DK>(q_s, k_s, sc_s);
+    __syncthreads();
+    const TokenScalars ts = make_scalars(sc_s, scale, gb_s[0], gb_s[1]);
+    state_step<DK, DV>(S, q_s, k_s, v_s, ts, red_s, delta_s, o_s);
+    write_output<T, DV>(a, t, vh, o_s);
+    __syncthreads();
+  }
+  store_state<DK, DV>(S, st);
+}
+
+template <int DK, int DV>
+constexpr size_t decode_smem(int vpk) {
+  return (size_t)(2 * DK + vpk * DV + 16 * DV + 2 * DV + 4 + 2 * vpk) * 4;
+}
+
+template <typename T, int DK, int DV>
+cudaError_t launch_decode_t(const tf_gdn_args& a, cudaStream_t s) {
+  const int vpk = a.num_v_heads / a.num_k_heads;
+  const size_t smem = decode_smem<DK, DV>(vpk);
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, DK, DV>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  decode_kernel<T, DK, DV><<<a.batch_size * a.num_k_heads, 2 * DV, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+struct ExtWs {
+  int64_t* start;  // [B+1]
+  void* conv_out;  // [T, conv_dim] of T
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+inline ExtWs carve_ext(void* base, const tf_gdn_args& a) {
+  ExtWs w;
+  w.start = (int64_t*)base;
+  w.conv_out = (char*)base + align256((size_t)(a.batch_size + 1) * 8);
+  return w;
+}
+
+template <typename T, int DK, int DV>
+cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
+  ExtWs w = carve_ext(ws, a);
+  const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+  offsets_kernel<<<1, 32, 0, s>>>(a.extend_lens, a.batch_size, w.start);
+  conv_extend_kernel<T><<<a.num_tokens, 256, 0, s>>>(a, w.start, (T*)w.conv_out);
+  dim3 rg((conv_dim + 255) / 256, a.batch_size);
+  conv_state_roll_kernel<T><<<rg, 256, 0, s>>>(a, w.start);
+  const size_t smem = (size_t)(2 * DK + DV + 16 * DV + 2 * DV + 4 + 2) * 4;
+  cudaError_t e = cudaFuncSetAttribute(recurrent_extend_kernel<T, DK, DV>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  recurrent_extend_kernel<T, DK, DV><<<a.batch_size * a.num_v_heads, 2 * DV, smem, s>>>(
+      a, w.start, (const T*)w.conv_out);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_decode(const tf_gdn_args& a, cudaStream_t s) {
+  const int dk = a.head_k_dim, dv = a.head_v_dim;
+  if (dk == 128 && dv == 128) return launch_decode_t<T, 128, 128>(a, s);
+  if (dk == 64 && dv == 64) return launch_decode_t<T, 64, 64>(a, s);
+  if (dk == 32 && dv == 32) return launch_decode_t<T, 32, 32>(a, s);
+  if (dk == 16 && dv == 16) return launch_decode_t<T, 16, 16>(a, s);
+  return cudaErrorNotSupported;
+}
+
+template <typename T>
+cudaError_t dispatch_extend(const tf_gdn_args& a, void* ws, cudaStream_t s) {
+  const int dk = a.head_k_dim, dv = a.head_v_dim;
+  if (dk == 128 && dv == 128) return launch_extend_t<T, 128, 128>(a, ws, s);
+  if (dk == 64 && dv == 64) return launch_extend_t<T, 64, 64>(a, ws, s);
+  if (dk == 32 && dv == 32) return launch_extend_t<T, 32, 32>(a, ws, s);
+  if (dk == 16 && dv == 16) return launch_extend_t<T, 16, 16>(a, ws, s);
+  return cudaErrorNotSupported;
+}
+
+}  // namespace gdn
+
+bool gdn_dims_supported(int dk, int dv) {
+  return dk == dv && (dk == 16 || dk == 32 || dk == 64 || dk == 128);
+}
+
+cudaError_t launch_gdn_decode(const tf_gdn_args& a, cudaStream_t s) {
+  if (a.batch_size == 0) return cudaSuccess;
+  switch (a.dtype) {
+    case TF_DTYPE_F32: return gdn::dispatch_decode<float>(a, s);
+    case TF_DTYPE_BF16: return gdn::dispatch_decode<__nv_bfloat16>(a, s);
+    default: return gdn::dispatch_decode<__half>(a, s);
+  }
+}
+
+size_t gdn_extend_workspace(const tf_gdn_args& a) {
+  const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
+  const size_t eb = a.dtype == TF_DTYPE_F32 ? 4 : 2;
+  return gdn::align256((size_t)(a.batch_size + 1) * 8) + (size_t)a.num_tokens * conv_dim * eb;
+}
+
+cudaError_t launch_gdn_extend(const tf_gdn_args& a, void* ws, size_t ws_bytes, cudaStream_t s) {
+  (void)ws_bytes;
+  if (a.batch_size == 0 || a.num_tokens == 0) return cudaSuccess;
+  switch (a.dtype) {
+    case TF_DTYPE_F32: return gdn::dispatch_extend<float>(a, ws, s);
+    case TF_DTYPE_BF16: return gdn::dispatch_extend<__nv_bfloat16>(a, ws, s);
+    default: return gdn::dispatch_extend<__half>(a, ws, s);
+  }
+}
+
+}  // namespace tf

@@ -1,0 +1,35 @@
+// Internal launchers behind the C ABI (capi.cu validates arguments, then calls these).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include "tfattn.h"
+
+namespace tf {
+
+// kv_store.cu
+cudaError_t launch_kv_store(const tf_kv_store_args& a, cudaStream_t s);
+
+// paged_attn_simt.cu: any dtype / head_dim <= 256, decode and extend
+cudaError_t launch_paged_attn_simt(const tf_paged_attn_args& a, cudaStream_t s);
+
+// paged_decode_mma.cu: bf16 / fp16 decode on tensor cores, balanced split-KV
+bool paged_decode_mma_supported(const tf_paged_attn_args& a);
+size_t paged_decode_mma_workspace(const tf_paged_attn_args& a, int num_sms);
+cudaError_t launch_paged_decode_mma(const tf_paged_attn_args& a, void* ws, size_t ws_bytes,
+                                    int num_sms, cudaStream_t s);
+
+// gdn.cu
+bool gdn_dims_supported(int dk, int dv);
+cudaError_t launch_gdn_decode(const tf_gdn_args& a, cudaStream_t s);
+size_t gdn_extend_workspace(const tf_gdn_args& a);
+cudaError_t launch_gdn_extend(const tf_gdn_args& a, void* ws, size_t ws_bytes, cudaStream_t s);
+
+// rmsnorm.cu
+cudaError_t launch_gated_rmsnorm(const tf_gated_rmsnorm_args& a, cudaStream_t s);
+
+// capi.cu
+int device_sm_count();
+
+}  // namespace tf

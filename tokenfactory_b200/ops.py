@@ -1,0 +1,306 @@
+"""torch-tensor front end of the C ABI (libtfattn.so).
+
+Each function takes torch CUDA tensors in the reference's layouts, checks shapes, fills the C
+argument structure with data pointers and strides, and launches on the current torch stream of the
+tensors' device.  Scratch memory comes from a per-(device, stream) workspace that is grown on demand
+and reused in stream order.  Nothing here computes on the CPU.
+"""
+
+import ctypes
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _capi as C
+
+_DTYPES = {torch.float32: C.TF_DTYPE_F32, torch.bfloat16: C.TF_DTYPE_BF16,
+           torch.float16: C.TF_DTYPE_F16}
+GATE_MODES = {"none": C.TF_GATE_NONE, "silu": C.TF_GATE_SILU, "sigmoid": C.TF_GATE_SIGMOID}
+SLOT_MODES = {"clamp": C.TF_SLOT_CLAMP, "wrap": C.TF_SLOT_WRAP}
+
+_workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _dtype(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("tokenfactory_b200 kernels need CUDA tensors (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """A 256-byte aligned scratch buffer of at least `nbytes` for the current stream of `dev`."""
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), _stream(dev))
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _workspaces[key] = buf
+    return buf
+
+
+def _i64(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.int64:
+        raise TypeError(f"{name} must be int64 (got {t.dtype})")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------------------------
+# a1. KV store
+# ---------------------------------------------------------------------------------------------
+def kv_store(k_buffer: torch.Tensor, v_buffer: torch.Tensor, out_cache_loc: torch.Tensor,
+             k: torch.Tensor, v: torch.Tensor, err: Optional[torch.Tensor] = None) -> None:
+    """k_buffer[out_cache_loc] = k; v_buffer[out_cache_loc] = v (qwen3_8/full_attention.py:147-149).
+
+    k_buffer/v_buffer: layer views [num_slots, Hkv, D]; k, v: [T, Hkv, D]; out_cache_loc [T] int64.
+    """
+    dev = _need_cuda(k_buffer, v_buffer, out_cache_loc, k, v)
+    if k.dim() != 3 or k.shape != v.shape or k_buffer.shape != v_buffer.shape:
+        raise ValueError(f"kv_store shapes: k {tuple(k.shape)} v {tuple(v.shape)} "
+                         f"pool {tuple(k_buffer.shape)} / {tuple(v_buffer.shape)}")
+    if k_buffer.stride() != v_buffer.stride() or k_buffer.stride(2) != 1 or k.stride(2) != 1 or \
+            v.stride(2) != 1:
+        raise ValueError("kv_store needs unit stride on head_dim and equal pool strides")
+    if k.shape[1:] != k_buffer.shape[1:] or k.dtype != k_buffer.dtype or v.dtype != k.dtype:
+        raise ValueError("kv_store: k/v rows must match the pool's [Hkv, D] and dtype")
+    loc = _i64(out_cache_loc, "out_cache_loc")
+    if loc.numel() != k.shape[0]:
+        raise ValueError("out_cache_loc must have one entry per token")
+    a = C.KVStoreArgs(
+        k_buffer=k_buffer.data_ptr(), v_buffer=v_buffer.data_ptr(),
+        buf_stride_slot=k_buffer.stride(0), buf_stride_head=k_buffer.stride(1),
+        num_slots=k_buffer.shape[0], k=k.data_ptr(), v=v.data_ptr(),
+        k_stride_tok=k.stride(0), k_stride_head=k.stride(1),
+        v_stride_tok=v.stride(0), v_stride_head=v.stride(1),
+        out_cache_loc=loc.data_ptr(), num_tokens=k.shape[0], num_kv_heads=k.shape[1],
+        head_dim=k.shape[2], dtype=_dtype(k), err=_ptr(err))
+    with torch.cuda.device(dev):
+        C.check("tf_kv_store", C.load().tf_kv_store(ctypes.byref(a), _stream(dev)))
+
+
+# ---------------------------------------------------------------------------------------------
+# a2-a4. paged attention
+# ---------------------------------------------------------------------------------------------
+def _paged_args(q, k_buffer, v_buffer, req_to_token, req_pool_indices, seq_lens, extend_lens,
+                scale, gate, gate_mode, out, max_seq_len, max_extend_len, slot_mode, err):
+    if q.dim() != 3 or k_buffer.dim() != 3 or k_buffer.shape != v_buffer.shape:
+        raise ValueError(f"paged attention shapes: q {tuple(q.shape)}, pool {tuple(k_buffer.shape)}")
+    t, hq, d = q.shape
+    if k_buffer.shape[2] != d or hq % k_buffer.shape[1] != 0:
+        raise ValueError("q heads must be a multiple of kv heads and head dims must agree")
+    if q.stride(2) != 1 or k_buffer.stride(2) != 1 or out.stride(2) != 1 or \
+            k_buffer.stride() != v_buffer.stride():
+        raise ValueError("paged attention needs unit stride on head_dim")
+    if q.dtype != k_buffer.dtype or v_buffer.dtype != q.dtype or out.dtype != q.dtype:
+        raise TypeError("q, pools and out must share a dtype")
+    if gate is not None:
+        if gate.shape != q.shape or gate.stride(2) != 1 or gate.dtype != q.dtype:
+            raise ValueError("gate must be a [T, Hq, D] view with unit stride on D")
+    r2t = req_to_token
+    if r2t.dtype != torch.int64 or r2t.dim() != 2 or r2t.stride(1) != 1:
+        raise ValueError("req_to_token must be a row-major int64 [rows, cols] table")
+    rpi = _i64(req_pool_indices, "req_pool_indices")
+    sl = _i64(seq_lens, "seq_lens")
+    el = None if extend_lens is None else _i64(extend_lens, "extend_lens")
+    return C.PagedAttnArgs(
+        q=q.data_ptr(), q_stride_tok=q.stride(0), q_stride_head=q.stride(1),
+        k_buffer=k_buffer.data_ptr(), v_buffer=v_buffer.data_ptr(),
+        kv_stride_slot=k_buffer.stride(0), kv_stride_head=k_buffer.stride(1),
+        num_slots=k_buffer.shape[0],
+        req_to_token=r2t.data_ptr(), r2t_stride=r2t.stride(0), r2t_rows=r2t.shape[0],
+        r2t_cols=r2t.shape[1],
+        req_pool_indices=rpi.data_ptr(), seq_lens=sl.data_ptr(),
+        extend_lens=None if el is None else el.data_ptr(),
+        gate=_ptr(gate), gate_stride_tok=0 if gate is None else gate.stride(0),
+        gate_stride_head=0 if gate is None else gate.stride(1),
+        out=out.data_ptr(), out_stride_tok=out.stride(0), out_stride_head=out.stride(1),
+        batch_size=rpi.numel(), num_tokens=t, num_q_heads=hq, num_kv_heads=k_buffer.shape[1],
+        head_dim=d, max_seq_len=int(max_seq_len), max_extend_len=int(max_extend_len),
+        scale=float(scale), dtype=_dtype(q), gate_mode=GATE_MODES[gate_mode],
+        slot_mode=SLOT_MODES[slot_mode], err=_ptr(err)), (rpi, sl, el)
+
+
+def paged_decode(q: torch.Tensor, k_buffer: torch.Tensor, v_buffer: torch.Tensor,
+                 req_to_token: torch.Tensor, req_pool_indices: torch.Tensor,
+                 seq_lens: torch.Tensor, scale: float, max_seq_len: int,
+                 gate: Optional[torch.Tensor] = None, gate_mode: str = "none",
+                 out: Optional[torch.Tensor] = None, slot_mode: str = "clamp",
+                 err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode step of paged GQA attention, one query token per request
+    (qwen3_8/full_attention.py:215-242), with the output gate fused (:157-158).  Returns
+    out [B, Hq, D]."""
+    dev = _need_cuda(q, k_buffer, v_buffer, req_to_token, req_pool_indices, seq_lens, gate)
+    if out is None:
+        out = torch.empty_like(q)
+    args, keep = _paged_args(q, k_buffer, v_buffer, req_to_token, req_pool_indices, seq_lens,
+                             None, scale, gate, gate_mode, out, max_seq_len, 1, slot_mode, err)
+    lib = C.load()
+    with torch.cuda.device(dev):
+        nbytes = lib.tf_paged_decode_workspace_size(ctypes.byref(args))
+        ws = workspace(dev, nbytes) if nbytes else None
+        C.check("tf_paged_decode_attn",
+                lib.tf_paged_decode_attn(ctypes.byref(args), _ptr(ws), nbytes, _stream(dev)))
+    del keep
+    return out
+
+
+def paged_extend(q: torch.Tensor, k_buffer: torch.Tensor, v_buffer: torch.Tensor,
+                 req_to_token: torch.Tensor, req_pool_indices: torch.Tensor,
+                 seq_lens: torch.Tensor, extend_lens: torch.Tensor, scale: float,
+                 max_seq_len: int, max_extend_len: int, gate: Optional[torch.Tensor] = None,
+                 gate_mode: str = "none", out: Optional[torch.Tensor] = None,
+                 slot_mode: str = "clamp", err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Varlen extend over a radix-cached prefix (qwen3_8/full_attention.py:179-213, 244-283):
+    query i of request b attends to positions <= seq_len_b - extend_len_b + i.  q is packed
+    [T, Hq, D] in request order.  Returns out [T, Hq, D]."""
+    dev = _need_cuda(q, k_buffer, v_buffer, req_to_token, req_pool_indices, seq_lens,
+                     extend_lens, gate)
+    if out is None:
+        out = torch.empty_like(q)
+    args, keep = _paged_args(q, k_buffer, v_buffer, req_to_token, req_pool_indices, seq_lens,
+                             extend_lens, scale, gate, gate_mode, out, max_seq_len,
+                             max_extend_len, slot_mode, err)
+    lib = C.load()
+    with torch.cuda.device(dev):
+        nbytes = lib.tf_paged_extend_workspace_size(ctypes.byref(args))
+        ws = workspace(dev, nbytes) if nbytes else None
+        C.check("tf_paged_extend_attn",
+                lib.tf_paged_extend_attn(ctypes.byref(args), _ptr(ws), nbytes, _stream(dev)))
+    del keep
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# a5-a9. Gated DeltaNet
+# ---------------------------------------------------------------------------------------------
+def _gdn_args(qkv, b, a, conv_weight, conv_bias, A_log, dt_bias, conv_state, ssm_state,
+              req_pool_indices, extend_lens, z, norm_weight, norm_eps, out, num_k_heads,
+              head_k_dim, head_v_dim, max_extend_len, err):
+    t, conv_dim = qkv.shape
+    hv = b.shape[1]
+    kc = conv_weight.shape[-1]
+    if conv_dim != 2 * num_k_heads * head_k_dim + hv * head_v_dim:
+        raise ValueError(f"qkv width {conv_dim} != 2*Hk*dk + Hv*dv")
+    if conv_state.dim() != 3 or conv_state.shape[1:] != (conv_dim, kc - 1) or \
+            conv_state.stride(2) != 1 or conv_state.stride(1) != kc - 1:
+        raise ValueError(f"conv_state must be a [slots, {conv_dim}, {kc - 1}] view, channel-major")
+    if ssm_state.dim() != 4 or ssm_state.shape[1:] != (hv, head_k_dim, head_v_dim) or \
+            ssm_state.dtype != torch.float32 or \
+            ssm_state.stride()[1:] != (head_k_dim * head_v_dim, head_v_dim, 1):
+        raise ValueError("ssm_state must be a float32 [slots, Hv, dk, dv] view, contiguous per slot")
+    if conv_state.shape[0] != ssm_state.shape[0]:
+        raise ValueError("conv_state and ssm_state must have the same slots")
+    for name, x in (("qkv", qkv), ("b", b), ("a", a), ("out", out)):
+        if x.stride(-1) != 1:
+            raise ValueError(f"{name} needs unit stride on its last dim")
+    if z is not None and z.stride(-1) != 1:
+        raise ValueError("z needs unit stride on its last dim")
+    cw = conv_weight.reshape(conv_dim, kc)
+    if not cw.is_contiguous():
+        cw = cw.contiguous()
+    dt = qkv.dtype
+    for name, x in (("b", b), ("a", a), ("conv_weight", cw), ("A_log", A_log),
+                    ("dt_bias", dt_bias), ("conv_state", conv_state), ("out", out)):
+        if x.dtype != dt:
+            raise TypeError(f"{name} has dtype {x.dtype}, expected {dt} (one model dtype)")
+    rpi = _i64(req_pool_indices, "req_pool_indices")
+    el = None if extend_lens is None else _i64(extend_lens, "extend_lens")
+    A_log_c, dt_bias_c = A_log.contiguous(), dt_bias.contiguous()
+    nw = None if norm_weight is None else norm_weight.contiguous()
+    bias = None if conv_bias is None else conv_bias.contiguous()
+    args = C.GdnArgs(
+        qkv=qkv.data_ptr(), qkv_stride_tok=qkv.stride(0), b=b.data_ptr(), b_stride_tok=b.stride(0),
+        a=a.data_ptr(), a_stride_tok=a.stride(0), conv_weight=cw.data_ptr(), conv_bias=_ptr(bias),
+        A_log=A_log_c.data_ptr(), dt_bias=dt_bias_c.data_ptr(),
+        conv_state=conv_state.data_ptr(), conv_stride_slot=conv_state.stride(0),
+        ssm_state=ssm_state.data_ptr(), ssm_stride_slot=ssm_state.stride(0),
+        num_slots=ssm_state.shape[0], req_pool_indices=rpi.data_ptr(),
+        extend_lens=_ptr(el), z=_ptr(z), z_stride_tok=0 if z is None else z.stride(0),
+        norm_weight=_ptr(nw), norm_weight_len=0 if nw is None else nw.numel(),
+        norm_eps=float(norm_eps), out=out.data_ptr(), out_stride_tok=out.stride(0),
+        batch_size=rpi.numel(), num_tokens=t, max_extend_len=int(max_extend_len),
+        num_k_heads=num_k_heads, num_v_heads=hv, head_k_dim=head_k_dim, head_v_dim=head_v_dim,
+        conv_kernel=kc, dtype=_dtype(qkv), err=_ptr(err))
+    return args, (cw, rpi, el, A_log_c, dt_bias_c, nw, bias)
+
+
+def gdn_decode(qkv, b, a, conv_weight, A_log, dt_bias, conv_state, ssm_state, req_pool_indices,
+               num_k_heads: int, head_k_dim: int, head_v_dim: int, conv_bias=None, z=None,
+               norm_weight=None, norm_eps: float = 1e-6, out=None, err=None) -> torch.Tensor:
+    """Batched one-token GDN step (qwen3_8/linear_attention.py:244-298) updating conv_state and
+    ssm_state in place at the request rows; with z given, the gated RMSNorm of
+    qwen3_8/rms_norm_gated.py:26-40 is fused.  Returns out [B, Hv*dv]."""
+    dev = _need_cuda(qkv, b, a, conv_weight, A_log, dt_bias, conv_state, ssm_state,
+                     req_pool_indices, z, norm_weight)
+    if out is None:
+        out = torch.empty((qkv.shape[0], b.shape[1] * head_v_dim), dtype=qkv.dtype, device=dev)
+    args, keep = _gdn_args(qkv, b, a, conv_weight, conv_bias, A_log, dt_bias, conv_state,
+                           ssm_state, req_pool_indices, None, z, norm_weight, norm_eps, out,
+                           num_k_heads, head_k_dim, head_v_dim, 1, err)
+    with torch.cuda.device(dev):
+        C.check("tf_gdn_decode", C.load().tf_gdn_decode(ctypes.byref(args), _stream(dev)))
+    del keep
+    return out
+
+
+def gdn_extend(qkv, b, a, conv_weight, A_log, dt_bias, conv_state, ssm_state, req_pool_indices,
+               extend_lens, num_k_heads: int, head_k_dim: int, head_v_dim: int,
+               max_extend_len: int, conv_bias=None, z=None, norm_weight=None,
+               norm_eps: float = 1e-6, out=None, err=None) -> torch.Tensor:
+    """Varlen GDN over packed tokens of several requests (extend / mixed batches), replacing the
+    per-request loop of qwen3_8/linear_attention.py:329-358.  Returns out [T, Hv*dv]."""
+    dev = _need_cuda(qkv, b, a, conv_weight, A_log, dt_bias, conv_state, ssm_state,
+                     req_pool_indices, extend_lens, z, norm_weight)
+    if out is None:
+        out = torch.empty((qkv.shape[0], b.shape[1] * head_v_dim), dtype=qkv.dtype, device=dev)
+    args, keep = _gdn_args(qkv, b, a, conv_weight, conv_bias, A_log, dt_bias, conv_state,
+                           ssm_state, req_pool_indices, extend_lens, z, norm_weight, norm_eps,
+                           out, num_k_heads, head_k_dim, head_v_dim, max_extend_len, err)
+    lib = C.load()
+    with torch.cuda.device(dev):
+        nbytes = lib.tf_gdn_extend_workspace_size(ctypes.byref(args))
+        ws = workspace(dev, nbytes) if nbytes else None
+        C.check("tf_gdn_extend",
+                lib.tf_gdn_extend(ctypes.byref(args), _ptr(ws), nbytes, _stream(dev)))
+    del keep
+    return out
+
+
+def gated_rmsnorm(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, head_dim: int,
+                  eps: float = 1e-6, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """w * x/rms_head(x) * silu(z) (qwen3_8/rms_norm_gated.py:26-40); x, z [T, H*hd]."""
+    dev = _need_cuda(x, z, weight)
+    if out is None:
+        out = torch.empty_like(x)
+    if x.shape != z.shape or x.stride(-1) != 1 or z.stride(-1) != 1 or x.shape[1] % head_dim:
+        raise ValueError("gated_rmsnorm: x and z must be [T, H*head_dim] with unit inner stride")
+    w = weight.contiguous()
+    args = C.GatedRMSNormArgs(
+        x=x.data_ptr(), x_stride_tok=x.stride(0), z=z.data_ptr(), z_stride_tok=z.stride(0),
+        weight=w.data_ptr(), weight_len=w.numel(), out=out.data_ptr(),
+        out_stride_tok=out.stride(0), num_tokens=x.shape[0], num_heads=x.shape[1] // head_dim,
+        head_dim=head_dim, eps=float(eps), dtype=_dtype(x))
+    with torch.cuda.device(dev):
+        C.check("tf_gated_rmsnorm", C.load().tf_gated_rmsnorm(ctypes.byref(args), _stream(dev)))
+    return out
