@@ -175,6 +175,8 @@ def _decode_inputs(seed: int, rank: int, world: int, dev):
     B, Hq, Hkv, D, S = C2["B"], C2["Hq"], C2["Hkv"], C2["D"], C2["slots"]
     gen = torch.Generator().manual_seed(seed)
     lens = torch.randint(C2["Lmin"], C2["Lmax"] + 1, (B,), generator=gen)
+    if int(lens.sum()) > S - 1:
+        raise ValueError(f"pool of {S} slots too small for {int(lens.sum())} tokens")
     perm = torch.randperm(S - 1, generator=gen)[: int(lens.sum())] + 1
     r2t = torch.full((B, C2["Lmax"]), -1, dtype=torch.int64)
     off = 0
@@ -247,6 +249,13 @@ def bench_decode(args, rank, world, dev):
     dec_s = sum(e_b.elapsed_time(e_c) for _, e_b, e_c in ev) / 1e3 / args.steps
     dec_s = _max_over_ranks(dec_s, world)
 
+    hbm, peak_kind = _peaks()
+    nbytes = _decode_bytes(inp["lens"], inp["lq"], inp["lkv"], D)
+    achieved = nbytes / dec_s / 1e9
+    if args.no_e2e:
+        return dict(value=B * args.steps / elapsed, ms=elapsed / args.steps * 1e3,
+                    achieved_gbs=achieved, frac=achieved / hbm)
+
     # e2e through the public API: per-step inputs from pinned host memory, output back to host
     h_q = inp["q"].cpu().pin_memory()
     h_gate = inp["gate"].cpu().pin_memory()
@@ -283,9 +292,6 @@ def bench_decode(args, rank, world, dev):
     _barrier(world)
     e2e_s = _max_over_ranks(s0.elapsed_time(s1) / 1e3, world)
 
-    hbm, peak_kind = _peaks()
-    nbytes = _decode_bytes(inp["lens"], inp["lq"], inp["lkv"], D)
-    achieved = nbytes / dec_s / 1e9
     traffic = _profile_traffic("paged_decode_config2.md")
     res = {
         "metric": METRIC, "value": B * args.steps / elapsed, "unit": "tok/s",
@@ -476,7 +482,14 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
+    ap.add_argument("--batch", type=int, default=C2["B"],
+                    help="profiling only: decode batch (default: config 2's 128)")
+    ap.add_argument("--pool-slots", type=int, default=C2["slots"],
+                    help="profiling only: KV pool slots (default: config 2's 1.2M)")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="profiling only: device-timed leg alone, short output")
     args = ap.parse_args()
+    C2["B"], C2["slots"] = args.batch, args.pool_slots
     args.warmup = max(3, args.warmup)
 
     if args.impl == "reference":
@@ -493,7 +506,8 @@ def main():
     dev = torch.device("cuda", torch.cuda.current_device())
     res = bench_decode(args, rank, world, dev) if args.config == 2 else \
         bench_gdn_decode(args, rank, world, dev)
-    if rank == 0 and world == 1 and args.config == 2:
+    if rank == 0 and world == 1 and args.config == 2 and not args.no_e2e and \
+            args.cpu_baseline_seconds > 0:
         threads = os.cpu_count() or 1
         v, n = cpu_decode_baseline(args.cpu_baseline_seconds, threads)
         res["cpu_baseline"] = {

@@ -2,46 +2,60 @@
 // gate of :157-158), HBM-bound by design.
 //
 // Work decomposition (balanced split-KV).  A unit is (request b, kv head h); its keys are cut into
-// tiles of 32 tokens.  All tiles of all units form one sequence (request-major, then kv head), and
+// tiles of 16 tokens.  All tiles of all units form one sequence (request-major, then kv head), and
 // persistent CTA c (one per SM) takes the contiguous range [c*T/G, (c+1)*T/G) of it, so every SM
 // streams the same number of K/V bytes whatever the spread of seq_lens.  A unit that lies inside one
 // CTA range is finished in place; a unit cut by range boundaries leaves (max, sum, unnormalised O)
 // partials that a combine kernel merges.  A plan kernel computes the tile prefix over requests on
 // the device, so nothing about seq_lens needs to reach the host.
 //
-// Inside a CTA: one producer warp gathers the token rows of each tile (slot ids from req_to_token,
-// 16-byte cp.async per lane, XOR-swizzled rows) into a ring of shared-memory stages, signalling each
-// stage's full mbarrier with cp.async.mbarrier.arrive; four consumer warps take tiles round-robin.
-// A consumer computes S^T = K.Q^T with mma.m16n8k16 (A = 16 tokens x 16 dims of K via ldmatrix,
-// B = Q^T of the 8 query heads sharing the kv head), keeps an online softmax per head in registers,
-// turns P into the B operand of O^T = V^T.P^T with movmatrix (8x8 transpose in registers) and
-// accumulates O^T[D x 8] in registers (V^T via ldmatrix.trans).  The four warps merge through
-// shared memory at the end of each unit piece.  Every mbarrier wait is bounded.
+// Inside a CTA the eight warps take the tiles of a unit round-robin and stream K/V rows straight
+// from HBM into registers with 16-byte loads (no shared-memory staging: many warps with loads in
+// flight is what saturates HBM for 512-byte random rows), one tile ahead, slot ids two tiles ahead.
+// The tensor cores consume the loaded registers directly:
+//   S^T = K.Q^T   mma.m16n8k16, A = 16 tokens x 16 dims of K.  The reduction over dims may visit
+//                 the dims in any order as long as Q^T uses the same order, so the k-step order is
+//                 chosen such that a thread's 16-byte load (8 consecutive dims of one token) IS its
+//                 A fragment for two k-steps: k-step 2j takes dims 32j+8t+{0,1 | 2,3}, k-step 2j+1
+//                 dims 32j+8t+{4,5 | 6,7} (t = lane%4); Q^T is read from shared memory in the same
+//                 order.  B = Q^T of the 8 query heads sharing the kv head (GQA packed in n).
+//   O^T = V^T.P^T A = V^T, 16 dims x 16 tokens.  Each 32-bit word of a V load is one row of an 8x8
+//                 (token x dim-pair) matrix fragment; movmatrix.trans turns it into the A fragment of
+//                 V^T for a dim permutation phi_c(g) = 32j + 8(g>>1) + 2c + (g&1), undone when the
+//                 warps merge.  P^T (B operand) comes from the S^T accumulator through movmatrix.
+// Online softmax per query head in registers; the eight warps merge through shared memory at the
+// end of each unit piece.
 #include "common.cuh"
 #include "launch.h"
 
 namespace tf {
 namespace dec {
 
-constexpr int kTileTok = 32;
-constexpr int kConsumers = 4;
-constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kTileTok = 16;
+constexpr int kWarps = 8;
+constexpr int kThreads = 32 * kWarps;
 constexpr int kHeads = 8;  // n of the mma tiles: query heads per kv head, padded to 8
 constexpr float kLog2e = 1.4426950408889634f;
 
+constexpr int kMaxCachedReqs = 256;
+
+struct ReqCache {
+  int bf, n;  // cached requests [bf, bf + n)
+  int32_t ts[kMaxCachedReqs + 1];
+  int64_t row_off[kMaxCachedReqs];  // req_pool_indices[b] * r2t_stride (validated)
+  int64_t len[kMaxCachedReqs];
+};
+
 template <int D>
 struct Cfg {
-  static constexpr int kRowBytes = D * 2;
-  static constexpr int kTileBytes = kTileTok * kRowBytes;  // K (or V) rows of one tile
-  static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStages = D == 256 ? 5 : 8;
-  static constexpr int kChunks = D / 8;  // 16-byte chunks per row
-  static constexpr int kRowsPerIssue = 32 / kChunks;
-  static constexpr int kOStride = D + 4;  // merge buffer row stride (floats), bank-conflict free
-  static constexpr size_t kStagesBytes = (size_t)kStages * kStageBytes;
-  static constexpr size_t kMergeBytes = (size_t)kConsumers * kHeads * kOStride * 4 +
-                                        2 * kConsumers * kHeads * 4;
-  static constexpr size_t kSmem = kStagesBytes + kMergeBytes + 2 * kStages * 8 + 64;
+  static constexpr int kBlocks = D / 32;  // 32-dim blocks
+  static constexpr int kQStride = D + 8;  // bf16 per q_s row: +16 B keeps LDS.128 conflict-free
+  static constexpr int kOStride = D + 4;  // floats per merge row
+  static constexpr size_t kQBytes = (size_t)kHeads * kQStride * 2;
+  static constexpr size_t kMergeBytes = (size_t)kWarps * kHeads * kOStride * 4 +
+                                        2 * (size_t)kWarps * kHeads * 4;
+  static constexpr size_t kCacheOff = (kQBytes + kMergeBytes + 15) & ~(size_t)15;
+  static constexpr size_t kSmem = kCacheOff + sizeof(ReqCache);
 };
 
 struct Ws {
@@ -115,8 +129,43 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int
 }
 
 // ---------------------------------------------------------------------------------------------
-// walking the tile sequence
+// walking the tile sequence.  The per-request metadata a CTA needs (tile starts, req_to_token row,
+// seq_len) is copied to shared memory once at kernel start, so the walkers never wait on global
+// memory; only requests beyond kMaxCachedReqs (a CTA spanning that many requests) are read from
+// global memory.
 // ---------------------------------------------------------------------------------------------
+struct Meta {
+  const ReqCache* c;
+  const int32_t* g_ts;
+  const tf_paged_attn_args* a;
+  int32_t* err;
+  __device__ __forceinline__ int32_t ts(int b) const {
+    const int i = b - c->bf;
+    return (i >= 0 && i <= c->n) ? c->ts[i] : g_ts[b];
+  }
+  __device__ __forceinline__ int64_t row_off(int b) const {
+    const int i = b - c->bf;
+    if (i >= 0 && i < c->n) return c->row_off[i];
+    int64_t r = a->req_pool_indices[b];
+    if (r < 0 || r >= a->r2t_rows) { record_err(err, TF_KERR_REQ_RANGE); r = 0; }
+    return r * a->r2t_stride;
+  }
+  __device__ __forceinline__ int64_t len(int b) const {
+    const int i = b - c->bf;
+    return (i >= 0 && i < c->n) ? c->len[i] : a->seq_lens[b];
+  }
+};
+
+// first b with ts[b+1] * Hkv > g (b in [0, B-1])
+__device__ int first_req_after(const int32_t* ts, int B, int Hkv, int64_t g) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((int64_t)ts[mid + 1] * Hkv > g) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
 struct Piece {
   int b, h, t0, n;  // tiles [t0, t0+n) of unit (b, h)
   int nt;           // tiles of the whole unit
@@ -124,25 +173,18 @@ struct Piece {
 };
 
 struct Walker {
-  const int32_t* ts;
-  int B, Hkv;
+  int Hkv;
   int64_t g, g1;
   int b;
-  __device__ void init(const int32_t* ts_, int B_, int Hkv_, int64_t g0, int64_t g1_) {
-    ts = ts_; B = B_; Hkv = Hkv_; g = g0; g1 = g1_;
-    // first b with ts[b+1]*Hkv > g0
-    int lo = 0, hi = B - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if ((int64_t)ts[mid + 1] * Hkv > g0) hi = mid; else lo = mid + 1;
-    }
-    b = lo;
+  __device__ void init(int b0, int Hkv_, int64_t g0, int64_t g1_) {
+    Hkv = Hkv_; g = g0; g1 = g1_; b = b0;
   }
-  __device__ bool next(Piece& p) {
+  __device__ bool next(const Meta& m, Piece& p) {
     if (g >= g1) return false;
-    while ((int64_t)ts[b + 1] * Hkv <= g) ++b;
-    const int nt = ts[b + 1] - ts[b];
-    const int64_t within = g - (int64_t)ts[b] * Hkv;
+    while ((int64_t)m.ts(b + 1) * Hkv <= g) ++b;
+    const int tsb = m.ts(b);
+    const int nt = m.ts(b + 1) - tsb;
+    const int64_t within = g - (int64_t)tsb * Hkv;
     p.b = b;
     p.h = (int)(within / nt);
     p.t0 = (int)(within - (int64_t)p.h * nt);
@@ -162,18 +204,6 @@ __device__ __forceinline__ int64_t cta_range(int c, int64_t total, int nctas) {
 // ---------------------------------------------------------------------------------------------
 // tensor-core helpers (legacy warp-level mma; operands staged by cp.async + ldmatrix)
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
 __device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -195,20 +225,32 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // ---------------------------------------------------------------------------------------------
 // main kernel
 // ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int c) {
+  return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(tf_paged_attn_args a, Ws ws, int nctas_launched) {
   using C = Cfg<D>;
-  extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* stages = smem;
-  float* o_s = reinterpret_cast<float*>(smem + C::kStagesBytes);       // [4][8][kOStride]
-  float* m_s = o_s + kConsumers * kHeads * C::kOStride;                // [4][8]
-  float* l_s = m_s + kConsumers * kHeads;                              // [4][8]
-  uint64_t* full = reinterpret_cast<uint64_t*>(l_s + kConsumers * kHeads);
-  uint64_t* empty = full + C::kStages;
-  volatile int* aborted = reinterpret_cast<volatile int*>(empty + C::kStages);
+  constexpr int NB = C::kBlocks;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem);             // [8][kQStride]
+  float* o_s = reinterpret_cast<float*>(smem + C::kQBytes);                  // [8 warps][8][kOStride]
+  float* m_s = o_s + kWarps * kHeads * C::kOStride;                          // [8][8]
+  float* l_s = m_s + kWarps * kHeads;                                        // [8][8]
+  ReqCache* rc = reinterpret_cast<ReqCache*>(smem + C::kCacheOff);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;  // mma groupID / thread-in-group
   const int B = a.batch_size, Hkv = a.num_kv_heads;
   const int G = a.num_q_heads / Hkv;
   int32_t* err = a.err ? a.err : ws.status;
@@ -220,178 +262,144 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t g0 = cta_range(c, total, nctas), g1 = cta_range(c + 1, total, nctas);
 
   if (tid == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 32);  // one cp.async arrival per producer lane
-      mbar_init(&empty[s], 1);  // the consumer warp that read the stage
-    }
-    *aborted = 0;
-    fence_mbar_init();
+    const int bf = first_req_after(ws.tile_start, B, Hkv, g0);
+    const int bl = first_req_after(ws.tile_start, B, Hkv, g1 - 1);
+    rc->bf = bf;
+    rc->n = min(bl - bf + 1, kMaxCachedReqs);
   }
   __syncthreads();
+  for (int i = tid; i <= rc->n; i += kThreads) {  // metadata of the requests this CTA spans
+    const int b = rc->bf + i;
+    rc->ts[i] = ws.tile_start[b];
+    if (i < rc->n) {
+      int64_t r = a.req_pool_indices[b];
+      if (r < 0 || r >= a.r2t_rows) { record_err(err, TF_KERR_REQ_RANGE); r = 0; }
+      rc->row_off[i] = r * a.r2t_stride;
+      rc->len[i] = a.seq_lens[b];
+    }
+  }
+  __syncthreads();
+  const Meta meta{rc, ws.tile_start, &a, err};
 
-  const uint32_t stage0 = smem_u32(stages);
+  const float scale_log2 = a.scale * kLog2e;
+  const __nv_bfloat16* qg = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  const int64_t* r2t = a.req_to_token;
+  Walker wk;
+  wk.init(rc->bf, Hkv, g0, g1);
+  Piece p;
+  while (wk.next(meta, p)) {
+    // Q of the query heads of kv head p.h (token index == request index in decode); padded heads 0
+    for (int e = tid; e < kHeads * D; e += kThreads) {
+      const int hd = e / D, d = e - hd * D;
+      q_s[hd * C::kQStride + d] =
+          hd < G ? qg[(int64_t)p.b * a.q_stride_tok + (int64_t)(p.h * G + hd) * a.q_stride_head + d]
+                 : __float2bfloat16_rn(0.f);
+    }
+    __syncthreads();
+    const int64_t L = meta.len(p.b);
+    const int64_t roff = meta.row_off(p.b);
+    const char* kbase = (const char*)a.k_buffer + (int64_t)p.h * a.kv_stride_head * 2;
+    const char* vbase = (const char*)a.v_buffer + (int64_t)p.h * a.kv_stride_head * 2;
+    const int64_t sstride = a.kv_stride_slot * 2;
 
-  if (warp == kConsumers) {
-    // ===================================== producer =====================================
-    Walker wk;
-    wk.init(ws.tile_start, B, Hkv, g0, g1);
-    Piece p;
-    int i = 0;
-    const char* kb = (const char*)a.k_buffer;
-    const char* vb = (const char*)a.v_buffer;
-    const int row_in = lane / C::kChunks, chunk = lane % C::kChunks;
-    bool ok = true;
-    while (ok && wk.next(p)) {
-      int64_t row = a.req_pool_indices[p.b];
-      if (row < 0 || row >= a.r2t_rows) { record_err(err, TF_KERR_REQ_RANGE); row = 0; }
-      const int64_t* r2t = a.req_to_token + row * a.r2t_stride;
-      const int64_t L = a.seq_lens[p.b];
-      const int64_t head_off = (int64_t)p.h * a.kv_stride_head * 2 + chunk * 16;
-      // slot ids of the first tile, then one tile of look-ahead
-      int64_t pos = (int64_t)p.t0 * kTileTok + lane;
-      int64_t raw_next = r2t[pos < L ? pos : (int64_t)p.t0 * kTileTok];
-      for (int tt = 0; tt < p.n; ++tt, ++i) {
-        const int64_t raw = raw_next;
-        if (tt + 1 < p.n) {
-          const int64_t base = (int64_t)(p.t0 + tt + 1) * kTileTok;
-          raw_next = r2t[base + lane < L ? base + lane : base];
+    float acc[NB][2][4];
+#pragma unroll
+    for (int j = 0; j < NB; ++j)
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) acc[j][q2][0] = acc[j][q2][1] = acc[j][q2][2] = acc[j][q2][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    // raw req_to_token entries of tokens g and g+8 of a tile (positions clamped into the request)
+    auto raw_slots = [&](int tile, int64_t& s0, int64_t& s1) {
+      const int64_t base = (int64_t)tile * kTileTok + gq;
+      s0 = r2t[roff + (base < L ? base : L - 1)];
+      s1 = r2t[roff + (base + 8 < L ? base + 8 : L - 1)];
+    };
+    uint4 kr[2][NB], vr[2][NB];
+    auto load_rows = [&](const char* basep, int64_t s0, int64_t s1, uint4 (&dst)[2][NB]) {
+      const char* p0 = basep + s0 * sstride;
+      const char* p1 = basep + s1 * sstride;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        dst[0][j] = ld_stream(p0 + (4 * j + tq) * 16);
+        dst[1][j] = ld_stream(p1 + (4 * j + tq) * 16);
+      }
+    };
+
+    int kt = warp;  // this warp's tiles: local indices warp, warp+8, ... of the piece
+    if (kt < p.n) {
+      int64_t r0, r1, n0 = 0, n1 = 0;
+      raw_slots(p.t0 + kt, r0, r1);
+      if (kt + kWarps < p.n) raw_slots(p.t0 + kt + kWarps, n0, n1);
+      int64_t s0 = resolve_slot(r0, a.num_slots, a.slot_mode, err);
+      int64_t s1 = resolve_slot(r1, a.num_slots, a.slot_mode, err);
+      load_rows(kbase, s0, s1, kr);
+      load_rows(vbase, s0, s1, vr);
+      for (; kt < p.n; kt += kWarps) {
+        const bool has_next = kt + kWarps < p.n;
+        int64_t nn0 = 0, nn1 = 0;  // slots two tiles ahead
+        if (kt + 2 * kWarps < p.n) raw_slots(p.t0 + kt + 2 * kWarps, nn0, nn1);
+        // ---- S^T = K.Q^T (two accumulators halve the dependent mma chain)
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(q_s + gq * C::kQStride + 32 * j + 8 * tq);
+          mma_bf16(sa, kr[0][j].x, kr[1][j].x, kr[0][j].y, kr[1][j].y, qv.x, qv.y);
+          mma_bf16(sb, kr[0][j].z, kr[1][j].z, kr[0][j].w, kr[1][j].w, qv.z, qv.w);
         }
-        const int64_t slot = resolve_slot(raw, a.num_slots, a.slot_mode, err);
-        const int s = i % C::kStages;
-        if (i >= C::kStages) {
-          if (!mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1)) {
-            record_err(err, TF_KERR_TIMEOUT);
-            ok = false;
-            break;
+        int64_t ns0 = 0, ns1 = 0;
+        if (has_next) {
+          ns0 = resolve_slot(n0, a.num_slots, a.slot_mode, err);
+          ns1 = resolve_slot(n1, a.num_slots, a.slot_mode, err);
+          load_rows(kbase, ns0, ns1, kr);
+        }
+        // ---- online softmax (rows = tokens g, g+8; columns = query heads 2tq, 2tq+1)
+        const int64_t tok = (int64_t)(p.t0 + kt) * kTileTok + gq;
+        const bool v_lo = tok < L, v_hi = tok + 8 < L;
+        float sc0 = v_lo ? (sa[0] + sb[0]) * scale_log2 : -INFINITY;
+        float sc1 = v_lo ? (sa[1] + sb[1]) * scale_log2 : -INFINITY;
+        float sc2 = v_hi ? (sa[2] + sb[2]) * scale_log2 : -INFINITY;
+        float sc3 = v_hi ? (sa[3] + sb[3]) * scale_log2 : -INFINITY;
+        float mx0 = fmaxf(sc0, sc2), mx1 = fmaxf(sc1, sc3);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        const float p0 = exp2f(sc0 - mn0), p1 = exp2f(sc1 - mn1);
+        const float p2 = exp2f(sc2 - mn0), p3 = exp2f(sc3 - mn1);
+        l0 = l0 * al0 + p0 + p2;
+        l1 = l1 * al1 + p1 + p3;
+        const uint32_t pb0 = movmatrix_t(pack_bf16(p0, p1));
+        const uint32_t pb1 = movmatrix_t(pack_bf16(p2, p3));
+        // ---- O^T += V^T.P^T
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+#pragma unroll
+          for (int q2 = 0; q2 < 2; ++q2) {
+            float* ac = acc[j][q2];
+            ac[0] *= al0;
+            ac[1] *= al1;
+            ac[2] *= al0;
+            ac[3] *= al1;
+            const uint32_t a0 = movmatrix_t(word(vr[0][j], 2 * q2));
+            const uint32_t a1 = movmatrix_t(word(vr[0][j], 2 * q2 + 1));
+            const uint32_t a2 = movmatrix_t(word(vr[1][j], 2 * q2));
+            const uint32_t a3 = movmatrix_t(word(vr[1][j], 2 * q2 + 1));
+            mma_bf16(ac, a0, a1, a2, a3, pb0, pb1);
           }
         }
-        const uint32_t kdst = stage0 + s * C::kStageBytes;
-#pragma unroll 4
-        for (int r = 0; r < kTileTok; r += C::kRowsPerIssue) {
-          const int rr = r + row_in;
-          const int64_t sl = __shfl_sync(0xffffffffu, slot, rr);
-          const int64_t off = sl * a.kv_stride_slot * 2 + head_off;
-          const uint32_t dst = kdst + rr * C::kRowBytes + ((chunk ^ (rr & 7)) << 4);
-          cp_async16(dst, kb + off);
-          cp_async16(dst + C::kTileBytes, vb + off);
-        }
-        cp_async_arrive_noinc(&full[s]);
+        if (has_next) load_rows(vbase, ns0, ns1, vr);
+        n0 = nn0;
+        n1 = nn1;
       }
     }
-    cp_async_wait_all();
-    return;
-  }
 
-  // ====================================== consumers ======================================
-  const int gq = lane >> 2, tq = lane & 3;  // mma groupID / thread-in-group
-  const float scale_log2 = a.scale * kLog2e;
-  Walker wk;
-  wk.init(ws.tile_start, B, Hkv, g0, g1);
-  Piece p;
-  int i_base = 0;
-  const __nv_bfloat16* qg = reinterpret_cast<const __nv_bfloat16*>(a.q);
-  while (wk.next(p)) {
-    // Q^T fragments of the query heads of kv head p.h (token index == request index in decode)
-    uint32_t qf[D / 16][2];
-    {
-      const bool live = gq < G;
-      const __nv_bfloat16* qrow =
-          qg + (int64_t)p.b * a.q_stride_tok + (int64_t)(p.h * G + (live ? gq : 0)) * a.q_stride_head;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        qf[kk][0] = live ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * tq) : 0u;
-        qf[kk][1] = live ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * tq + 8) : 0u;
-      }
-    }
-    float acc[D / 16][4];
-#pragma unroll
-    for (int md = 0; md < D / 16; ++md) acc[md][0] = acc[md][1] = acc[md][2] = acc[md][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    const int64_t L = a.seq_lens[p.b];
-
-    const int first = i_base + (((warp - i_base) % kConsumers) + kConsumers) % kConsumers;
-    for (int i = first; i < i_base + p.n; i += kConsumers) {
-      const int s = i % C::kStages;
-      if (*aborted) continue;
-      if (!mbar_wait(&full[s], (i / C::kStages) & 1)) {
-        if (lane == 0) { record_err(err, TF_KERR_TIMEOUT); *aborted = 1; }
-        continue;
-      }
-      const uint32_t kbase = stage0 + s * C::kStageBytes;
-      const uint32_t vbase = kbase + C::kTileBytes;
-      const int64_t tok0 = (int64_t)(p.t0 + (i - i_base)) * kTileTok;
-
-      float sc[2][4];
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
-        const int row = mt * 16 + (lane & 15);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int ch = kk * 2 + (lane >> 4);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(kbase + row * C::kRowBytes + ((ch ^ (row & 7)) << 4), a0, a1, a2, a3);
-          mma_bf16(sc[mt], a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
-        }
-      }
-      // scale, mask, online softmax (columns 2tq, 2tq+1 are query heads; rows are tokens)
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const bool v_lo = tok0 + mt * 16 + gq < L;
-        const bool v_hi = tok0 + mt * 16 + gq + 8 < L;
-        sc[mt][0] = v_lo ? sc[mt][0] * scale_log2 : -INFINITY;
-        sc[mt][1] = v_lo ? sc[mt][1] * scale_log2 : -INFINITY;
-        sc[mt][2] = v_hi ? sc[mt][2] * scale_log2 : -INFINITY;
-        sc[mt][3] = v_hi ? sc[mt][3] * scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, fmaxf(sc[mt][0], sc[mt][2]));
-        mx1 = fmaxf(mx1, fmaxf(sc[mt][1], sc[mt][3]));
-      }
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-      }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-      m0 = mn0;
-      m1 = mn1;
-      l0 *= al0;
-      l1 *= al1;
-      uint32_t pb[2][2];
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const float p0 = exp2f(sc[mt][0] - mn0), p1 = exp2f(sc[mt][1] - mn1);
-        const float p2 = exp2f(sc[mt][2] - mn0), p3 = exp2f(sc[mt][3] - mn1);
-        l0 += p0 + p2;
-        l1 += p1 + p3;
-        pb[mt][0] = movmatrix_t(pack_bf16(p0, p1));
-        pb[mt][1] = movmatrix_t(pack_bf16(p2, p3));
-      }
-#pragma unroll
-      for (int md = 0; md < D / 16; ++md) {
-        acc[md][0] *= al0;
-        acc[md][1] *= al1;
-        acc[md][2] *= al0;
-        acc[md][3] *= al1;
-      }
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const int row = mt * 16 + (lane & 7) + ((lane >> 4) << 3);
-#pragma unroll
-        for (int md = 0; md < D / 16; ++md) {
-          const int ch = md * 2 + ((lane >> 3) & 1);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(vbase + row * C::kRowBytes + ((ch ^ (row & 7)) << 4), a0, a1, a2, a3);
-          mma_bf16(acc[md], a0, a1, a2, a3, pb[mt][0], pb[mt][1]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    i_base += p.n;
-
-    // ---------------- merge the four consumer warps of this piece ----------------
+    // ---------------- merge the eight warps of this piece ----------------
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       l0 += __shfl_xor_sync(0xffffffffu, l0, o);
@@ -403,10 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_s[warp * kHeads + 2 * tq] = l0;
       l_s[warp * kHeads + 2 * tq + 1] = l1;
     }
-    named_barrier(1, 32 * kConsumers);
+    __syncthreads();
     float M0 = -INFINITY, M1 = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumers; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       M0 = fmaxf(M0, m_s[w * kHeads + 2 * tq]);
       M1 = fmaxf(M1, m_s[w * kHeads + 2 * tq + 1]);
     }
@@ -414,25 +422,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float f1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
     float* ow = o_s + warp * kHeads * C::kOStride;
 #pragma unroll
-    for (int md = 0; md < D / 16; ++md) {
-      ow[(2 * tq) * C::kOStride + md * 16 + gq] = acc[md][0] * f0;
-      ow[(2 * tq + 1) * C::kOStride + md * 16 + gq] = acc[md][1] * f1;
-      ow[(2 * tq) * C::kOStride + md * 16 + gq + 8] = acc[md][2] * f0;
-      ow[(2 * tq + 1) * C::kOStride + md * 16 + gq + 8] = acc[md][3] * f1;
+    for (int j = 0; j < NB; ++j) {
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        // rows g / g+8 of A tile (j, q2) are dims phi_{2q2}(g) / phi_{2q2+1}(g)
+        const int d_lo = 32 * j + 8 * (gq >> 1) + 4 * q2 + (gq & 1);
+        const int d_hi = d_lo + 2;
+        ow[(2 * tq) * C::kOStride + d_lo] = acc[j][q2][0] * f0;
+        ow[(2 * tq + 1) * C::kOStride + d_lo] = acc[j][q2][1] * f1;
+        ow[(2 * tq) * C::kOStride + d_hi] = acc[j][q2][2] * f0;
+        ow[(2 * tq + 1) * C::kOStride + d_hi] = acc[j][q2][3] * f1;
+      }
     }
-    named_barrier(1, 32 * kConsumers);
+    __syncthreads();
     const bool complete = (p.t0 == 0 && p.n == p.nt);
     const int pslot = 2 * c + (p.g_start == g0 ? 0 : 1);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
     const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
-    for (int e = tid; e < G * D; e += 32 * kConsumers) {
+    for (int e = tid; e < G * D; e += kThreads) {
       const int hd = e / D, d = e - hd * D;
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, m_s[w * kHeads + hd]);
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w * kHeads + hd]);
       float Ls = 0.f, o = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumers; ++w) {
+      for (int w = 0; w < kWarps; ++w) {
         const float mw = m_s[w * kHeads + hd];
         Ls += mw == -INFINITY ? 0.f : l_s[w * kHeads + hd] * exp2f(mw - M);
         o += o_s[(w * kHeads + hd) * C::kOStride + d];
@@ -454,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    named_barrier(1, 32 * kConsumers);
+    __syncthreads();
   }
 }
 
@@ -464,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws ws,
                                                       int nctas_launched) {
+  extern __shared__ float csm[];  // w[np][kHeads] then int sl[np]
   const int B = a.batch_size, Hkv = a.num_kv_heads;
   const int G = a.num_q_heads / Hkv;
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
@@ -484,25 +499,37 @@ __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws w
   const int c0 = (int)(((su + 1) * nctas - 1) / total);
   const int c1 = (int)((eu * nctas - 1) / total);
   if (c0 == c1) return;  // finished inside one CTA
+  const int np = c1 - c0 + 1;
+  float* w = csm;
+  int* sl = reinterpret_cast<int*>(csm + np * kHeads);
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int cc = c0 + i;
+    const int64_t rc = cta_range(cc, total, nctas);
+    sl[i] = 2 * cc + ((su > rc ? su : rc) == rc ? 0 : 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int hd = threadIdx.x;
+    float M = -INFINITY;
+    for (int i = 0; i < np; ++i) M = fmaxf(M, ws.part_ml[(sl[i] * kHeads + hd) * 2]);
+    float L = 0.f;
+    for (int i = 0; i < np; ++i) {
+      const float m = ws.part_ml[(sl[i] * kHeads + hd) * 2];
+      const float f = m == -INFINITY ? 0.f : exp2f(m - M);
+      w[i * kHeads + hd] = f;
+      L += ws.part_ml[(sl[i] * kHeads + hd) * 2 + 1] * f;
+    }
+    const float inv = 1.0f / L;
+    for (int i = 0; i < np; ++i) w[i * kHeads + hd] *= inv;
+  }
+  __syncthreads();
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     const int hd = e / D, d = e - hd * D;
-    float M = -INFINITY;
-    for (int cc = c0; cc <= c1; ++cc) {
-      const int64_t rc = cta_range(cc, total, nctas);
-      const int sl = 2 * cc + ((su > rc ? su : rc) == rc ? 0 : 1);
-      M = fmaxf(M, ws.part_ml[(sl * kHeads + hd) * 2]);
-    }
-    float Ls = 0.f, o = 0.f;
-    for (int cc = c0; cc <= c1; ++cc) {
-      const int64_t rc = cta_range(cc, total, nctas);
-      const int sl = 2 * cc + ((su > rc ? su : rc) == rc ? 0 : 1);
-      const float mw = ws.part_ml[(sl * kHeads + hd) * 2];
-      const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
-      Ls += ws.part_ml[(sl * kHeads + hd) * 2 + 1] * f;
-      o += ws.part_o[((int64_t)sl * kHeads + hd) * D + d] * f;
-    }
+    float o = 0.f;
+    for (int i = 0; i < np; ++i)
+      o = fmaf(w[i * kHeads + hd], ws.part_o[((int64_t)sl[i] * kHeads + hd) * D + d], o);
     const int hq = h * G + hd;
-    float r = round_to<__nv_bfloat16>(o / Ls);
+    float r = round_to<__nv_bfloat16>(o);
     if (a.gate_mode != TF_GATE_NONE && gate != nullptr)
       r = apply_gate<__nv_bfloat16>(
           r, to_f(gate[(int64_t)b * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + d]),
@@ -519,7 +546,11 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, c
   if (e != cudaSuccess) return e;
   plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, ws.tile_start);
   decode_kernel<D><<<nctas, kThreads, Cfg<D>::kSmem, s>>>(a, ws, nctas);
-  combine_kernel<D><<<a.batch_size * a.num_kv_heads, 256, 0, s>>>(a, ws, nctas);
+  // a unit spans at most every CTA: weights [nctas][kHeads] + slot ids [nctas]
+  const size_t csmem = (size_t)nctas * (kHeads * 4 + 4);
+  e = cudaFuncSetAttribute(combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
+  if (e != cudaSuccess) return e;
+  combine_kernel<D><<<a.batch_size * a.num_kv_heads, 256, csmem, s>>>(a, ws, nctas);
   return cudaGetLastError();
 }
 
@@ -533,7 +564,6 @@ bool paged_decode_mma_supported(const tf_paged_attn_args& a) {
   auto al = [](const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
   if (!al(a.k_buffer, 16) || !al(a.v_buffer, 16)) return false;
   if ((a.kv_stride_slot * 2) % 16 != 0 || (a.kv_stride_head * 2) % 16 != 0) return false;
-  if (!al(a.q, 4) || (a.q_stride_tok % 2) != 0 || (a.q_stride_head % 2) != 0) return false;
   return true;
 }
 
