@@ -134,6 +134,18 @@ TF_API size_t tf_paged_decode_workspace_size(const tf_paged_attn_args* args);
 TF_API tf_status tf_paged_decode_attn(const tf_paged_attn_args* args, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* a2 without a caller workspace.  No counterpart in the reference: an addition for callers that
+ * cannot allocate device memory (a host runtime binding this ABI through a plain FFI with no CUDA
+ * allocator, or a process whose device memory is all reserved by its own pool).  Same kernels and
+ * results as tf_paged_decode_attn; the scratch is a fixed 4 MiB device array inside the library
+ * that every GPU loading the library holds until exit.  Batches whose scratch would exceed it are
+ * rejected with TF_ERR_WORKSPACE (for head_dim 256 on 148 SMs, 2.4 MiB of partials plus
+ * 4 bytes per request: about 400K requests).  The first call on a device resolves the array's
+ * device address (make it before any stream capture).  Calls share the array and it keeps the
+ * last call's contents, so calls whose kernels overlap on one GPU race and must be serialised.
+ * Allocates nothing (no cudaMalloc, cudaFree or allocating library call). */
+TF_API tf_status tf_paged_decode_attn_noalloc(const tf_paged_attn_args* args, void* stream);
+
 /* a3: extend / mixed batch over a radix-cached prefix (qwen3_8/full_attention.py:179-213 for one
  * request, :244-283 for the padded batched path).  Padded query rows do not exist here: only the
  * T real rows are computed and written. */

@@ -94,6 +94,7 @@ SIGNATURES = [
     ("tf_kv_store", _i32, [ctypes.POINTER(KVStoreArgs), _vp]),
     ("tf_paged_decode_workspace_size", ctypes.c_size_t, [ctypes.POINTER(PagedAttnArgs)]),
     ("tf_paged_decode_attn", _i32, [ctypes.POINTER(PagedAttnArgs), _vp, ctypes.c_size_t, _vp]),
+    ("tf_paged_decode_attn_noalloc", _i32, [ctypes.POINTER(PagedAttnArgs), _vp]),
     ("tf_paged_extend_workspace_size", ctypes.c_size_t, [ctypes.POINTER(PagedAttnArgs)]),
     ("tf_paged_extend_attn", _i32, [ctypes.POINTER(PagedAttnArgs), _vp, ctypes.c_size_t, _vp]),
     ("tf_gdn_decode", _i32, [ctypes.POINTER(GdnArgs), _vp]),

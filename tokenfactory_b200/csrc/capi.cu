@@ -209,6 +209,28 @@ tf_status tf_paged_decode_attn(const tf_paged_attn_args* a, void* ws, size_t ws_
   return cuda_status(launch_paged_attn_simt(d, s), "tf_paged_decode_attn");
 }
 
+tf_status tf_paged_decode_attn_noalloc(const tf_paged_attn_args* a, void* stream) {
+  tf_status st = check_paged(a, true);
+  if (st != TF_OK || a->batch_size == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  if (!paged_decode_mma_supported(*a)) {  // the CUDA-core path needs no scratch at all
+    tf_paged_attn_args d = *a;
+    d.extend_lens = nullptr;
+    return cuda_status(launch_paged_attn_simt(d, s), "tf_paged_decode_attn_noalloc");
+  }
+  const int nsm = device_sm_count();
+  const size_t need = paged_decode_mma_workspace(*a, nsm);
+  if (need > kNoAllocScratchBytes)
+    return fail(TF_ERR_WORKSPACE,
+                "tf_paged_decode_attn_noalloc: this batch needs %zu bytes of scratch but the "
+                "built-in scratch holds %zu (batch_size %d, head_dim %d, %d SMs); use "
+                "tf_paged_decode_attn with a caller workspace",
+                need, kNoAllocScratchBytes, a->batch_size, a->head_dim, nsm);
+  return cuda_status(launch_paged_decode_mma_noalloc(*a, nsm, s), "tf_paged_decode_attn_noalloc");
+}
+
 size_t tf_paged_extend_workspace_size(const tf_paged_attn_args* a) {
   (void)a;
   return 0;

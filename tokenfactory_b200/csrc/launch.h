@@ -19,6 +19,10 @@ bool paged_decode_mma_supported(const tf_paged_attn_args& a);
 size_t paged_decode_mma_workspace(const tf_paged_attn_args& a, int num_sms);
 cudaError_t launch_paged_decode_mma(const tf_paged_attn_args& a, void* ws, size_t ws_bytes,
                                     int num_sms, cudaStream_t s);
+// same kernels with the scratch in a fixed device array of kNoAllocScratchBytes (no allocation)
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+cudaError_t launch_paged_decode_mma_noalloc(const tf_paged_attn_args& a, int num_sms,
+                                            cudaStream_t s);
 
 // gdn.cu
 bool gdn_dims_supported(int dk, int dv);

@@ -25,6 +25,8 @@
 //                 warps merge.  P^T (B operand) comes from the S^T accumulator through movmatrix.
 // Online softmax per query head in registers; the eight warps merge through shared memory at the
 // end of each unit piece.
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -580,6 +582,56 @@ cudaError_t launch_paged_decode_mma(const tf_paged_attn_args& a, void* ws, size_
     case 128: return dec::launch_d<128>(a, ws, num_sms, s);
     default: return dec::launch_d<256>(a, ws, num_sms, s);
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant (tf_paged_decode_attn_noalloc).
+//
+// Some callers cannot allocate device memory themselves: a host runtime that binds this C ABI
+// through a plain FFI and has no CUDA allocator of its own, or a serving process whose device
+// memory is all handed to its own pool at start-up.  For them the decode's scratch (schedule and
+// split partials) lives in this fixed file-scope array instead of a caller workspace.  Every GPU
+// that loads the library holds these kNoAllocScratchBytes until the process exits; all calls on a
+// device share the one array and it keeps the last call's contents, so calls whose kernels overlap
+// on that GPU (other streams, other threads) race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kScratchMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kScratchMaxDevices] = {};
+}  // namespace
+
+// Device address of g_decode_scratch on the current device.  In host code the array's name is a
+// host-side stand-in, never a device address, so it is resolved once per device (with that device
+// current) by cudaGetSymbolAddress; this first call per device should come before any stream
+// capture.
+static cudaError_t decode_scratch_ptr(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kScratchMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+cudaError_t launch_paged_decode_mma_noalloc(const tf_paged_attn_args& a, int num_sms,
+                                            cudaStream_t s) {
+  void* ws = nullptr;
+  cudaError_t e = decode_scratch_ptr(&ws);
+  if (e != cudaSuccess) return e;
+  // the status word keeps the previous call's error code: start every call from zero
+  e = cudaMemsetAsync(ws, 0, 256, s);
+  if (e != cudaSuccess) return e;
+  return launch_paged_decode_mma(a, ws, kNoAllocScratchBytes, num_sms, s);
 }
 
 }  // namespace tf
