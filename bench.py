@@ -163,12 +163,10 @@ C2 = dict(B=128, Hq=32, Hkv=4, D=256, Lmin=512, Lmax=8192, slots=1_200_000)
 
 
 def _tp_heads(hq, hkv, rank, world):
-    """Local q heads and the kv heads they read under the reference's TP split
-    (qwen3_8/full_attention.py:43-52, qwen3_8/hybrid_cache_pool.py:48)."""
-    lq = hq // world
-    if hkv >= world:
-        return lq, hkv // world
-    return lq, 1
+    """Local q heads and kv heads under the reference's TP split (tokenfactory_b200.tp)."""
+    from tokenfactory_b200.tp import head_shard
+    sh = head_shard(hq, hkv, world, world, rank, world)
+    return len(sh.q_heads), len(sh.kv_heads)
 
 
 def _decode_inputs(seed: int, rank: int, world: int, dev):

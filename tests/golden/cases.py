@@ -133,3 +133,86 @@ def checksum(arrays: dict) -> str:
         h.update(str(a.shape).encode())
         h.update(a.tobytes())
     return h.hexdigest()
+
+
+# ---------------------------------------------------------------------------------------------
+# module-level cases: a whole Qwen3_8FullAttention / Qwen3_8LinearAttention forward
+# ---------------------------------------------------------------------------------------------
+MODULE_DIMS = dict(hidden=128, hq=8, hkv=2, d=64, nk=2, nv=4, dk=32, dv=32, kc=4)
+
+MODULE_CASES: Dict[str, dict] = {
+    "full_mixed_f32": dict(kind="full", dtype="f32", seq=[10, 6, 16], ext=[1, 6, 11],
+                           req=[2, 0, 1], slots=96, rows=4, cols=32, seed=61),
+    "full_decode_bf16": dict(kind="full", dtype="bf16", seq=[9, 30, 2, 17], ext=[1, 1, 1, 1],
+                             req=[3, 1, 0, 2], slots=96, rows=4, cols=32, seed=62),
+    "full_mixed_bf16": dict(kind="full", dtype="bf16", seq=[12, 7], ext=[5, 7], req=[1, 0],
+                            slots=64, rows=2, cols=16, seed=63),
+    "full_bsz1_bf16": dict(kind="full", dtype="bf16", seq=[20], ext=[20], req=[1],
+                           slots=64, rows=2, cols=32, seed=64),
+    "linear_mixed_f32": dict(kind="linear", dtype="f32", ext=[1, 9, 70], req=[2, 0, 1],
+                             slots=4, seed=65),
+    "linear_decode_bf16": dict(kind="linear", dtype="bf16", ext=[1, 1, 1], req=[1, 3, 0],
+                               slots=4, seed=66),
+    "linear_mixed_bf16": dict(kind="linear", dtype="bf16", ext=[3, 1, 40], req=[0, 2, 1],
+                              slots=3, seed=67),
+}
+
+
+def module_weights(spec: dict) -> dict:
+    """float32 weights of the case's module, with the reference's parameter names."""
+    rng = np.random.default_rng(1000 + spec["seed"])
+    m = MODULE_DIMS
+    h = m["hidden"]
+    if spec["kind"] == "full":
+        return {
+            "q_proj.weight": _normal(rng, (m["hq"] * m["d"] * 2, h), 0.08),
+            "k_proj.weight": _normal(rng, (m["hkv"] * m["d"], h), 0.08),
+            "v_proj.weight": _normal(rng, (m["hkv"] * m["d"], h), 0.08),
+            "o_proj.weight": _normal(rng, (h, m["hq"] * m["d"]), 0.08),
+            "q_norm.weight": (1.0 + _normal(rng, (m["d"],), 0.1)).astype(np.float32),
+            "k_norm.weight": (1.0 + _normal(rng, (m["d"],), 0.1)).astype(np.float32),
+        }
+    conv_dim = 2 * m["nk"] * m["dk"] + m["nv"] * m["dv"]
+    return {
+        "in_proj_qkv.weight": _normal(rng, (conv_dim, h), 0.08),
+        "in_proj_z.weight": _normal(rng, (m["nv"] * m["dv"], h), 0.08),
+        "in_proj_b.weight": _normal(rng, (m["nv"], h), 0.08),
+        "in_proj_a.weight": _normal(rng, (m["nv"], h), 0.08),
+        "conv1d.weight": _normal(rng, (conv_dim, 1, m["kc"]), 0.5),
+        "A_log": rng.uniform(0.0, 1.5, m["nv"]).astype(np.float32),
+        "dt_bias": _normal(rng, (m["nv"],), 0.5),
+        "norm.weight": (1.0 + _normal(rng, (m["nv"] * m["dv"],), 0.1)).astype(np.float32),
+        "out_proj.weight": _normal(rng, (h, m["nv"] * m["dv"]), 0.08),
+    }
+
+
+def module_inputs(spec: dict) -> dict:
+    """hidden states, positions, batch metadata and the pools (float32 values)."""
+    rng = np.random.default_rng(2000 + spec["seed"])
+    m = MODULE_DIMS
+    t = int(sum(spec["ext"]))
+    out = dict(hidden=_normal(rng, (t, m["hidden"])),
+               req_pool_indices=np.asarray(spec["req"], np.int64),
+               extend_lens=np.asarray(spec["ext"], np.int64))
+    if spec["kind"] == "full":
+        seq, ext, req = spec["seq"], spec["ext"], spec["req"]
+        s = spec["slots"]
+        out["k_buf"] = _normal(rng, (s, m["hkv"], m["d"]))
+        out["v_buf"] = _normal(rng, (s, m["hkv"], m["d"]))
+        r2t = np.full((spec["rows"], spec["cols"]), -1, dtype=np.int64)
+        perm = rng.permutation(np.arange(1, s, dtype=np.int64))
+        off = 0
+        for b, L in enumerate(seq):
+            r2t[req[b], :L] = perm[off:off + L]
+            off += L
+        out["req_to_token"] = r2t
+        out["seq_lens"] = np.asarray(seq, np.int64)
+        out["out_cache_loc"] = np.concatenate(
+            [r2t[req[b], seq[b] - ext[b]:seq[b]] for b in range(len(seq))]).astype(np.int64)
+        out["positions"] = np.concatenate(
+            [np.arange(seq[b] - ext[b], seq[b]) for b in range(len(seq))]).astype(np.int64)
+    else:
+        conv_dim = 2 * m["nk"] * m["dk"] + m["nv"] * m["dv"]
+        out["conv_state"] = _normal(rng, (spec["slots"], conv_dim, m["kc"] - 1))
+        out["ssm_state"] = _normal(rng, (spec["slots"], m["nv"], m["dk"], m["dv"]), 0.05)
+    return out

@@ -34,3 +34,13 @@ def gdn_case(name: str):
     assert bytes(z[f"{name}/checksum"]).decode() == C.checksum(inp), f"input drift in {name}"
     gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
     return spec, inp, gold
+
+
+def module_case(name: str):
+    spec = C.MODULE_CASES[name]
+    w = C.module_weights(spec)
+    inp = C.module_inputs(spec)
+    z = _npz("module_golden.npz")
+    assert bytes(z[f"{name}/checksum"]).decode() == C.checksum({**w, **inp}), f"input drift in {name}"
+    gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
+    return spec, w, inp, gold

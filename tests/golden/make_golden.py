@@ -14,6 +14,8 @@ Reference functions exercised (paths inside the reference project):
   Qwen3_8LinearAttention._gated_delta_rule_step qwen3_8/linear_attention.py:154-242
   the extend loop of forward()                 qwen3_8/linear_attention.py:329-358
   Qwen3_8RMSNormGated.forward                  qwen3_8/rms_norm_gated.py:26-40
+  Qwen3_8FullAttention.forward                 qwen3_8/full_attention.py:112-161
+  Qwen3_8LinearAttention.forward               qwen3_8/linear_attention.py:300-364
 """
 
 import argparse
@@ -145,6 +147,82 @@ def gdn_golden(ref) -> dict:
     return out
 
 
+class _Pool:
+    """The two cache-pool views the attention forwards read (qwen3_8/hybrid_cache_pool.py:151-158)."""
+
+    def __init__(self, k_buf=None, v_buf=None, conv_state=None, ssm_state=None):
+        self.k, self.v, self.c, self.s = k_buf, v_buf, conv_state, ssm_state
+
+    def get_full_kv_buffers(self, layer_idx):
+        return self.k, self.v
+
+    def get_linear_states(self, layer_idx):
+        return self.c, self.s
+
+
+def module_golden(ref) -> dict:
+    from qwen3_8 import ForwardBatch, Qwen3_8Config
+    from qwen3_8.full_attention import Qwen3_8FullAttention
+    from qwen3_8.linear_attention import Qwen3_8LinearAttention
+
+    m = C.MODULE_DIMS
+    cfg = Qwen3_8Config(hidden_size=m["hidden"], intermediate_size=64, num_hidden_layers=4,
+                        layer_types=["linear_attention"] * 3 + ["full_attention"],
+                        num_attention_heads=m["hq"], num_key_value_heads=m["hkv"],
+                        head_dim=m["d"], linear_num_key_heads=m["nk"],
+                        linear_num_value_heads=m["nv"], linear_key_head_dim=m["dk"],
+                        linear_value_head_dim=m["dv"], linear_conv_kernel_dim=m["kc"])
+    out = {}
+    for name, spec in C.MODULE_CASES.items():
+        dt = _tdt(spec["dtype"])
+        w = C.module_weights(spec)
+        inp = C.module_inputs(spec)
+        out[f"{name}/checksum"] = np.frombuffer(
+            C.checksum({**w, **inp}).encode(), dtype=np.uint8)
+        inp = {k: v.copy() for k, v in inp.items()}  # the forward writes the pools in place
+        mod = (Qwen3_8FullAttention(cfg, 3) if spec["kind"] == "full"
+               else Qwen3_8LinearAttention(cfg, 0))
+        mod.load_state_dict({k: torch.from_numpy(v) for k, v in w.items()}, strict=False)
+        mod = mod.eval().to(dt)
+        hidden = torch.from_numpy(inp["hidden"]).to(dt)
+        ext = spec["ext"]
+        T = int(sum(ext))
+        with torch.inference_mode():
+            if spec["kind"] == "full":
+                kb = torch.from_numpy(inp["k_buf"]).to(dt)
+                vb = torch.from_numpy(inp["v_buf"]).to(dt)
+                pool = _Pool(kb, vb)
+                fb = ForwardBatch(batch_size=len(ext),
+                                  req_pool_indices=torch.from_numpy(inp["req_pool_indices"]),
+                                  seq_lens=torch.from_numpy(inp["seq_lens"]),
+                                  prefix_lens=torch.from_numpy(inp["seq_lens"] - inp["extend_lens"]),
+                                  extend_lens=list(ext),
+                                  out_cache_loc=torch.from_numpy(inp["out_cache_loc"]),
+                                  req_to_token=torch.from_numpy(inp["req_to_token"]),
+                                  is_prefill=max(ext) > 1)
+                y = mod(hidden, torch.from_numpy(inp["positions"]), pool, fb)
+                loc = torch.from_numpy(inp["out_cache_loc"])
+                out[f"{name}/k_rows"] = _np(kb[loc])
+                out[f"{name}/v_rows"] = _np(vb[loc])
+            else:
+                cs = torch.from_numpy(inp["conv_state"]).to(dt)
+                ss = torch.from_numpy(inp["ssm_state"].copy())
+                pool = _Pool(conv_state=cs, ssm_state=ss)
+                fb = ForwardBatch(batch_size=len(ext),
+                                  req_pool_indices=torch.from_numpy(inp["req_pool_indices"]),
+                                  seq_lens=torch.from_numpy(inp["extend_lens"] + 5),
+                                  prefix_lens=torch.full((len(ext),), 5, dtype=torch.long),
+                                  extend_lens=list(ext),
+                                  out_cache_loc=torch.zeros(T, dtype=torch.long),
+                                  req_to_token=torch.zeros((1, 1), dtype=torch.long),
+                                  is_prefill=max(ext) > 1)
+                y = mod(hidden, pool, fb)
+                out[f"{name}/conv_state"] = _np(cs)
+                out[f"{name}/ssm_state"] = _np(ss)
+        out[f"{name}/out"] = _np(y)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True,
@@ -154,7 +232,8 @@ def main() -> None:
     torch.manual_seed(0)
     np.savez_compressed(os.path.join(HERE, "attention_golden.npz"), **attention_golden(args))
     np.savez_compressed(os.path.join(HERE, "gdn_golden.npz"), **gdn_golden(args))
-    for f in ("attention_golden.npz", "gdn_golden.npz"):
+    np.savez_compressed(os.path.join(HERE, "module_golden.npz"), **module_golden(args))
+    for f in ("attention_golden.npz", "gdn_golden.npz", "module_golden.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

@@ -110,3 +110,15 @@ def test_bf16_roundtrip_matches_torch():
     theirs = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     np.testing.assert_array_equal(ours, theirs)
     np.testing.assert_array_equal(BF.to_f32(ours), torch.from_numpy(x).to(torch.bfloat16).float().numpy())
+
+
+def test_every_golden_fixture_matches_its_regenerated_inputs():
+    """The committed fixtures were computed from exactly the inputs tests/golden/cases.py
+    regenerates (checksummed), so every GPU comparison against them is meaningful."""
+    from tests.golden.load import module_case
+    for name in C.ATTN_CASES:
+        attention_case(name)
+    for name in C.GDN_CASES:
+        gdn_case(name)
+    for name in C.MODULE_CASES:
+        module_case(name)
