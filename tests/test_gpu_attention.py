@@ -196,3 +196,30 @@ def test_empty_batch_is_a_no_op():
     e = torch.zeros(0, dtype=torch.int64, device="cuda")
     out = ops.paged_decode(q, kb, kb, r2t, e, e, 0.125, 0)
     assert out.shape == (0, 8, 64)
+
+
+@pytest.mark.parametrize("shape", [
+    # (Hq, Hkv, D, [(prefix, extend), ...]): tcgen05 extend path (bf16, D 64/128/256, G 1..16)
+    (32, 4, 256, [(0, 300), (700, 129), (13, 1), (64, 64)]),
+    (8, 2, 256, [(1000, 77), (0, 17)]),
+    (16, 8, 128, [(250, 200), (5, 3)]),
+    (8, 8, 64, [(90, 140)]),
+    (16, 1, 128, [(40, 33), (0, 8)]),
+])
+def test_extend_random_shapes_vs_oracle(shape):
+    hq, hkv, d, reqs = shape
+    seq = [p + e for p, e in reqs]
+    ext = [e for _, e in reqs]
+    B = len(reqs)
+    spec = dict(dtype="bf16", hq=hq, hkv=hkv, d=d, seq=seq, ext=ext,
+                req=[int(x) for x in np.random.default_rng(d + hq).permutation(B + 2)[:B]],
+                slots=sum(seq) + 11, rows=B + 2, cols=max(seq) + 5, seed=hq * d + sum(seq))
+    inp = C.attn_inputs(spec)
+    out = values(_run(inp, spec, gate_mode="sigmoid"), "bf16").reshape(sum(ext), -1)
+    orc = OA.slot_based_attention(inp["q"], inp["k_buf"], inp["v_buf"], inp["req_to_token"],
+                                  inp["req_pool_indices"], inp["seq_lens"], inp["extend_lens"],
+                                  d ** -0.5, "bf16")
+    t = orc.shape[0]
+    want = OA.output_gate(BF.round_f32(orc).reshape(t, -1), inp["gate"].reshape(t, -1),
+                          "sigmoid", "bf16")
+    assert_close(out, want, "bf16", what=f"extend {shape}")

@@ -245,6 +245,8 @@ tf_status tf_paged_extend_attn(const tf_paged_attn_args* a, void* ws, size_t ws_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DeviceGuard g(s);
   if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  if (paged_extend_tc_supported(*a))
+    return cuda_status(launch_paged_extend_tc(*a, s), "tf_paged_extend_attn");
   return cuda_status(launch_paged_attn_simt(*a, s), "tf_paged_extend_attn");
 }
 

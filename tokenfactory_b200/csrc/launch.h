@@ -14,6 +14,10 @@ cudaError_t launch_kv_store(const tf_kv_store_args& a, cudaStream_t s);
 // paged_attn_simt.cu: any dtype / head_dim <= 256, decode and extend
 cudaError_t launch_paged_attn_simt(const tf_paged_attn_args& a, cudaStream_t s);
 
+// paged_extend_tc.cu: bf16 extend on tcgen05 / TMEM
+bool paged_extend_tc_supported(const tf_paged_attn_args& a);
+cudaError_t launch_paged_extend_tc(const tf_paged_attn_args& a, cudaStream_t s);
+
 // paged_decode_mma.cu: bf16 / fp16 decode on tensor cores, balanced split-KV
 bool paged_decode_mma_supported(const tf_paged_attn_args& a);
 size_t paged_decode_mma_workspace(const tf_paged_attn_args& a, int num_sms);

@@ -73,7 +73,11 @@ __global__ void __launch_bounds__(kThreads) paged_attn_simt_kernel(tf_paged_attn
   const int b = sh_b;
   if (b < 0) return;  // token beyond sum(extend_lens): nothing to compute
   const int64_t i = t - sh_start;
-  const int64_t L = a.seq_lens[b];
+  int64_t L = a.seq_lens[b];
+  if (L > a.r2t_cols) {
+    if (tid == 0) record_err(a.err, TF_KERR_SLOT_RANGE);
+    L = a.r2t_cols;
+  }
   const int64_t E = a.extend_lens ? a.extend_lens[b] : 1;
   const int64_t q_abs = L - E + i;
   const int64_t limit = q_abs + 1 < L ? q_abs + 1 : L;  // keys j < limit are visible

@@ -91,7 +91,7 @@ inline size_t ws_bytes(int B, int nctas, int D) {
 // plan: tile_start[b] = sum_{b'<b} ceil(seq_lens[b'] / 32)
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int B,
-                                                    int32_t* tile_start) {
+                                                    int64_t max_len, int32_t* tile_start) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int
     const int b = b0 + tid;
     int64_t L = b < B ? seq_lens[b] : 0;
     if (L < 0) L = 0;
+    if (L > max_len) L = max_len;
     int32_t v = (int32_t)((L + kTileTok - 1) / kTileTok);
     int32_t incl = v;
 #pragma unroll
@@ -154,7 +155,9 @@ struct Meta {
   }
   __device__ __forceinline__ int64_t len(int b) const {
     const int i = b - c->bf;
-    return (i >= 0 && i < c->n) ? c->len[i] : a->seq_lens[b];
+    if (i >= 0 && i < c->n) return c->len[i];
+    const int64_t len = a->seq_lens[b];
+    return len < a->r2t_cols ? len : a->r2t_cols;
   }
 };
 
@@ -277,7 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t r = a.req_pool_indices[b];
       if (r < 0 || r >= a.r2t_rows) { record_err(err, TF_KERR_REQ_RANGE); r = 0; }
       rc->row_off[i] = r * a.r2t_stride;
-      rc->len[i] = a.seq_lens[b];
+      int64_t len = a.seq_lens[b];
+      if (len > a.r2t_cols) { record_err(err, TF_KERR_SLOT_RANGE); len = a.r2t_cols; }
+      rc->len[i] = len;
     }
   }
   __syncthreads();
@@ -546,7 +551,7 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, c
   cudaError_t e = cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<D>::kSmem);
   if (e != cudaSuccess) return e;
-  plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, ws.tile_start);
+  plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, a.r2t_cols, ws.tile_start);
   decode_kernel<D><<<nctas, kThreads, Cfg<D>::kSmem, s>>>(a, ws, nctas);
   // a unit spans at most every CTA: weights [nctas][kHeads] + slot ids [nctas]
   const size_t csmem = (size_t)nctas * (kHeads * 4 + 4);
