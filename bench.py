@@ -12,6 +12,8 @@ step of one full-attention layer: KV store of the new token (a1) + paged decode 
 (qwen3_8/full_attention.py:43-52, kv heads replicated once N > 4) and every rank decodes the whole
 batch for its heads: total work is fixed, so scaling is "strong".
 --config 3: Gated DeltaNet recurrent decode (B=256, Hk=16, Hv=48, dk=dv=128, fp32 state).
+--config 4: extend over a radix-cached prefix (16 requests, prefix U[0,4096], extend U[512,2048]):
+            causal extend attention in TFLOP/s, and the GDN extend of the same tokens.
 
 Timing: W warm-up steps, then K steps between CUDA events on the launching stream, bracketed by a
 barrier and synchronize; the max over ranks is reported.  The K/V read per step (2.3 GB) is far
@@ -385,6 +387,128 @@ def bench_gdn_decode(args, rank, world, dev):
 
 
 # ---------------------------------------------------------------------------------------------
+# config 4: extend / prefill over a radix-cached prefix
+# ---------------------------------------------------------------------------------------------
+C4 = dict(B=16, Pmax=4096, Emin=512, Emax=2048, Hq=32, Hkv=4, D=256, Hk=16, Hv=48, dk=128,
+          dv=128, K=4, slots=1_200_000)
+
+
+def _peak_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def bench_extend(args, rank, world, dev):
+    from tokenfactory_b200 import ops
+    from tokenfactory_b200.tp import head_shard
+
+    B, D = C4["B"], C4["D"]
+    sh = head_shard(C4["Hq"], C4["Hkv"], C4["Hk"], C4["Hv"], rank, world)
+    hq, hkv, hk, hv = len(sh.q_heads), len(sh.kv_heads), len(sh.k_heads), len(sh.v_heads)
+    gen = torch.Generator().manual_seed(4)
+    P = torch.randint(0, C4["Pmax"] + 1, (B,), generator=gen)
+    E = torch.randint(C4["Emin"], C4["Emax"] + 1, (B,), generator=gen)
+    L = P + E
+    T = int(E.sum())
+    S = C4["slots"]
+    perm = torch.randperm(S - 1, generator=gen)[: int(L.sum())] + 1
+    Lmax = int(L.max())
+    r2t = torch.full((B, Lmax), -1, dtype=torch.int64)
+    off = 0
+    for b in range(B):
+        r2t[b, :int(L[b])] = perm[off:off + int(L[b])]
+        off += int(L[b])
+    out_loc = torch.cat([r2t[b, int(P[b]):int(L[b])] for b in range(B)])
+    g = torch.Generator(device=dev).manual_seed(40 + rank)
+    bf = torch.bfloat16
+    kb = torch.randn((S, hkv, D), generator=g, device=dev, dtype=bf)
+    vb = torch.randn((S, hkv, D), generator=g, device=dev, dtype=bf)
+    q = torch.randn((T, hq, D), generator=g, device=dev, dtype=bf)
+    gate = torch.randn((T, hq, D), generator=g, device=dev, dtype=bf)
+    knew = torch.randn((T, hkv, D), generator=g, device=dev, dtype=bf)
+    vnew = torch.randn((T, hkv, D), generator=g, device=dev, dtype=bf)
+    r2t_d, loc_d = r2t.to(dev), out_loc.to(dev)
+    rpi = torch.arange(B, dtype=torch.int64, device=dev)
+    L_d, E_d = L.to(dev), E.to(dev)
+    attn_out = torch.empty_like(q)
+    # GDN extend inputs for the same requests (state resident at their pool rows)
+    dk, dv, K = C4["dk"], C4["dv"], C4["K"]
+    conv_dim = 2 * hk * dk + hv * dv
+    ssm = torch.randn((2 * B, hv, dk, dv), generator=g, device=dev) * 0.02
+    conv = torch.randn((2 * B, conv_dim, K - 1), generator=g, device=dev, dtype=bf)
+    qkv = torch.randn((T, conv_dim), generator=g, device=dev, dtype=bf)
+    bb = torch.randn((T, hv), generator=g, device=dev, dtype=bf)
+    aa = torch.randn((T, hv), generator=g, device=dev, dtype=bf)
+    z = torch.randn((T, hv * dv), generator=g, device=dev, dtype=bf)
+    w = torch.randn((conv_dim, 1, K), generator=g, device=dev, dtype=bf) * 0.5
+    A_log = (torch.rand((hv,), generator=g, device=dev) * 1.5).to(bf)
+    dt_bias = torch.randn((hv,), generator=g, device=dev, dtype=bf) * 0.5
+    nw = torch.ones((hv * dv,), device=dev, dtype=bf)
+    gdn_out = torch.empty((T, hv * dv), device=dev, dtype=bf)
+    scale = D ** -0.5
+    stream = torch.cuda.current_stream()
+
+    def attn_step():
+        ops.kv_store(kb, vb, loc_d, knew, vnew)
+        ops.paged_extend(q, kb, vb, r2t_d, rpi, L_d, E_d, scale, Lmax, int(E.max()), gate=gate,
+                         gate_mode="sigmoid", out=attn_out)
+
+    def gdn_step():
+        ops.gdn_extend(qkv, bb, aa, w, A_log, dt_bias, conv, ssm, rpi, E_d, num_k_heads=hk,
+                       head_k_dim=dk, head_v_dim=dv, max_extend_len=int(E.max()), z=z,
+                       norm_weight=nw, out=gdn_out)
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        _barrier(world)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        return _max_over_ranks(t0.elapsed_time(t1) / 1e3, world) / steps
+
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        attn_s = timed(attn_step, args.steps)
+        gdn_s = timed(gdn_step, max(1, args.steps // 4))
+    Pf, Ef = P.double(), E.double()
+    flops = float((4 * C4["Hq"] * D * (Ef * Pf + Ef * (Ef + 1) / 2)).sum())  # whole job
+    gdn_flops_tok = C4["Hv"] * (6 * dk * dv + 3 * 64 * dv) + C4["Hk"] * 4 * 64 * dk
+    peak, peak_kind = _peak_tflops()
+    tflops = flops / attn_s / 1e12
+    per_gpu = tflops / world
+    return {
+        "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": attn_s * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config4 extend over a cached prefix (one full-attention layer: "
+                               "KV store + causal extend attention with sigmoid gate)",
+                   "requests": B, "prefix": f"U[0,{C4['Pmax']}]",
+                   "extend": f"U[{C4['Emin']},{C4['Emax']}]", "new_tokens": T,
+                   "q_heads": C4["Hq"], "kv_heads": C4["Hkv"], "head_dim": D,
+                   "parallelism": f"tp{world}",
+                   "l2": "K/V of the prefixes re-read from L2 by the query tiles; no flush"},
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                     "frac": per_gpu / peak, "peak_kind": peak_kind,
+                     "kernel": "tf_paged_extend_attn (tcgen05)", "flops_per_launch": flops / world,
+                     "traffic": _profile_traffic("paged_extend_config4.md")},
+        "gdn_extend": {"tok_per_s": T / gdn_s, "ms_per_step": gdn_s * 1e3,
+                       "tflops_min_count": T * gdn_flops_tok / gdn_s / 1e12,
+                       "kernel": "tf_gdn_extend (conv + recurrent state in registers)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU baseline: the oracle (restatement of the reference's torch algorithm) on this host
 # ---------------------------------------------------------------------------------------------
 def _cpu_decode_sample(n_requests: int, seed: int = 0):
@@ -477,7 +601,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=C2["B"],
@@ -502,8 +626,8 @@ def main():
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     dev = torch.device("cuda", torch.cuda.current_device())
-    res = bench_decode(args, rank, world, dev) if args.config == 2 else \
-        bench_gdn_decode(args, rank, world, dev)
+    res = {2: bench_decode, 3: bench_gdn_decode, 4: bench_extend}[args.config](args, rank, world,
+                                                                              dev)
     if rank == 0 and world == 1 and args.config == 2 and not args.no_e2e and \
             args.cpu_baseline_seconds > 0:
         threads = os.cpu_count() or 1
