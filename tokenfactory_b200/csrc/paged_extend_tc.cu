@@ -1,20 +1,26 @@
 // a3 + a4: paged GQA extend / prefill attention over a radix-cached prefix on the 5th-generation
 // tensor cores (qwen3_8/full_attention.py:179-213 and :244-283, output gate :157-158).
 //
-// One CTA (one warpgroup, 128 threads) owns 128 query rows: 128/G consecutive query tokens of one
-// request times the G query heads that share kv head h (GQA packed into M).  Q stays resident in
-// shared memory (SWIZZLE_128B, K-major).  Keys are visited in tiles of 64 token rows gathered
-// through req_to_token by cp.async into a double-buffered SWIZZLE_128B ring (K and V with the same
-// physical layout: K is read K-major, V MN-major).  Per tile:
-//   S = Q.K^T      tcgen05.mma M128 N64 K16 x D/16 -> TMEM (64 fp32 columns)
-//   softmax        thread r owns row r: tcgen05.ld of its 64 scores, causal mask, online max/sum
-//                  with a lazy rescale (O in TMEM is rescaled only when a row's max grows by more
-//                  than 2^8), P in bf16 written to shared memory (SWIZZLE_128B, K-major)
-//   O += P.V       tcgen05.mma M128 N=D K16 x 4 -> TMEM (D fp32 columns)
-// Completion of each MMA group is tracked with tcgen05.commit on an mbarrier; every wait is
-// bounded.  The epilogue reads O from TMEM, divides by the row sum, applies the output gate and
-// stores bf16.  Rows past the end of the request and keys outside a row's causal window are
-// masked; query i of request b sees keys j <= seq_len - extend_len + i.
+// One CTA owns 128 query rows: 128/G consecutive query tokens of one request times the G query
+// heads that share kv head h (GQA packed into M), and walks the visible keys in tiles of 64 token
+// rows gathered through req_to_token.  The CTA is warp-specialised:
+//   warps 0-3  softmax: thread r owns row r (TMEM lane r).  Reads S_j from TMEM, applies the causal
+//              mask and an online max/sum with a lazy rescale (O is rescaled in TMEM only when a
+//              row's max grows by more than 2^8), writes P_j as bf16 into TMEM, then runs the
+//              epilogue (O / l, output gate, bf16 store).
+//   warps 4-7  producers: load Q once, then gather K and V rows (one 16-byte cp.async per lane,
+//              whole rows per warp instruction) into a ring of SWIZZLE_128B slots; each slot holds
+//              the K or the V half of a key tile and is filled in the order the MMAs consume it
+//              (K0 K1 V0 K2 V1 K3 ...).  Completion is tracked by cp.async.mbarrier.arrive.
+//   warp 8     one thread issues the tcgen05.mma chain: S_0, S_1, then per tile PV_j followed by
+//              S_{j+2}, so the tensor core computes while the softmax of tile j+1 runs.
+//                S = Q.K^T    M128 N64 K16 x D/16, A and B from shared memory
+//                O += P.V     M128 N=D K16 x 4, A (P) from TMEM, B (V) MN-major in shared memory
+// TMEM holds two S buffers, O, and two P buffers, so no MMA overwrites an operand that an
+// earlier MMA still reads.  Every wait is bounded; a wait that gives up raises a CTA-wide abort
+// flag, the other roles leave their loops, and the kernel records TF_KERR_TIMEOUT.  Rows past the
+// end of the request and keys outside a row's causal window are masked; query i of request b
+// sees keys j <= seq_len - extend_len + i.
 #include "common.cuh"
 #include "launch.h"
 #include "tcgen05.cuh"
@@ -24,7 +30,12 @@ namespace ext {
 
 constexpr int kRows = 128;
 constexpr int kBN = 64;
-constexpr int kThreads = 128;
+constexpr int kSoftmaxWarps = 4;
+constexpr int kProducerWarps = 4;
+constexpr int kMmaWarp = kSoftmaxWarps + kProducerWarps;
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kProducerThreads = kProducerWarps * 32;
+constexpr int kRowsPerProducer = kBN / kProducerWarps;  // key rows of a tile per producer warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;
 
@@ -34,18 +45,40 @@ struct Cfg {
   static constexpr int kQBlock = kRows * 128;    // one 64-dim block of Q
   static constexpr int kKVBlock = kBN * 128;     // one 64-dim block of a K or V tile
   static constexpr int kQBytes = kKB * kQBlock;
-  static constexpr int kKBytes = kKB * kKVBlock;
-  static constexpr int kStage = 2 * kKBytes;     // K tile then V tile
-  static constexpr int kPBytes = kRows * 128;    // P: 128 rows x 64 keys bf16
-  static constexpr int kOffKV = kQBytes;
-  static constexpr int kOffP = kOffKV + 2 * kStage;
-  static constexpr int kOffMisc = kOffP + kPBytes;   // barriers, TMEM holder, slot ids
-  static constexpr int kMiscBytes = 64 + 2 * kBN * 8;
-  static constexpr int kSmem = kOffMisc + kMiscBytes + 1024;  // + slack to align the base
-  static constexpr int kColO = kBN;
-  static constexpr int kTmemCols = (kBN + D) <= 256 ? 256 : 512;
+  static constexpr int kSlotBytes = kKB * kKVBlock;
+  static constexpr int kSlots = D == 256 ? 5 : (D == 128 ? 10 : 8);
+  static constexpr int kOffRing = kQBytes;
+  static constexpr int kOffBars = kOffRing + kSlots * kSlotBytes;
+  // barriers: full[kSlots], empty[kSlots], s_full[2], p_full[2], o_done, q_full, fin
+  static constexpr int kNumBars = 2 * kSlots + 7;
+  static constexpr int kOffWords = kOffBars + 8 * kNumBars;   // tmem holder, abort, q0 (int64)
+  static constexpr int kOffSlotIds = kOffWords + 16;          // int64 [2][kBN]
+  static constexpr int kSmem = kOffSlotIds + 2 * kBN * 8 + 1024;  // + slack to align the base
+  static constexpr int kColS = 0;                 // S buffers at [0,64) and [64,128)
+  static constexpr int kColO = 2 * kBN;           // O: D columns
+  static constexpr int kColP = kColO + D;         // P buffers: 32 columns each (bf16 pairs)
+  static constexpr int kTmemCols = kColP + kBN <= 256 ? 256 : 512;
   static_assert(D % 64 == 0, "head_dim multiple of 64");
+  static_assert(kSmem <= 232448, "shared memory per CTA");
+  static_assert(kOffSlotIds % 8 == 0, "slot id alignment");
 };
+
+// Bounded mbarrier wait that also gives up when another role raised the abort flag.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kSpinLimitNs) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -55,10 +88,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023) & ~1023u;
   unsigned char* sbase = smem_raw + (base - raw_base);
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sbase + C::kOffMisc);
-  uint64_t* bar_o = bar_s + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar_s + 2);
-  int64_t* slot_s = reinterpret_cast<int64_t*>(sbase + C::kOffMisc + 64);  // [2][kBN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + C::kOffBars);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kSlots;
+  uint64_t* s_full = bars + 2 * C::kSlots;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* q_full = o_done + 1;
+  uint64_t* fin = q_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sbase + C::kOffWords);
+  volatile int* abort = reinterpret_cast<volatile int*>(sbase + C::kOffWords + 4);
+  int64_t* s_q0 = reinterpret_cast<int64_t*>(sbase + C::kOffWords + 8);
+  int64_t* slot_ids = reinterpret_cast<int64_t*>(sbase + C::kOffSlotIds);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int Hkv = a.num_kv_heads, G = a.num_q_heads / Hkv;
@@ -71,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tile_start >= E) return;
   const int64_t L = a.seq_lens[b];
   if (L > a.r2t_cols || L < E) {  // a length the req_to_token table cannot hold
-    if (threadIdx.x == 0) record_err(a.err, TF_KERR_SLOT_RANGE);
+    if (tid == 0) record_err(a.err, TF_KERR_SLOT_RANGE);
     return;
   }
   const int64_t P = L - E;
@@ -79,236 +120,290 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t kv_end = P + tile_start + n_tok;  // keys [0, kv_end) are visible to some row
   const int ntiles = (int)((kv_end + kBN - 1) / kBN);
 
-  // token offset of request b (exclusive prefix of extend_lens), by warp 0
-  __shared__ int64_t s_q0;
-  if (warp == 0) {
+  if (warp == 0) {  // token offset of request b: exclusive prefix of extend_lens
     int64_t acc = 0;
     for (int i = lane; i < b; i += 32) acc += a.extend_lens ? a.extend_lens[i] : 1;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) s_q0 = acc;
+    if (lane == 0) *s_q0 = acc;
   }
-  int64_t row = a.req_pool_indices[b];
-  if (row < 0 || row >= a.r2t_rows) {
-    if (tid == 0) record_err(a.err, TF_KERR_REQ_RANGE);
-    row = 0;
-  }
-  const int64_t* r2t = a.req_to_token + row * a.r2t_stride;
-
   if (tid == 0) {
-    mbar_init(bar_s, 1);
-    mbar_init(bar_o, 1);
+    for (int i = 0; i < C::kSlots; ++i) {
+      mbar_init(&full[i], kProducerThreads);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], kSoftmaxWarps);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(q_full, kProducerThreads);
+    mbar_init(fin, 1);
+    *abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0) tc::tmem_alloc(tmem_holder, C::kTmemCols);
+  if (warp == kMmaWarp) tc::tmem_alloc(tmem_holder, C::kTmemCols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_holder;
-  const int64_t q0 = s_q0 + tile_start;
+  const int64_t q0 = *s_q0 + tile_start;
 
-  // ---- Q tile -> shared memory (rows past the request end are zero)
-  {
-    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
-    constexpr int CPR = D / 8;  // 16-byte chunks per row
-    for (int e = tid; e < kRows * CPR; e += kThreads) {
-      const int r = e / CPR, ch = e - (e / CPR) * CPR;
-      const int i = r / G, g = r - (r / G) * G;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (i < n_tok)
-        v = *reinterpret_cast<const uint4*>(q + (q0 + i) * a.q_stride_tok +
-                                            (int64_t)(h * G + g) * a.q_stride_head + ch * 8);
-      const uint32_t dst = base + (ch >> 3) * C::kQBlock + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(v.x), "r"(v.y),
-                   "r"(v.z), "r"(v.w)
-                   : "memory");
+  if (warp >= kSoftmaxWarps && warp < kMmaWarp) {
+    // ======================= producers =======================
+    const int pw = warp - kSoftmaxWarps;
+    constexpr int CPR = D / 8;          // 16-byte chunks per row
+    constexpr int RPI = 32 / CPR;       // rows per warp instruction
+    const int sub = lane / CPR, ch = lane - (lane / CPR) * CPR;
+    // Q: 128 rows, pw owns rows [32 pw, 32 pw + 32); rows past the request end are zero
+    {
+      const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+#pragma unroll 4
+      for (int i = 0; i < 32; i += RPI) {
+        const int r = pw * 32 + i + sub;
+        const int ti = r / G, g = r - (r / G) * G;
+        const bool v = ti < n_tok;
+        const __nv_bfloat16* src =
+            v ? q + (q0 + ti) * a.q_stride_tok + (int64_t)(h * G + g) * a.q_stride_head + ch * 8
+              : q;
+        const uint32_t dst = base + (ch >> 3) * C::kQBlock + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+        cp_async16_zfill(dst, src, v ? 16u : 0u);
+      }
+      cp_async_arrive_noinc(q_full);
     }
-  }
-
-  const char* kbuf = (const char*)a.k_buffer + (int64_t)h * a.kv_stride_head * 2;
-  const char* vbuf = (const char*)a.v_buffer + (int64_t)h * a.kv_stride_head * 2;
-  const int64_t sstride = a.kv_stride_slot * 2;
-  auto raw_slot = [&](int tile) -> int64_t {  // threads < kBN: key tile*64 + tid
-    int64_t key = (int64_t)tile * kBN + tid;
-    if (key >= kv_end) key = (int64_t)tile * kBN;  // past the window: repeat the tile's first key
-    return r2t[key];
-  };
-  auto issue_tile = [&](int tile, int buf, int64_t raw) {
-    if (tid < kBN) slot_s[buf * kBN + tid] = resolve_slot(raw, a.num_slots, a.slot_mode, a.err);
-    __syncthreads();
-    constexpr int CPR = D / 8;
-    const uint32_t st = base + C::kOffKV + buf * C::kStage;
-    for (int e = tid; e < 2 * kBN * CPR; e += kThreads) {
-      const int isv = e / (kBN * CPR);
-      const int rem = e - isv * (kBN * CPR);
-      const int key = rem / CPR, ch = rem - (rem / CPR) * CPR;
-      const char* src = (isv ? vbuf : kbuf) + slot_s[buf * kBN + key] * sstride + ch * 16;
-      const uint32_t dst = st + isv * C::kKBytes + (ch >> 3) * C::kKVBlock + key * 128 +
-                           (((ch & 7) ^ (key & 7)) << 4);
-      cp_async16(dst, src);
+    int64_t row = a.req_pool_indices[b];
+    if (row < 0 || row >= a.r2t_rows) {
+      if (tid == kSoftmaxWarps * 32) record_err(a.err, TF_KERR_REQ_RANGE);
+      row = 0;
     }
-    (void)tile;
-  };
-
-  const float c2 = a.scale * kLog2e;
-  const int r = tid;                 // this thread's row == TMEM lane
-  const int ri = r / G, rg = r - (r / G) * G;
-  const bool row_valid = ri < n_tok;
-  const int64_t klim = P + tile_start + ri + 1;  // keys [0, klim) visible to this row
-  float m_used = -INFINITY, l_sum = 0.f;
-  constexpr uint32_t kIdS = tc::idesc_bf16(kRows, kBN, false, false);
-  constexpr uint32_t kIdO = tc::idesc_bf16(kRows, D, false, true);
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-  int64_t next_raw = tid < kBN ? raw_slot(0) : 0;
-  issue_tile(0, 0, next_raw);
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  next_raw = (tid < kBN && ntiles > 1) ? raw_slot(1) : 0;
-
-  // Only thread 0 waits on the MMA barriers (bounded); it publishes the outcome in s_ok before a
-  // CTA barrier, so every thread takes the same exit, and the others order their TMEM accesses
-  // after that barrier with tcgen05.fence::after_thread_sync.
-  __shared__ int s_ok;
-  if (tid == 0) s_ok = 1;
-  for (int j = 0; j < ntiles; ++j) {
-    const int buf = j & 1;
-    if (tid == 0 && j >= 1 && !mbar_wait(bar_o, (j - 1) & 1)) s_ok = 0;  // PV_{j-1} done
-    __syncthreads();
-    if (!s_ok) break;
-    tc::fence_after_sync();
-    if (j + 1 < ntiles) {
-      issue_tile(j + 1, buf ^ 1, next_raw);
-      next_raw = (tid < kBN && j + 2 < ntiles) ? raw_slot(j + 2) : 0;
+    const int64_t* r2t = a.req_to_token + row * a.r2t_stride;
+    const char* kbuf = (const char*)a.k_buffer + (int64_t)h * a.kv_stride_head * 2;
+    const char* vbuf = (const char*)a.v_buffer + (int64_t)h * a.kv_stride_head * 2;
+    const int64_t sstride = a.kv_stride_slot * 2;
+    const int seg = pw * kRowsPerProducer;
+    auto raw_of = [&](int tile) -> int64_t {  // lanes < kRowsPerProducer: key of this lane's row
+      int64_t key = (int64_t)tile * kBN + seg + lane;
+      if (key >= kv_end) key = (int64_t)tile * kBN;  // past the window: repeat the tile's first key
+      return r2t[key];
+    };
+    int64_t raw_next = lane < kRowsPerProducer ? raw_of(0) : 0;
+    int slot = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    auto produce = [&](int tile, bool isv) {
+      const bool got = wait_bar(&empty[slot], phase ^ 1u, abort);
+      ok = __all_sync(0xffffffffu, got);
+      if (!ok) return;
+      int64_t* ids = slot_ids + (tile & 1) * kBN + seg;
+      if (!isv) {
+        const int64_t raw = raw_next;
+        if (tile + 1 < ntiles && lane < kRowsPerProducer) raw_next = raw_of(tile + 1);
+        if (lane < kRowsPerProducer) ids[lane] = resolve_slot(raw, a.num_slots, a.slot_mode, a.err);
+        __syncwarp();
+      }
+      const char* src0 = (isv ? vbuf : kbuf) + ch * 16;
+      const uint32_t dst0 = base + C::kOffRing + slot * C::kSlotBytes + (ch >> 3) * C::kKVBlock;
+#pragma unroll
+      for (int i = 0; i < kRowsPerProducer; i += RPI) {
+        const int r = seg + i + sub;  // key row in the tile
+        const int64_t sl = ids[i + sub];
+        cp_async16(dst0 + r * 128 + (((ch & 7) ^ (r & 7)) << 4), src0 + sl * sstride);
+      }
+      cp_async_arrive_noinc(&full[slot]);
+      if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
+    };
+    produce(0, false);
+    if (ok && ntiles > 1) produce(1, false);
+    for (int j = 0; ok && j < ntiles; ++j) {
+      produce(j, true);
+      if (ok && j + 2 < ntiles) produce(j + 2, false);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    tc::fence_proxy_async_smem();
-    __syncthreads();
-
-    // ---- S = Q . K_j^T
-    if (tid == 0) {
+    cp_async_wait_all();
+  } else if (warp == kMmaWarp) {
+    // ======================= MMA issue (one thread) =======================
+    if (lane == 0) {
+      constexpr uint32_t kIdS = tc::idesc_bf16(kRows, kBN, false, false);
+      constexpr uint32_t kIdO = tc::idesc_bf16(kRows, D, false, true);
+      bool ok = wait_bar(q_full, 0, abort);
+      tc::fence_proxy_async_smem();
+      int slot = 0;
+      uint32_t phase = 0;
+      auto take = [&]() -> uint32_t {  // wait for the next ring slot; returns its address
+        ok = ok && wait_bar(&full[slot], phase, abort);
+        tc::fence_proxy_async_smem();
+        return base + C::kOffRing + slot * C::kSlotBytes;
+      };
+      auto release = [&]() {
+        tc::commit(&empty[slot]);
+        if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
+      };
+      auto issue_s = [&](int t) {
+        const uint32_t kb = take();
+        if (!ok) return;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = tc::sw128_desc(base + (kk >> 2) * C::kQBlock + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sw128_desc(kb + (kk >> 2) * C::kKVBlock + (kk & 3) * 32, 16, 1024);
+          tc::mma_bf16(tmem + C::kColS + (t & 1) * kBN, ad, bd, kIdS, kk > 0);
+        }
+        tc::commit(&s_full[t & 1]);
+        release();
+      };
+      auto issue_pv = [&](int t) {
+        ok = ok && wait_bar(&p_full[t & 1], (t >> 1) & 1, abort);
+        tc::fence_after_sync();
+        const uint32_t vb = take();
+        if (!ok) return;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = tc::sw128_desc(vb + kk * 2048, C::kKVBlock, 1024);
+          tc::mma_bf16_ts(tmem + C::kColO, tmem + C::kColP + (t & 1) * (kBN / 2) + kk * 8, bd, kIdO,
+                          t > 0 || kk > 0);
+        }
+        tc::commit(o_done);
+        release();
+      };
+      if (ok) issue_s(0);
+      if (ok && ntiles > 1) issue_s(1);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        issue_pv(j);
+        if (ok && j + 2 < ntiles) issue_s(j + 2);
+      }
+      // every MMA issued above has completed before TMEM is read for the last time or released
+      tc::commit(fin);
+      if (!wait_bar(fin, 0, abort)) *abort = 1;
+    }
+    __syncwarp();
+  } else {
+    // ======================= softmax + epilogue (thread r = row r) =======================
+    const float c2 = a.scale * kLog2e;
+    const int r = tid;
+    const int ri = r / G, rg = r - (r / G) * G;
+    const bool row_valid = ri < n_tok;
+    const int64_t klim = P + tile_start + ri + 1;  // keys [0, klim) visible to this row
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float m_used = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int bi = j & 1;
+      ok = __all_sync(0xffffffffu, wait_bar(&s_full[bi], (j >> 1) & 1, abort));
+      if (!ok) break;
       tc::fence_after_sync();
-      const uint32_t kb = base + C::kOffKV + buf * C::kStage;
+      float s[2][32];
+      tc::ld32(tmem + lane_base + C::kColS + bi * kBN, s[0]);
+      tc::ld32(tmem + lane_base + C::kColS + bi * kBN + 32, s[1]);
+      tc::wait_ld();
+      const int64_t key0 = (int64_t)j * kBN;
+      float tmax = -INFINITY;
+      if (row_valid && key0 + kBN <= klim) {
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint64_t ad = tc::sw128_desc(base + (kk >> 2) * C::kQBlock + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = tc::sw128_desc(kb + (kk >> 2) * C::kKVBlock + (kk & 3) * 32, 16, 1024);
-        tc::mma_bf16(tmem, ad, bd, kIdS, kk > 0);
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            s[hh][k] *= c2;
+            tmax = fmaxf(tmax, s[hh][k]);
+          }
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const bool v = row_valid && key0 + hh * 32 + k < klim;
+            s[hh][k] = v ? s[hh][k] * c2 : -INFINITY;
+            tmax = fmaxf(tmax, s[hh][k]);
+          }
       }
-      tc::commit(bar_s);
-      if (!mbar_wait(bar_s, j & 1)) s_ok = 0;
+      const bool need = tmax > m_used + kRescaleLog2 || (m_used == -INFINITY && tmax > -INFINITY);
+      const float m_new = need ? tmax : m_used;
+      const float alpha = need ? (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new)) : 1.f;
+      m_used = m_new;
+      l_sum *= alpha;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {  // rescale this warp's O rows (PV_{j-1} done)
+        ok = __all_sync(0xffffffffu, wait_bar(o_done, (j - 1) & 1, abort));
+        if (!ok) break;
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float o[32];
+          tc::ld32(tmem + lane_base + C::kColO + cc * 32, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) o[k] *= alpha;
+          tc::st32(tmem + lane_base + C::kColO + cc * 32, o);
+        }
+      }
+      // P_j in bf16 -> TMEM (32 columns of bf16 pairs)
+      const float mu = m_used == -INFINITY ? 0.f : m_used;
+      float pk[32];
+#pragma unroll
+      for (int k2 = 0; k2 < 32; ++k2) {
+        const float p0 = exp2f(s[k2 >> 4][(2 * k2) & 31] - mu);
+        const float p1 = exp2f(s[k2 >> 4][(2 * k2 + 1) & 31] - mu);
+        l_sum += p0 + p1;
+        __nv_bfloat162 pv = __floats2bfloat162_rn(p0, p1);
+        pk[k2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&pv));
+      }
+      tc::st32(tmem + lane_base + C::kColP + bi * (kBN / 2), pk);
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[bi]);
     }
-    __syncthreads();
-    if (!s_ok) break;
-    tc::fence_after_sync();
-
-    // ---- online softmax of row r over this tile's 64 keys
-    float s[2][32];
-    tc::ld32(tmem + lane_base + 0, s[0]);
-    tc::ld32(tmem + lane_base + 32, s[1]);
-    tc::wait_ld();
-    const int64_t key0 = (int64_t)j * kBN;
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const bool v = row_valid && key0 + hh * 32 + k < klim;
-        s[hh][k] = v ? s[hh][k] * c2 : -INFINITY;
-        tmax = fmaxf(tmax, s[hh][k]);
-      }
-    const bool need = tmax > m_used + kRescaleLog2 || (m_used == -INFINITY && tmax > -INFINITY);
-    const float m_new = need ? tmax : m_used;
-    const float alpha = need ? (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new)) : 1.f;
-    m_used = m_new;
-    l_sum *= alpha;
-    if (j > 0 && __any_sync(0xffffffffu, need)) {  // rescale O rows of this warp (TMEM)
+    // ---- epilogue: O / l, output gate, bf16
+    // fin (one phase, committed after the last PV) rather than o_done: o_done can still be two
+    // phases short here, since PV_{n-2} is issued after S_{n-1}
+    if (ok) ok = __all_sync(0xffffffffu, wait_bar(fin, 0, abort));
+    if (ok) {
+      tc::fence_after_sync();
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+      const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
+      const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr;
+      const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(gate)) & 15) == 0 &&
+                       (a.out_stride_tok | a.out_stride_head | a.gate_stride_tok | a.gate_stride_head) % 8 == 0;
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const int64_t t = q0 + ri;
+      const int hq = h * G + rg;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
         tc::ld32(tmem + lane_base + C::kColO + cc * 32, o);
         tc::wait_ld();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) o[k] *= alpha;
-        tc::st32(tmem + lane_base + C::kColO + cc * 32, o);
-      }
-      tc::wait_st();
-    }
-    // P (bf16) -> shared memory, row r, SWIZZLE_128B
-    const uint32_t prow = base + C::kOffP + r * 128;
-#pragma unroll
-    for (int cch = 0; cch < 8; ++cch) {
-      uint32_t w[4];
-#pragma unroll
-      for (int q2 = 0; q2 < 4; ++q2) {
-        const int k = cch * 8 + q2 * 2;
-        const float x0 = s[k >> 5][k & 31], x1 = s[(k + 1) >> 5][(k + 1) & 31];
-        const float p0 = x0 == -INFINITY ? 0.f : exp2f(x0 - m_used);
-        const float p1 = x1 == -INFINITY ? 0.f : exp2f(x1 - m_used);
-        l_sum += p0 + p1;
-        __nv_bfloat162 pv = __floats2bfloat162_rn(p0, p1);
-        w[q2] = *reinterpret_cast<uint32_t*>(&pv);
-      }
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(prow + ((cch ^ (r & 7)) << 4)),
-                   "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
-                   : "memory");
-    }
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-
-    // ---- O (+)= P . V_j
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t vb = base + C::kOffKV + buf * C::kStage + C::kKBytes;
-#pragma unroll
-      for (int kk = 0; kk < kBN / 16; ++kk) {
-        const uint64_t ad = tc::sw128_desc(base + C::kOffP + kk * 32, 16, 1024);
-        const uint64_t bd = tc::sw128_desc(vb + kk * 2048, C::kKVBlock, 1024);
-        tc::mma_bf16(tmem + C::kColO, ad, bd, kIdO, j > 0 || kk > 0);
-      }
-      tc::commit(bar_o);
-    }
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  // the last PV must be complete before TMEM is read or released (bounded wait, thread 0)
-  if (tid == 0) {
-    if (!mbar_wait(bar_o, (ntiles - 1) & 1)) s_ok = 0;
-    if (!s_ok) record_err(a.err, TF_KERR_TIMEOUT);
-  }
-  __syncthreads();
-  const bool ok = s_ok != 0;
-  tc::fence_after_sync();
-
-  // ---- epilogue: O / l, output gate, bf16
-  if (ok) {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-    const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
-    const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-    const int64_t t = q0 + ri;
-    const int hq = h * G + rg;
-#pragma unroll 1
-    for (int cc = 0; cc < D / 32; ++cc) {
-      float o[32];
-      tc::ld32(tmem + lane_base + C::kColO + cc * 32, o);
-      tc::wait_ld();
-      if (row_valid) {
+        if (!row_valid) continue;
         __nv_bfloat16* op = out + t * a.out_stride_tok + (int64_t)hq * a.out_stride_head + cc * 32;
         const __nv_bfloat16* gp =
-            gate ? gate + t * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + cc * 32 : nullptr;
+            gated ? gate + t * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + cc * 32 : nullptr;
+        if (vec) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          float v = round_to<__nv_bfloat16>(l_sum > 0.f ? o[k] * inv : NAN);
-          if (a.gate_mode != TF_GATE_NONE && gp != nullptr)
-            v = apply_gate<__nv_bfloat16>(v, to_f(gp[k]), a.gate_mode);
-          op[k] = __float2bfloat16_rn(v);
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint4 gw = make_uint4(0, 0, 0, 0);
+            if (gated) gw = *reinterpret_cast<const uint4*>(gp + c8 * 8);
+            const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&gw);
+            uint4 ow;
+            __nv_bfloat16* ov = reinterpret_cast<__nv_bfloat16*>(&ow);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              float v = round_to<__nv_bfloat16>(l_sum > 0.f ? o[c8 * 8 + k] * inv : NAN);
+              if (gated) v = apply_gate<__nv_bfloat16>(v, to_f(gv[k]), a.gate_mode);
+              ov[k] = __float2bfloat16_rn(v);
+            }
+            *reinterpret_cast<uint4*>(op + c8 * 8) = ow;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            float v = round_to<__nv_bfloat16>(l_sum > 0.f ? o[k] * inv : NAN);
+            if (gated) v = apply_gate<__nv_bfloat16>(v, to_f(gp[k]), a.gate_mode);
+            op[k] = __float2bfloat16_rn(v);
+          }
         }
       }
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, C::kTmemCols);
+  if (tid == 0 && *abort) record_err(a.err, TF_KERR_TIMEOUT);
+  tc::fence_after_sync();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, C::kTmemCols);
 }
 
 template <int D>
