@@ -80,6 +80,33 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
   }
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// max of 64 scores as a tree of three-input maxima (depth 4 instead of a 64-long chain)
+__device__ __forceinline__ float max_of_64(const float (&s)[2][32]) {
+  float t[22];
+#pragma unroll
+  for (int i = 0; i < 21; ++i) {
+    const int k = 3 * i;
+    t[i] = max3(s[k >> 5][k & 31], s[(k + 1) >> 5][(k + 1) & 31], s[(k + 2) >> 5][(k + 2) & 31]);
+  }
+  t[21] = s[1][31];
+  float u[8];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) u[i] = max3(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
+  u[7] = t[21];
+  return fmaxf(max3(u[0], u[1], u[2]), max3(u[3], u[4], max3(u[5], u[6], u[7])));
+}
+// 2^x with the hardware approximation (flush-to-zero): x = -inf gives +0
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     extend_kernel(tf_paged_attn_args a, int tiles_per_req) {
@@ -186,7 +213,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (key >= kv_end) key = (int64_t)tile * kBN;  // past the window: repeat the tile's first key
       return r2t[key];
     };
-    int64_t raw_next = lane < kRowsPerProducer ? raw_of(0) : 0;
+    // raw req_to_token entries of the next kPrefetch K tiles: this load returns behind the
+    // tile gathers already in flight, so it is issued several tiles ahead of its use
+    constexpr int kPrefetch = 4;
+    int64_t raw_q[kPrefetch];
+#pragma unroll
+    for (int i = 0; i < kPrefetch; ++i) raw_q[i] = (lane < kRowsPerProducer && i < ntiles) ? raw_of(i) : 0;
     int slot = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -196,8 +228,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) return;
       int64_t* ids = slot_ids + (tile & 1) * kBN + seg;
       if (!isv) {
-        const int64_t raw = raw_next;
-        if (tile + 1 < ntiles && lane < kRowsPerProducer) raw_next = raw_of(tile + 1);
+        const int64_t raw = raw_q[0];
+#pragma unroll
+        for (int i = 0; i + 1 < kPrefetch; ++i) raw_q[i] = raw_q[i + 1];
+        raw_q[kPrefetch - 1] =
+            (tile + kPrefetch < ntiles && lane < kRowsPerProducer) ? raw_of(tile + kPrefetch) : 0;
         if (lane < kRowsPerProducer) ids[lane] = resolve_slot(raw, a.num_slots, a.slot_mode, a.err);
         __syncwarp();
       }
@@ -294,25 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::ld32(tmem + lane_base + C::kColS + bi * kBN + 32, s[1]);
       tc::wait_ld();
       const int64_t key0 = (int64_t)j * kBN;
-      float tmax = -INFINITY;
-      if (row_valid && key0 + kBN <= klim) {
+      // raw scores: masked keys become -inf, the max is taken on raw scores (c2 > 0; the host
+      // routes c2 <= 0 elsewhere) and the scale is folded into the exponent's FFMA
+      if (!(row_valid && key0 + kBN <= klim)) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            s[hh][k] *= c2;
-            tmax = fmaxf(tmax, s[hh][k]);
-          }
-      } else {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const bool v = row_valid && key0 + hh * 32 + k < klim;
-            s[hh][k] = v ? s[hh][k] * c2 : -INFINITY;
-            tmax = fmaxf(tmax, s[hh][k]);
-          }
+          for (int k = 0; k < 32; ++k)
+            if (!(row_valid && key0 + hh * 32 + k < klim)) s[hh][k] = -INFINITY;
       }
+      const float tmax = max_of_64(s) * c2;
       const bool need = tmax > m_used + kRescaleLog2 || (m_used == -INFINITY && tmax > -INFINITY);
       const float m_new = need ? tmax : m_used;
       const float alpha = need ? (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new)) : 1.f;
@@ -333,16 +359,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // P_j in bf16 -> TMEM (32 columns of bf16 pairs)
-      const float mu = m_used == -INFINITY ? 0.f : m_used;
+      const float nmu = m_used == -INFINITY ? 0.f : -m_used;
       float pk[32];
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k2 = 0; k2 < 32; ++k2) {
-        const float p0 = exp2f(s[k2 >> 4][(2 * k2) & 31] - mu);
-        const float p1 = exp2f(s[k2 >> 4][(2 * k2 + 1) & 31] - mu);
-        l_sum += p0 + p1;
+        const float p0 = ex2_ftz(fmaf(s[k2 >> 4][(2 * k2) & 31], c2, nmu));
+        const float p1 = ex2_ftz(fmaf(s[k2 >> 4][(2 * k2 + 1) & 31], c2, nmu));
+        ls[k2 & 3] += p0 + p1;
         __nv_bfloat162 pv = __floats2bfloat162_rn(p0, p1);
         pk[k2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&pv));
       }
+      l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tc::st32(tmem + lane_base + C::kColP + bi * (kBN / 2), pk);
       tc::wait_st();
       tc::fence_before_sync();
@@ -419,6 +447,517 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+
+// =============================================================================================
+// Pair kernel (head_dim 128 / 256): two CTAs of a cluster on an SM pair run one M=256 tile with
+// tcgen05.mma.cta_group::2.  CTA r holds query rows [128 r, 128 r + 128) of the pair tile, and of
+// every key tile only keys [32 r, 32 r + 32) of K and dims [r D/2, (r+1) D/2) of V: the MMA reads
+// the B operand from both CTAs' shared memory, so each SM gathers half of the K/V bytes.
+//   rank 0, warp 8: issues every MMA of the pair; commits arrive on both CTAs' barriers
+//   rank 1, warp 8: relays "this CTA's half of slot s has landed" to rank 0's full barrier
+//   warps 0-3 of each CTA: softmax + epilogue of its own 128 rows (own TMEM)
+//   warps 4-7 of each CTA: gather its halves into its own ring
+// =============================================================================================
+namespace pair {
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void remote_store(uint32_t cluster_addr, int v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ bool try_wait_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire; on timeout raises the abort flag of both CTAs.
+__device__ __forceinline__ bool wait_c(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                       uint32_t peer_abort) {
+  const uint32_t addr = smem_u32(bar);
+  if (try_wait_cluster(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (try_wait_cluster(addr, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kSpinLimitNs) {
+        *abort = 1;
+        remote_store(peer_abort, 1);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void mma2_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc ? 1u : 0u)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc ? 1u : 0u)
+      : "memory");
+}
+// arrive once on the barrier at this offset in both CTAs when all prior MMAs have completed
+__device__ __forceinline__ void commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)), "h"((uint16_t)3)
+      : "memory");
+}
+
+constexpr int kSmWarps = 8;                    // two warps per 32-row group: key columns 0-31 / 32-63
+constexpr int kPrWarp0 = kSmWarps;             // producers: warps 8-11
+constexpr int kIssueWarp = kSmWarps + kProducerWarps;  // MMA issue (rank 0) / relay (rank 1)
+constexpr int kPairThreads = (kIssueWarp + 1) * 32;
+
+// p = 2^(s c2 - m) for 32 scores, packed as 16 bf16 pairs; returns the sum of the fp32 p
+__device__ __forceinline__ float exp_pack(const float (&sh)[32], float c2, float nmu, float (&pk)[16]) {
+  float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int k2 = 0; k2 < 16; ++k2) {
+    const float p0 = ex2_ftz(fmaf(sh[2 * k2], c2, nmu));
+    const float p1 = ex2_ftz(fmaf(sh[2 * k2 + 1], c2, nmu));
+    ls[k2 & 3] += p0 + p1;
+    __nv_bfloat162 pv = __floats2bfloat162_rn(p0, p1);
+    pk[k2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&pv));
+  }
+  return (ls[0] + ls[1]) + (ls[2] + ls[3]);
+}
+
+template <int D>
+struct Cfg {
+  static constexpr int kKB = D / 64;
+  static constexpr int kQBlock = kRows * 128;       // one 64-dim block of this CTA's Q rows
+  static constexpr int kQBytes = kKB * kQBlock;
+  static constexpr int kKBlk = (kBN / 2) * 128;     // K half: 32 keys x 128 B per 64-dim block
+  static constexpr int kVBlk = kBN * 128;           // V half: 64 keys x 128 B per 64-dim block
+  static constexpr int kSlotBytes = kKB * kKBlk;    // == (kKB / 2) * kVBlk
+  static constexpr int kSlots = D == 256 ? 10 : 16;
+  static constexpr int kOffRing = kQBytes;
+  static constexpr int kOffBars = kOffRing + kSlots * kSlotBytes;
+  static constexpr int kNumBars = 2 * kSlots + 7;   // full, empty, s_full[2], p_full[2], o_done, q_full, fin
+  static constexpr int kOffWords = kOffBars + 8 * kNumBars;
+  static constexpr int kOffIds = kOffWords + 16;    // int64 [2][kProducerWarps][24]
+  static constexpr int kSmem = kOffIds + 2 * kProducerWarps * 24 * 8 + 1024;
+  static constexpr int kColS = 0;
+  static constexpr int kColO = 2 * kBN;
+  static constexpr int kColP = kColO + D;
+  static constexpr int kTmemCols = 512;
+  static_assert(D == 128 || D == 256, "pair kernel head dims");
+  static_assert(kSlotBytes == (kKB / 2) * kVBlk, "K and V halves share the slot size");
+  static_assert(kSmem <= 232448, "shared memory per CTA");
+  static_assert(kColP + kBN <= kTmemCols, "TMEM columns");
+};
+
+template <int D>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    extend_pair_kernel(tf_paged_attn_args a, int pairs_per_req) {
+  using C = Cfg<D>;
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023) & ~1023u;
+  unsigned char* sbase = smem_raw + (base - raw_base);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + C::kOffBars);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kSlots;
+  uint64_t* s_full = bars + 2 * C::kSlots;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* q_full = o_done + 1;
+  uint64_t* fin = q_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sbase + C::kOffWords);
+  volatile int* abort = reinterpret_cast<volatile int*>(sbase + C::kOffWords + 4);
+  int64_t* s_q0 = reinterpret_cast<int64_t*>(sbase + C::kOffWords + 8);
+  int64_t* ids_all = reinterpret_cast<int64_t*>(sbase + C::kOffIds);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t peer = rank ^ 1u;
+  const uint32_t peer_abort = peer_addr(smem_u32((const void*)abort), peer);
+  const int Hkv = a.num_kv_heads, G = a.num_q_heads / Hkv;
+  const int TQ = kRows / G;  // query tokens per CTA
+  const int pidx = blockIdx.x >> 1;
+  const int b = pidx / pairs_per_req;
+  const int qp = pairs_per_req - 1 - (pidx - b * pairs_per_req);  // longest pair tiles first
+  const int h = blockIdx.y;
+  const int64_t E = a.extend_lens ? a.extend_lens[b] : 1;
+  const int64_t pair_start = (int64_t)qp * 2 * TQ;
+  if (pair_start >= E) return;  // both CTAs of the pair leave here, before any cluster barrier
+  const int64_t L = a.seq_lens[b];
+  if (L > a.r2t_cols || L < E) {
+    if (tid == 0 && rank == 0) record_err(a.err, TF_KERR_SLOT_RANGE);
+    return;
+  }
+  const int64_t P = L - E;
+  const int64_t cta_start = pair_start + (int64_t)rank * TQ;  // first token of this CTA's rows
+  const int n_tok = (int)(E - cta_start <= 0 ? 0 : (E - cta_start < TQ ? E - cta_start : TQ));
+  const int64_t pair_end = E - pair_start < 2 * TQ ? E : pair_start + 2 * TQ;
+  const int64_t kv_end = P + pair_end;  // keys [0, kv_end) are visible to some row of the pair
+  const int ntiles = (int)((kv_end + kBN - 1) / kBN);
+
+  if (warp == 0) {
+    int64_t acc = 0;
+    for (int i = lane; i < b; i += 32) acc += a.extend_lens ? a.extend_lens[i] : 1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) *s_q0 = acc;
+  }
+  if (tid == 0) {
+    const uint32_t in_count = rank == 0 ? kProducerThreads + 1 : kProducerThreads;
+    for (int i = 0; i < C::kSlots; ++i) {
+      mbar_init(&full[i], in_count);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 2 * kSmWarps);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(q_full, in_count);
+    mbar_init(fin, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kIssueWarp) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)), "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc::fence_before_sync();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const int64_t q0 = *s_q0 + cta_start;
+
+  if (warp >= kPrWarp0 && warp < kIssueWarp) {
+    // ======================= producers: this CTA's halves =======================
+    const int pw = warp - kPrWarp0;
+    {  // Q: this CTA's 128 rows
+      constexpr int CPR = D / 8, RPI = 32 / CPR;
+      const int sub = lane / CPR, ch = lane - (lane / CPR) * CPR;
+      const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+#pragma unroll 4
+      for (int i = 0; i < 32; i += RPI) {
+        const int r = pw * 32 + i + sub;
+        const int ti = r / G, g = r - (r / G) * G;
+        const bool v = ti < n_tok;
+        const __nv_bfloat16* src =
+            v ? q + (q0 + ti) * a.q_stride_tok + (int64_t)(h * G + g) * a.q_stride_head + ch * 8 : q;
+        cp_async16_zfill(base + (ch >> 3) * C::kQBlock + r * 128 + (((ch & 7) ^ (r & 7)) << 4), src,
+                         v ? 16u : 0u);
+      }
+      cp_async_arrive_noinc(q_full);
+    }
+    int64_t row = a.req_pool_indices[b];
+    if (row < 0 || row >= a.r2t_rows) {
+      if (tid == kPrWarp0 * 32 && rank == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+      row = 0;
+    }
+    const int64_t* r2t = a.req_to_token + row * a.r2t_stride;
+    const char* kbuf = (const char*)a.k_buffer + (int64_t)h * a.kv_stride_head * 2;
+    const char* vbuf = (const char*)a.v_buffer + (int64_t)h * a.kv_stride_head * 2 + rank * D;
+    const int64_t sstride = a.kv_stride_slot * 2;
+    // lanes 0-15: V keys 16 pw + lane; lanes 16-23: K keys 32 rank + 8 pw + (lane - 16)
+    const int my_key = lane < 16 ? 16 * pw + lane : (lane < 24 ? 32 * (int)rank + 8 * pw + lane - 16 : 0);
+    auto raw_of = [&](int tile) -> int64_t {
+      int64_t key = (int64_t)tile * kBN + my_key;
+      if (key >= kv_end) key = (int64_t)tile * kBN;  // past the window: repeat the tile's first key
+      return r2t[key];
+    };
+    constexpr int kPrefetch = 4;
+    int64_t raw_q[kPrefetch];
+#pragma unroll
+    for (int i = 0; i < kPrefetch; ++i) raw_q[i] = (lane < 24 && i < ntiles) ? raw_of(i) : 0;
+    int slot = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    auto produce = [&](int tile, bool isv) {
+      ok = __all_sync(0xffffffffu, wait_c(&empty[slot], phase ^ 1u, abort, peer_abort));
+      if (!ok) return;
+      int64_t* ids = ids_all + ((tile & 1) * kProducerWarps + pw) * 24;
+      if (!isv) {  // resolve this tile's slot ids (used by K now and by V later)
+        const int64_t raw = raw_q[0];
+#pragma unroll
+        for (int i = 0; i + 1 < kPrefetch; ++i) raw_q[i] = raw_q[i + 1];
+        raw_q[kPrefetch - 1] = (tile + kPrefetch < ntiles && lane < 24) ? raw_of(tile + kPrefetch) : 0;
+        if (lane < 24) ids[lane] = resolve_slot(raw, a.num_slots, a.slot_mode, a.err);
+        __syncwarp();
+      }
+      const uint32_t sb = base + C::kOffRing + slot * C::kSlotBytes;
+      if (!isv) {  // 8 key rows of D dims
+        constexpr int CPR = D / 8, RPI = 32 / CPR;
+        const int sub = lane / CPR, ch = lane - (lane / CPR) * CPR;
+#pragma unroll
+        for (int i = 0; i < 8; i += RPI) {
+          const int kr = 8 * pw + i + sub;  // row in this CTA's K half
+          const int64_t sl = ids[16 + i + sub];
+          cp_async16(sb + (ch >> 3) * C::kKBlk + kr * 128 + (((ch & 7) ^ (kr & 7)) << 4),
+                     kbuf + sl * sstride + ch * 16);
+        }
+      } else {  // 16 key rows of this CTA's D/2 dims
+        constexpr int CPR = D / 16, RPI = 32 / CPR;
+        const int sub = lane / CPR, ch = lane - (lane / CPR) * CPR;
+#pragma unroll
+        for (int i = 0; i < 16; i += RPI) {
+          const int vr = 16 * pw + i + sub;  // key row of the tile
+          const int64_t sl = ids[i + sub];
+          cp_async16(sb + (ch >> 3) * C::kVBlk + vr * 128 + (((ch & 7) ^ (vr & 7)) << 4),
+                     vbuf + sl * sstride + ch * 16);
+        }
+      }
+      cp_async_arrive_noinc(&full[slot]);
+      if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
+    };
+    produce(0, false);
+    if (ok && ntiles > 1) produce(1, false);
+    for (int j = 0; ok && j < ntiles; ++j) {
+      produce(j, true);
+      if (ok && j + 2 < ntiles) produce(j + 2, false);
+    }
+    cp_async_wait_all();
+  } else if (warp == kIssueWarp && rank == 1) {
+    // ======================= relay: this CTA's halves landed -> rank 0 =======================
+    if (lane == 0) {
+      bool ok = wait_c(q_full, 0, abort, peer_abort);
+      if (ok) {
+        tc::fence_proxy_async_smem();
+        remote_arrive(peer_addr(smem_u32(q_full), 0));
+      }
+      int slot = 0;
+      uint32_t phase = 0;
+      for (int it = 0; ok && it < 2 * ntiles; ++it) {
+        ok = wait_c(&full[slot], phase, abort, peer_abort);
+        if (!ok) break;
+        tc::fence_proxy_async_smem();
+        remote_arrive(peer_addr(smem_u32(&full[slot]), 0));
+        if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
+      }
+      wait_c(fin, 0, abort, peer_abort);  // rank 0's MMAs done with this CTA's TMEM and smem
+    }
+    __syncwarp();
+  } else if (warp == kIssueWarp) {
+    // ======================= MMA issue for the pair (rank 0, one thread) =======================
+    if (lane == 0) {
+      constexpr uint32_t kIdS = tc::idesc_bf16(2 * kRows, kBN, false, false);
+      constexpr uint32_t kIdO = tc::idesc_bf16(2 * kRows, D, false, true);
+      bool ok = wait_c(q_full, 0, abort, peer_abort);
+      tc::fence_proxy_async_smem();
+      int slot = 0;
+      uint32_t phase = 0;
+      auto take = [&]() -> uint32_t {
+        ok = ok && wait_c(&full[slot], phase, abort, peer_abort);
+        tc::fence_proxy_async_smem();
+        return base + C::kOffRing + slot * C::kSlotBytes;
+      };
+      auto release = [&]() {
+        commit_both(&empty[slot]);
+        if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
+      };
+      auto issue_s = [&](int t) {
+        const uint32_t kb = take();
+        if (!ok) return;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = tc::sw128_desc(base + (kk >> 2) * C::kQBlock + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sw128_desc(kb + (kk >> 2) * C::kKBlk + (kk & 3) * 32, 16, 1024);
+          mma2_ss(tmem + C::kColS + (t & 1) * kBN, ad, bd, kIdS, kk > 0);
+        }
+        commit_both(&s_full[t & 1]);
+        release();
+      };
+      auto issue_pv = [&](int t) {
+        ok = ok && wait_c(&p_full[t & 1], (t >> 1) & 1, abort, peer_abort);
+        tc::fence_after_sync();
+        const uint32_t vb = take();
+        if (!ok) return;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = tc::sw128_desc(vb + kk * 2048, C::kVBlk, 1024);
+          mma2_ts(tmem + C::kColO, tmem + C::kColP + (t & 1) * (kBN / 2) + kk * 8, bd, kIdO,
+                  t > 0 || kk > 0);
+        }
+        commit_both(o_done);
+        release();
+      };
+      if (ok) issue_s(0);
+      if (ok && ntiles > 1) issue_s(1);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        issue_pv(j);
+        if (ok && j + 2 < ntiles) issue_s(j + 2);
+      }
+      commit_both(fin);  // completes once every MMA issued above has completed
+      wait_c(fin, 0, abort, peer_abort);
+    }
+    __syncwarp();
+  } else {
+    // ============ softmax + epilogue: thread (half, r) = key columns [32 half, +32) of row r ============
+    const float c2 = a.scale * kLog2e;
+    const int r = tid & (kRows - 1);
+    const int half = tid >> 7;
+    const int ri = r / G, rg = r - (r / G) * G;
+    const bool row_valid = ri < n_tok;
+    const int64_t klim = P + cta_start + ri + 1;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t pf0 = peer_addr(smem_u32(&p_full[0]), 0), pf1 = peer_addr(smem_u32(&p_full[1]), 0);
+    constexpr int kOHalf = D / 2;  // O columns rescaled and stored by this thread
+    float m_used = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int bi = j & 1;
+      ok = __all_sync(0xffffffffu, wait_c(&s_full[bi], (j >> 1) & 1, abort, peer_abort));
+      if (!ok) break;
+      tc::fence_after_sync();
+      // both warps of a row group read all 64 scores and take the same max, so they agree on the
+      // running max and on every rescale without exchanging anything
+      float s[2][32];
+      tc::ld32(tmem + lane_base + C::kColS + bi * kBN, s[0]);
+      tc::ld32(tmem + lane_base + C::kColS + bi * kBN + 32, s[1]);
+      tc::wait_ld();
+      const int64_t key0 = (int64_t)j * kBN;
+      if (!(row_valid && key0 + kBN <= klim)) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (!(row_valid && key0 + hh * 32 + k < klim)) s[hh][k] = -INFINITY;
+      }
+      const float tmax = max_of_64(s) * c2;
+      const bool need = tmax > m_used + kRescaleLog2 || (m_used == -INFINITY && tmax > -INFINITY);
+      const float m_new = need ? tmax : m_used;
+      const float alpha = need ? (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new)) : 1.f;
+      m_used = m_new;
+      l_sum *= alpha;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {  // rescale this thread's half of its O row
+        ok = __all_sync(0xffffffffu, wait_c(o_done, (j - 1) & 1, abort, peer_abort));
+        if (!ok) break;
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int cc = 0; cc < kOHalf / 32; ++cc) {
+          const uint32_t ta = tmem + lane_base + C::kColO + half * kOHalf + cc * 32;
+          float o[32];
+          tc::ld32(ta, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) o[k] *= alpha;
+          tc::st32(ta, o);
+        }
+      }
+      const float nmu = m_used == -INFINITY ? 0.f : -m_used;
+      float pk[16];
+      l_sum += half ? exp_pack(s[1], c2, nmu, pk) : exp_pack(s[0], c2, nmu, pk);
+      tc::st16(tmem + lane_base + C::kColP + bi * (kBN / 2) + half * (kBN / 4), pk);
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) remote_arrive(bi ? pf1 : pf0);  // rank 0's p_full (own CTA when rank 0)
+    }
+    if (ok) ok = __all_sync(0xffffffffu, wait_c(fin, 0, abort, peer_abort));
+    // the two halves' row sums meet in shared memory (the Q tile is dead once fin completed);
+    // every softmax thread reaches this barrier, whatever its loop's outcome
+    float* l_part = reinterpret_cast<float*>(sbase);
+    if (ok) l_part[half * kRows + r] = l_sum;
+    named_barrier(1, kSmWarps * 32);
+    const float l_tot = ok ? l_part[r] + l_part[kRows + r] : 0.f;
+    if (ok) {
+      tc::fence_after_sync();
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+      const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
+      const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr;
+      const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(gate)) & 15) == 0 &&
+                       (a.out_stride_tok | a.out_stride_head | a.gate_stride_tok | a.gate_stride_head) % 8 == 0;
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      const int64_t t = q0 + ri;
+      const int hq = h * G + rg;
+#pragma unroll 1
+      for (int cc = 0; cc < kOHalf / 32; ++cc) {
+        const int col = half * kOHalf + cc * 32;
+        float o[32];
+        tc::ld32(tmem + lane_base + C::kColO + col, o);
+        tc::wait_ld();
+        if (!row_valid) continue;
+        __nv_bfloat16* op = out + t * a.out_stride_tok + (int64_t)hq * a.out_stride_head + col;
+        const __nv_bfloat16* gp =
+            gated ? gate + t * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + col : nullptr;
+        if (vec) {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint4 gw = make_uint4(0, 0, 0, 0);
+            if (gated) gw = *reinterpret_cast<const uint4*>(gp + c8 * 8);
+            const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&gw);
+            uint4 ow;
+            __nv_bfloat16* ov = reinterpret_cast<__nv_bfloat16*>(&ow);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              float v = round_to<__nv_bfloat16>(l_tot > 0.f ? o[c8 * 8 + k] * inv : NAN);
+              if (gated) v = apply_gate<__nv_bfloat16>(v, to_f(gv[k]), a.gate_mode);
+              ov[k] = __float2bfloat16_rn(v);
+            }
+            *reinterpret_cast<uint4*>(op + c8 * 8) = ow;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            float v = round_to<__nv_bfloat16>(l_tot > 0.f ? o[k] * inv : NAN);
+            if (gated) v = apply_gate<__nv_bfloat16>(v, to_f(gp[k]), a.gate_mode);
+            op[k] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  // rank 0's MMAs read this CTA's shared memory and TMEM, and remote arrivals target rank 0's
+  // barriers: neither CTA releases TMEM or exits before both are done
+  cluster_sync();
+  if (tid == 0 && *abort) record_err(a.err, TF_KERR_TIMEOUT);
+  tc::fence_after_sync();
+  if (warp == kIssueWarp)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols)
+                 : "memory");
+}
+
+template <int D>
+static cudaError_t launch_pair(const tf_paged_attn_args& a, cudaStream_t s) {
+  const int G = a.num_q_heads / a.num_kv_heads;
+  const int TQ = kRows / G;
+  const int pairs = (a.max_extend_len + 2 * TQ - 1) / (2 * TQ);
+  cudaError_t e = cudaFuncSetAttribute(extend_pair_kernel<D>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)(2 * a.batch_size * pairs), (unsigned)a.num_kv_heads);
+  extend_pair_kernel<D><<<grid, kPairThreads, Cfg<D>::kSmem, s>>>(a, pairs);
+  return cudaGetLastError();
+}
+
+}  // namespace pair
 }  // namespace ext
 
 bool paged_extend_tc_supported(const tf_paged_attn_args& a) {
@@ -427,6 +966,7 @@ bool paged_extend_tc_supported(const tf_paged_attn_args& a) {
   const int G = a.num_q_heads / a.num_kv_heads;
   if (G < 1 || G > 16 || ext::kRows % G != 0) return false;
   if (a.max_extend_len <= 0) return false;
+  if (!(a.scale > 0.f)) return false;  // the softmax takes its max on unscaled scores
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al(a.q) || !al(a.k_buffer) || !al(a.v_buffer)) return false;
   if (a.q_stride_tok % 8 || a.q_stride_head % 8 || a.kv_stride_slot % 8 || a.kv_stride_head % 8)
@@ -438,8 +978,8 @@ cudaError_t launch_paged_extend_tc(const tf_paged_attn_args& a, cudaStream_t s) 
   if (a.batch_size == 0 || a.num_tokens == 0) return cudaSuccess;
   switch (a.head_dim) {
     case 64: return ext::launch_d<64>(a, s);
-    case 128: return ext::launch_d<128>(a, s);
-    default: return ext::launch_d<256>(a, s);
+    case 128: return ext::pair::launch_pair<128>(a, s);
+    default: return ext::pair::launch_pair<256>(a, s);
   }
 }
 
