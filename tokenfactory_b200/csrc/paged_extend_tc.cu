@@ -509,6 +509,27 @@ __device__ __forceinline__ bool wait_c(uint64_t* bar, uint32_t parity, volatile 
     }
   }
 }
+// Same with the default (CTA-scope) acquire, for the many threads that poll barriers completed by
+// tcgen05.commit or by this CTA's own cp.async: what they read next is TMEM or this CTA's shared
+// memory behind tcgen05 / proxy fences, so no cluster-scope acquire is needed on their hot path.
+__device__ __forceinline__ bool wait_l(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                       uint32_t peer_abort, unsigned backoff_ns = 0) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (backoff_ns) __nanosleep(backoff_ns);
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kSpinLimitNs) {
+        *abort = 1;
+        remote_store(peer_abort, 1);
+        return false;
+      }
+    }
+  }
+}
 __device__ __forceinline__ void mma2_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -533,8 +554,23 @@ __device__ __forceinline__ void commit_both(uint64_t* bar) {
 
 constexpr int kSmWarps = 8;                    // two warps per 32-row group: key columns 0-31 / 32-63
 constexpr int kPrWarp0 = kSmWarps;             // producers: warps 8-11
-constexpr int kIssueWarp = kSmWarps + kProducerWarps;  // MMA issue (rank 0) / relay (rank 1)
-constexpr int kPairThreads = (kIssueWarp + 1) * 32;
+constexpr int kIssueWarp = kSmWarps + kProducerWarps;  // MMA issue (rank 0) / slot relay (rank 1)
+constexpr int kFwdWarp = kIssueWarp + 1;               // rank 1: forwards "P written" to rank 0
+constexpr int kPairThreads = (kFwdWarp + 1) * 32;
+
+// Output-gate activation for the epilogue: sigmoid as a hardware reciprocal of 1 + e^-x (within a
+// few fp32 ulp of the IEEE quotient, far below the bf16 rounding that follows); silu = x sigmoid(x).
+__device__ __forceinline__ float act_fast(float x, int mode) {
+  float sg;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(sg) : "f"(1.0f + __expf(-x)));
+  return mode == TF_GATE_SILU ? x * sg : sg;
+}
+
+// gate and output rows can be moved in 16-byte pieces
+__device__ __forceinline__ bool gate_vec(const tf_paged_attn_args& a) {
+  return ((reinterpret_cast<uintptr_t>(a.out) | reinterpret_cast<uintptr_t>(a.gate)) & 15) == 0 &&
+         (a.out_stride_tok | a.out_stride_head | a.gate_stride_tok | a.gate_stride_head) % 8 == 0;
+}
 
 // p = 2^(s c2 - m) for 32 scores, packed as 16 bf16 pairs; returns the sum of the fp32 p
 __device__ __forceinline__ float exp_pack(const float (&sh)[32], float c2, float nmu, float (&pk)[16]) {
@@ -561,7 +597,7 @@ struct Cfg {
   static constexpr int kSlots = D == 256 ? 10 : 16;
   static constexpr int kOffRing = kQBytes;
   static constexpr int kOffBars = kOffRing + kSlots * kSlotBytes;
-  static constexpr int kNumBars = 2 * kSlots + 7;   // full, empty, s_full[2], p_full[2], o_done, q_full, fin
+  static constexpr int kNumBars = 2 * kSlots + 8;   // full, empty, s_full[2], p_full[2], o_done, q_full, fin, q_dead
   static constexpr int kOffWords = kOffBars + 8 * kNumBars;
   static constexpr int kOffIds = kOffWords + 16;    // int64 [2][kProducerWarps][24]
   static constexpr int kSmem = kOffIds + 2 * kProducerWarps * 24 * 8 + 1024;
@@ -591,6 +627,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   uint64_t* o_done = p_full + 2;
   uint64_t* q_full = o_done + 1;
   uint64_t* fin = q_full + 1;
+  uint64_t* q_dead = fin + 1;  // the last S MMA has completed: Q's shared memory is free
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sbase + C::kOffWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sbase + C::kOffWords + 4);
   int64_t* s_q0 = reinterpret_cast<int64_t*>(sbase + C::kOffWords + 8);
@@ -636,11 +673,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2 * kSmWarps);
+      mbar_init(&p_full[i], rank == 0 ? kSmWarps + 1 : kSmWarps);
     }
     mbar_init(o_done, 1);
     mbar_init(q_full, in_count);
     mbar_init(fin, 1);
+    mbar_init(q_dead, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -699,7 +737,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     auto produce = [&](int tile, bool isv) {
-      ok = __all_sync(0xffffffffu, wait_c(&empty[slot], phase ^ 1u, abort, peer_abort));
+      // producers run far ahead of the MMAs: poll the slot gently to leave issue slots to softmax
+      ok = __all_sync(0xffffffffu, wait_l(&empty[slot], phase ^ 1u, abort, peer_abort, 128));
       if (!ok) return;
       int64_t* ids = ids_all + ((tile & 1) * kProducerWarps + pw) * 24;
       if (!isv) {  // resolve this tile's slot ids (used by K now and by V later)
@@ -741,11 +780,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       produce(j, true);
       if (ok && j + 2 < ntiles) produce(j + 2, false);
     }
+    // Output gate, off the softmax's critical path: once the last S MMA has completed (q_dead), the
+    // Q region is free; each producer warp copies 32 gate rows of this CTA into it (whole rows,
+    // coalesced) while the last tiles still run.  Every producer thread reaches the closing barrier.
+    const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
+    const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr && gate_vec(a);
+    constexpr int kChunks = D / 8, kRowsPerInstr = 32 / kChunks;
+    const int gsub = lane / kChunks, gch = lane - (lane / kChunks) * kChunks;
+    bool okg = ok && wait_l(q_dead, 0, abort, peer_abort);
+    okg = __all_sync(0xffffffffu, okg);
+    if (okg && gated) {
+#pragma unroll 1
+      for (int i = 0; i < 32; i += kRowsPerInstr) {
+        const int row = pw * 32 + i + gsub;
+        const int ti = row / G, g = row - (row / G) * G;
+        if (ti < n_tok)
+          cp_async16(base + row * (D * 2) + gch * 16,
+                     gate + (q0 + ti) * a.gate_stride_tok + (int64_t)(h * G + g) * a.gate_stride_head + gch * 8);
+      }
+    }
     cp_async_wait_all();
+    named_barrier(2, (kSmWarps + kProducerWarps) * 32);  // gate rows staged for the softmax warps
   } else if (warp == kIssueWarp && rank == 1) {
     // ======================= relay: this CTA's halves landed -> rank 0 =======================
     if (lane == 0) {
-      bool ok = wait_c(q_full, 0, abort, peer_abort);
+      bool ok = wait_l(q_full, 0, abort, peer_abort);
       if (ok) {
         tc::fence_proxy_async_smem();
         remote_arrive(peer_addr(smem_u32(q_full), 0));
@@ -753,13 +812,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       int slot = 0;
       uint32_t phase = 0;
       for (int it = 0; ok && it < 2 * ntiles; ++it) {
-        ok = wait_c(&full[slot], phase, abort, peer_abort);
+        ok = wait_l(&full[slot], phase, abort, peer_abort);
         if (!ok) break;
         tc::fence_proxy_async_smem();
         remote_arrive(peer_addr(smem_u32(&full[slot]), 0));
         if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
       }
-      wait_c(fin, 0, abort, peer_abort);  // rank 0's MMAs done with this CTA's TMEM and smem
+      wait_l(fin, 0, abort, peer_abort);  // rank 0's MMAs done with this CTA's TMEM and smem
+    }
+    __syncwarp();
+  } else if (warp == kFwdWarp) {
+    // =========== rank 1: "this CTA's P_j is in TMEM" -> rank 0's p_full, one arrive per tile ===========
+    if (rank == 1 && lane == 0) {
+      const uint32_t pf0 = peer_addr(smem_u32(&p_full[0]), 0), pf1 = peer_addr(smem_u32(&p_full[1]), 0);
+      for (int j = 0; j < ntiles; ++j) {
+        if (!wait_l(&p_full[j & 1], (j >> 1) & 1, abort, peer_abort)) break;
+        tc::fence_after_sync();
+        tc::fence_before_sync();
+        remote_arrive((j & 1) ? pf1 : pf0);
+      }
     }
     __syncwarp();
   } else if (warp == kIssueWarp) {
@@ -790,6 +861,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           mma2_ss(tmem + C::kColS + (t & 1) * kBN, ad, bd, kIdS, kk > 0);
         }
         commit_both(&s_full[t & 1]);
+        if (t == ntiles - 1) commit_both(q_dead);
         release();
       };
       auto issue_pv = [&](int t) {
@@ -812,26 +884,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         issue_pv(j);
         if (ok && j + 2 < ntiles) issue_s(j + 2);
       }
+      if (!ok) commit_both(q_dead);  // aborted before the last S: release the waiters anyway
       commit_both(fin);  // completes once every MMA issued above has completed
       wait_c(fin, 0, abort, peer_abort);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kSmWarps) {
     // ============ softmax + epilogue: thread (half, r) = key columns [32 half, +32) of row r ============
     const float c2 = a.scale * kLog2e;
     const int r = tid & (kRows - 1);
     const int half = tid >> 7;
-    const int ri = r / G, rg = r - (r / G) * G;
+    const int ri = r / G;
     const bool row_valid = ri < n_tok;
     const int64_t klim = P + cta_start + ri + 1;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t pf0 = peer_addr(smem_u32(&p_full[0]), 0), pf1 = peer_addr(smem_u32(&p_full[1]), 0);
     constexpr int kOHalf = D / 2;  // O columns rescaled and stored by this thread
     float m_used = -INFINITY, l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int bi = j & 1;
-      ok = __all_sync(0xffffffffu, wait_c(&s_full[bi], (j >> 1) & 1, abort, peer_abort));
+      ok = __all_sync(0xffffffffu, wait_l(&s_full[bi], (j >> 1) & 1, abort, peer_abort));
       if (!ok) break;
       tc::fence_after_sync();
       // both warps of a row group read all 64 scores and take the same max, so they agree on the
@@ -840,13 +912,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       tc::ld32(tmem + lane_base + C::kColS + bi * kBN, s[0]);
       tc::ld32(tmem + lane_base + C::kColS + bi * kBN + 32, s[1]);
       tc::wait_ld();
-      const int64_t key0 = (int64_t)j * kBN;
-      if (!(row_valid && key0 + kBN <= klim)) {
+      // keys [0, vis) of this tile are visible to the row (0 for rows past the request end)
+      const int64_t rem = row_valid ? klim - (int64_t)j * kBN : 0;
+      const int vis = rem <= 0 ? 0 : (rem >= kBN ? kBN : (int)rem);
+      if (vis < kBN) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
           for (int k = 0; k < 32; ++k)
-            if (!(row_valid && key0 + hh * 32 + k < klim)) s[hh][k] = -INFINITY;
+            if (hh * 32 + k >= vis) s[hh][k] = -INFINITY;
       }
       const float tmax = max_of_64(s) * c2;
       const bool need = tmax > m_used + kRescaleLog2 || (m_used == -INFINITY && tmax > -INFINITY);
@@ -855,7 +929,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       m_used = m_new;
       l_sum *= alpha;
       if (j > 0 && __any_sync(0xffffffffu, need)) {  // rescale this thread's half of its O row
-        ok = __all_sync(0xffffffffu, wait_c(o_done, (j - 1) & 1, abort, peer_abort));
+        ok = __all_sync(0xffffffffu, wait_l(o_done, (j - 1) & 1, abort, peer_abort));
         if (!ok) break;
         tc::fence_after_sync();
 #pragma unroll 1
@@ -876,58 +950,104 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       tc::wait_st();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) remote_arrive(bi ? pf1 : pf0);  // rank 0's p_full (own CTA when rank 0)
+      if (lane == 0) mbar_arrive(&p_full[bi]);  // rank 1's warp 13 forwards it to rank 0
     }
-    if (ok) ok = __all_sync(0xffffffffu, wait_c(fin, 0, abort, peer_abort));
-    // the two halves' row sums meet in shared memory (the Q tile is dead once fin completed);
-    // every softmax thread reaches this barrier, whatever its loop's outcome
-    float* l_part = reinterpret_cast<float*>(sbase);
+    constexpr int kChunks = D / 8;                           // 16-byte chunks of a row
+    constexpr int kRowsPerInstr = 32 / kChunks;              // 1 (D 256) or 2 (D 128)
+    constexpr int kRowsPerWarp = kRows / kSmWarps;           // 16
+    constexpr int kRowIters = kRowsPerWarp / kRowsPerInstr;
+    const int sub = lane / kChunks, ch = lane - (lane / kChunks) * kChunks;
+    const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr;
+    const bool vec = gate_vec(a);
+    const uint32_t gstage = base;  // gate rows, staged in the Q region by the producers
+    if (ok) ok = __all_sync(0xffffffffu, wait_l(fin, 0, abort, peer_abort));
+    // ---- epilogue.  Once fin completed, no MMA reads Q or the ring any more: the two halves' row
+    // sums meet in the Q region, and O (normalised, bf16) is staged row-major in the ring with the
+    // 16-byte chunk index XOR-swizzled by the row, so that warps then walk whole rows: gate loads
+    // and output stores are full coalesced rows.  Every softmax thread reaches both barriers.
+    float* l_part = reinterpret_cast<float*>(sbase + C::kOffRing + kRows * D * 2);  // after the O stage
     if (ok) l_part[half * kRows + r] = l_sum;
     named_barrier(1, kSmWarps * 32);
     const float l_tot = ok ? l_part[r] + l_part[kRows + r] : 0.f;
+    const uint32_t stage = base + C::kOffRing;
     if (ok) {
       tc::fence_after_sync();
-      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-      const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
-      const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr;
-      const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(gate)) & 15) == 0 &&
-                       (a.out_stride_tok | a.out_stride_head | a.gate_stride_tok | a.gate_stride_head) % 8 == 0;
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-      const int64_t t = q0 + ri;
-      const int hq = h * G + rg;
 #pragma unroll 1
       for (int cc = 0; cc < kOHalf / 32; ++cc) {
-        const int col = half * kOHalf + cc * 32;
         float o[32];
-        tc::ld32(tmem + lane_base + C::kColO + col, o);
+        tc::ld32(tmem + lane_base + C::kColO + half * kOHalf + cc * 32, o);
         tc::wait_ld();
-        if (!row_valid) continue;
-        __nv_bfloat16* op = out + t * a.out_stride_tok + (int64_t)hq * a.out_stride_head + col;
-        const __nv_bfloat16* gp =
-            gated ? gate + t * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + col : nullptr;
-        if (vec) {
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            uint4 gw = make_uint4(0, 0, 0, 0);
-            if (gated) gw = *reinterpret_cast<const uint4*>(gp + c8 * 8);
-            const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&gw);
-            uint4 ow;
-            __nv_bfloat16* ov = reinterpret_cast<__nv_bfloat16*>(&ow);
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint32_t w[4];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              float v = round_to<__nv_bfloat16>(l_tot > 0.f ? o[c8 * 8 + k] * inv : NAN);
-              if (gated) v = apply_gate<__nv_bfloat16>(v, to_f(gv[k]), a.gate_mode);
-              ov[k] = __float2bfloat16_rn(v);
-            }
-            *reinterpret_cast<uint4*>(op + c8 * 8) = ow;
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const float x0 = l_tot > 0.f ? o[c8 * 8 + 2 * q2] * inv : NAN;
+            const float x1 = l_tot > 0.f ? o[c8 * 8 + 2 * q2 + 1] * inv : NAN;
+            __nv_bfloat162 pv = __floats2bfloat162_rn(x0, x1);
+            w[q2] = *reinterpret_cast<uint32_t*>(&pv);
           }
-        } else {
+          const int chunk = (half * kOHalf + cc * 32 + c8 * 8) / 8;
+          const uint32_t dst = stage + r * (D * 2) + ((chunk ^ (r & (kChunks - 1))) << 4);
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(w[0]), "r"(w[1]),
+                       "r"(w[2]), "r"(w[3])
+                       : "memory");
+        }
+      }
+    }
+    named_barrier(1, kSmWarps * 32);
+    named_barrier(2, (kSmWarps + kProducerWarps) * 32);  // gate rows are staged
+    // (cold code, run once per CTA: kept compact, since it is fetched after the main loop has
+    // filled the instruction cache)
+    if (ok && vec) {
+#pragma unroll 1
+      for (int i = 0; i < kRowIters; ++i) {
+        const int row = warp * kRowsPerWarp + i * kRowsPerInstr + sub;
+        const int ti = row / G, g = row - (row / G) * G;
+        if (ti >= n_tok) continue;
+        uint4 ov;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(ov.x), "=r"(ov.y), "=r"(ov.z), "=r"(ov.w)
+                     : "r"(stage + row * (D * 2) + ((ch ^ (row & (kChunks - 1))) << 4)));
+        if (gated) {  // out = bf16(attn * bf16(act(gate))): a bf16 x bf16 product is exact in fp32
+          uint32_t gw[4];
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(gw[0]), "=r"(gw[1]), "=r"(gw[2]), "=r"(gw[3])
+                       : "r"(gstage + row * (D * 2) + ch * 16));
+          __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            float v = round_to<__nv_bfloat16>(l_tot > 0.f ? o[k] * inv : NAN);
-            if (gated) v = apply_gate<__nv_bfloat16>(v, to_f(gp[k]), a.gate_mode);
-            op[k] = __float2bfloat16_rn(v);
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(&gw[q2]);
+            const __nv_bfloat162 av = __floats2bfloat162_rn(act_fast(__low2float(gv), a.gate_mode),
+                                                            act_fast(__high2float(gv), a.gate_mode));
+            o2[q2] = __hmul2(o2[q2], av);
           }
+        }
+        *reinterpret_cast<uint4*>(out + (q0 + ti) * a.out_stride_tok +
+                                  (int64_t)(h * G + g) * a.out_stride_head + ch * 8) = ov;
+      }
+    } else if (ok) {  // unaligned gate/output rows: element by element
+#pragma unroll 1
+      for (int i = 0; i < kRowIters; ++i) {
+        const int row = warp * kRowsPerWarp + i * kRowsPerInstr + sub;
+        const int ti = row / G, g = row - (row / G) * G;
+        if (ti >= n_tok) continue;
+        const int64_t t = q0 + ti;
+        const int hq = h * G + g;
+        const uint32_t src = stage + row * (D * 2) + ((ch ^ (row & (kChunks - 1))) << 4);
+#pragma unroll 1
+        for (int k = 0; k < 8; ++k) {
+          unsigned short bits;
+          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(src + 2 * k));
+          float v = __bfloat162float(__ushort_as_bfloat16(bits));
+          if (gated)
+            v = apply_gate<__nv_bfloat16>(
+                v, to_f(gate[t * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + ch * 8 + k]),
+                a.gate_mode);
+          out[t * a.out_stride_tok + (int64_t)hq * a.out_stride_head + ch * 8 + k] = __float2bfloat16_rn(v);
         }
       }
     }
