@@ -552,6 +552,7 @@ __device__ __forceinline__ void commit_both(uint64_t* bar) {
       : "memory");
 }
 
+constexpr int kPBN = 128;                       // keys per tile: S = Q.K^T is M256 x N128
 constexpr int kSmWarps = 8;                    // two warps per 32-row group: key columns 0-31 / 32-63
 constexpr int kPrWarp0 = kSmWarps;             // producers: warps 8-11
 constexpr int kIssueWarp = kSmWarps + kProducerWarps;  // MMA issue (rank 0) / slot relay (rank 1)
@@ -591,24 +592,25 @@ struct Cfg {
   static constexpr int kKB = D / 64;
   static constexpr int kQBlock = kRows * 128;       // one 64-dim block of this CTA's Q rows
   static constexpr int kQBytes = kKB * kQBlock;
-  static constexpr int kKBlk = (kBN / 2) * 128;     // K half: 32 keys x 128 B per 64-dim block
-  static constexpr int kVBlk = kBN * 128;           // V half: 64 keys x 128 B per 64-dim block
+  static constexpr int kKBlk = (kPBN / 2) * 128;    // K half: 64 keys x 128 B per 64-dim block
+  static constexpr int kVBlk = kPBN * 128;          // V half: 128 keys x 128 B per 64-dim block
   static constexpr int kSlotBytes = kKB * kKBlk;    // == (kKB / 2) * kVBlk
-  static constexpr int kSlots = D == 256 ? 10 : 16;
+  static constexpr int kSlots = D == 256 ? 4 : 8;
   static constexpr int kOffRing = kQBytes;
   static constexpr int kOffBars = kOffRing + kSlots * kSlotBytes;
   static constexpr int kNumBars = 2 * kSlots + 8;   // full, empty, s_full[2], p_full[2], o_done, q_full, fin, q_dead
   static constexpr int kOffWords = kOffBars + 8 * kNumBars;
-  static constexpr int kOffIds = kOffWords + 16;    // int64 [2][kProducerWarps][24]
-  static constexpr int kSmem = kOffIds + 2 * kProducerWarps * 24 * 8 + 1024;
-  static constexpr int kColS = 0;
-  static constexpr int kColO = 2 * kBN;
-  static constexpr int kColP = kColO + D;
+  static constexpr int kOffIds = kOffWords + 16;    // int64 [2][kProducerWarps][32]
+  static constexpr int kOffPmax = kOffIds + 2 * kProducerWarps * 32 * 8;  // float [2][2][kRows]
+  static constexpr int kSmem = kOffPmax + 2 * 2 * kRows * 4 + 1024;
+  static constexpr int kColS = 0;                   // two S buffers of kPBN columns; P_j over S_j
+  static constexpr int kColO = 2 * kPBN;
   static constexpr int kTmemCols = 512;
   static_assert(D == 128 || D == 256, "pair kernel head dims");
   static_assert(kSlotBytes == (kKB / 2) * kVBlk, "K and V halves share the slot size");
   static_assert(kSmem <= 232448, "shared memory per CTA");
-  static_assert(kColP + kBN <= kTmemCols, "TMEM columns");
+  static_assert(kColO + D <= kTmemCols, "TMEM columns");
+  static_assert(kRows * D * 2 + 2 * kRows * 4 <= kSlots * kSlotBytes, "epilogue stage fits the ring");
 };
 
 template <int D>
@@ -632,6 +634,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(sbase + C::kOffWords + 4);
   int64_t* s_q0 = reinterpret_cast<int64_t*>(sbase + C::kOffWords + 8);
   int64_t* ids_all = reinterpret_cast<int64_t*>(sbase + C::kOffIds);
+  float* pmax = reinterpret_cast<float*>(sbase + C::kOffPmax);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
@@ -656,7 +659,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int n_tok = (int)(E - cta_start <= 0 ? 0 : (E - cta_start < TQ ? E - cta_start : TQ));
   const int64_t pair_end = E - pair_start < 2 * TQ ? E : pair_start + 2 * TQ;
   const int64_t kv_end = P + pair_end;  // keys [0, kv_end) are visible to some row of the pair
-  const int ntiles = (int)((kv_end + kBN - 1) / kBN);
+  const int ntiles = (int)((kv_end + kPBN - 1) / kPBN);
 
   if (warp == 0) {
     int64_t acc = 0;
@@ -722,17 +725,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const char* kbuf = (const char*)a.k_buffer + (int64_t)h * a.kv_stride_head * 2;
     const char* vbuf = (const char*)a.v_buffer + (int64_t)h * a.kv_stride_head * 2 + rank * D;
     const int64_t sstride = a.kv_stride_slot * 2;
-    // lanes 0-15: V keys 16 pw + lane; lanes 16-23: K keys 32 rank + 8 pw + (lane - 16)
-    const int my_key = lane < 16 ? 16 * pw + lane : (lane < 24 ? 32 * (int)rank + 8 * pw + lane - 16 : 0);
+    // lane l < 16: key 64 rank + 16 pw + l (this CTA's K rows and V rows); lane l >= 16: key
+    // 64 (1 - rank) + 16 pw + l - 16 (V rows only): a warp's V rows include its K rows
+    const int my_key = lane < 16 ? 64 * (int)rank + 16 * pw + lane : 64 * (1 - (int)rank) + 16 * pw + lane - 16;
     auto raw_of = [&](int tile) -> int64_t {
-      int64_t key = (int64_t)tile * kBN + my_key;
-      if (key >= kv_end) key = (int64_t)tile * kBN;  // past the window: repeat the tile's first key
+      int64_t key = (int64_t)tile * kPBN + my_key;
+      if (key >= kv_end) key = (int64_t)tile * kPBN;  // past the window: repeat the tile's first key
       return r2t[key];
     };
     constexpr int kPrefetch = 4;
     int64_t raw_q[kPrefetch];
 #pragma unroll
-    for (int i = 0; i < kPrefetch; ++i) raw_q[i] = (lane < 24 && i < ntiles) ? raw_of(i) : 0;
+    for (int i = 0; i < kPrefetch; ++i) raw_q[i] = i < ntiles ? raw_of(i) : 0;
     int slot = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -740,33 +744,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       // producers run far ahead of the MMAs: poll the slot gently to leave issue slots to softmax
       ok = __all_sync(0xffffffffu, wait_l(&empty[slot], phase ^ 1u, abort, peer_abort, 128));
       if (!ok) return;
-      int64_t* ids = ids_all + ((tile & 1) * kProducerWarps + pw) * 24;
+      int64_t* ids = ids_all + ((tile & 1) * kProducerWarps + pw) * 32;
       if (!isv) {  // resolve this tile's slot ids (used by K now and by V later)
         const int64_t raw = raw_q[0];
 #pragma unroll
         for (int i = 0; i + 1 < kPrefetch; ++i) raw_q[i] = raw_q[i + 1];
-        raw_q[kPrefetch - 1] = (tile + kPrefetch < ntiles && lane < 24) ? raw_of(tile + kPrefetch) : 0;
-        if (lane < 24) ids[lane] = resolve_slot(raw, a.num_slots, a.slot_mode, a.err);
+        raw_q[kPrefetch - 1] = tile + kPrefetch < ntiles ? raw_of(tile + kPrefetch) : 0;
+        ids[lane] = resolve_slot(raw, a.num_slots, a.slot_mode, a.err);
         __syncwarp();
       }
       const uint32_t sb = base + C::kOffRing + slot * C::kSlotBytes;
-      if (!isv) {  // 8 key rows of D dims
+      if (!isv) {  // 16 key rows of D dims
         constexpr int CPR = D / 8, RPI = 32 / CPR;
         const int sub = lane / CPR, ch = lane - (lane / CPR) * CPR;
 #pragma unroll
-        for (int i = 0; i < 8; i += RPI) {
-          const int kr = 8 * pw + i + sub;  // row in this CTA's K half
-          const int64_t sl = ids[16 + i + sub];
+        for (int i = 0; i < 16; i += RPI) {
+          const int kr = 16 * pw + i + sub;  // row in this CTA's K half
+          const int64_t sl = ids[i + sub];
           cp_async16(sb + (ch >> 3) * C::kKBlk + kr * 128 + (((ch & 7) ^ (kr & 7)) << 4),
                      kbuf + sl * sstride + ch * 16);
         }
-      } else {  // 16 key rows of this CTA's D/2 dims
+      } else {  // 32 key rows of this CTA's D/2 dims
         constexpr int CPR = D / 16, RPI = 32 / CPR;
         const int sub = lane / CPR, ch = lane - (lane / CPR) * CPR;
 #pragma unroll
-        for (int i = 0; i < 16; i += RPI) {
-          const int vr = 16 * pw + i + sub;  // key row of the tile
-          const int64_t sl = ids[i + sub];
+        for (int i = 0; i < 32; i += RPI) {
+          const int idx = i + sub;
+          const int vr = idx < 16 ? 64 * (int)rank + 16 * pw + idx : 64 * (1 - (int)rank) + 16 * pw + idx - 16;
+          const int64_t sl = ids[idx];
           cp_async16(sb + (ch >> 3) * C::kVBlk + vr * 128 + (((ch & 7) ^ (vr & 7)) << 4),
                      vbuf + sl * sstride + ch * 16);
         }
@@ -800,7 +805,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       }
     }
     cp_async_wait_all();
-    named_barrier(2, (kSmWarps + kProducerWarps) * 32);  // gate rows staged for the softmax warps
+    named_barrier(6, (kSmWarps + kProducerWarps) * 32);  // gate rows staged for the softmax warps
   } else if (warp == kIssueWarp && rank == 1) {
     // ======================= relay: this CTA's halves landed -> rank 0 =======================
     if (lane == 0) {
@@ -836,7 +841,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   } else if (warp == kIssueWarp) {
     // ======================= MMA issue for the pair (rank 0, one thread) =======================
     if (lane == 0) {
-      constexpr uint32_t kIdS = tc::idesc_bf16(2 * kRows, kBN, false, false);
+      constexpr uint32_t kIdS = tc::idesc_bf16(2 * kRows, kPBN, false, false);
       constexpr uint32_t kIdO = tc::idesc_bf16(2 * kRows, D, false, true);
       bool ok = wait_c(q_full, 0, abort, peer_abort);
       tc::fence_proxy_async_smem();
@@ -858,7 +863,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t ad = tc::sw128_desc(base + (kk >> 2) * C::kQBlock + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = tc::sw128_desc(kb + (kk >> 2) * C::kKBlk + (kk & 3) * 32, 16, 1024);
-          mma2_ss(tmem + C::kColS + (t & 1) * kBN, ad, bd, kIdS, kk > 0);
+          mma2_ss(tmem + C::kColS + (t & 1) * kPBN, ad, bd, kIdS, kk > 0);
         }
         commit_both(&s_full[t & 1]);
         if (t == ntiles - 1) commit_both(q_dead);
@@ -870,10 +875,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const uint32_t vb = take();
         if (!ok) return;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
+        for (int kk = 0; kk < kPBN / 16; ++kk) {
+          // P_j: keys [64 hf, 64 hf + 64) packed in columns [64 hf, 64 hf + 32) of S buffer j & 1
           const uint64_t bd = tc::sw128_desc(vb + kk * 2048, C::kVBlk, 1024);
-          mma2_ts(tmem + C::kColO, tmem + C::kColP + (t & 1) * (kBN / 2) + kk * 8, bd, kIdO,
-                  t > 0 || kk > 0);
+          mma2_ts(tmem + C::kColO, tmem + C::kColS + (t & 1) * kPBN + 64 * (kk >> 2) + (kk & 3) * 8, bd,
+                  kIdO, t > 0 || kk > 0);
         }
         commit_both(o_done);
         release();
@@ -890,7 +896,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     __syncwarp();
   } else if (warp < kSmWarps) {
-    // ============ softmax + epilogue: thread (half, r) = key columns [32 half, +32) of row r ============
+    // ============ softmax + epilogue: thread (half, r) = key columns [64 half, +64) of row r ============
     const float c2 = a.scale * kLog2e;
     const int r = tid & (kRows - 1);
     const int half = tid >> 7;
@@ -901,28 +907,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     constexpr int kOHalf = D / 2;  // O columns rescaled and stored by this thread
     float m_used = -INFINITY, l_sum = 0.f;
     bool ok = true;
+    // No early exit from this loop: the two warps of a row group meet at a barrier every tile, so
+    // a failed wait only turns the remaining iterations into barrier-only ones.
     for (int j = 0; j < ntiles; ++j) {
       const int bi = j & 1;
-      ok = __all_sync(0xffffffffu, wait_l(&s_full[bi], (j >> 1) & 1, abort, peer_abort));
-      if (!ok) break;
-      tc::fence_after_sync();
-      // both warps of a row group read all 64 scores and take the same max, so they agree on the
-      // running max and on every rescale without exchanging anything
+      if (ok) ok = __all_sync(0xffffffffu, wait_l(&s_full[bi], (j >> 1) & 1, abort, peer_abort));
       float s[2][32];
-      tc::ld32(tmem + lane_base + C::kColS + bi * kBN, s[0]);
-      tc::ld32(tmem + lane_base + C::kColS + bi * kBN + 32, s[1]);
-      tc::wait_ld();
-      // keys [0, vis) of this tile are visible to the row (0 for rows past the request end)
-      const int64_t rem = row_valid ? klim - (int64_t)j * kBN : 0;
-      const int vis = rem <= 0 ? 0 : (rem >= kBN ? kBN : (int)rem);
-      if (vis < kBN) {
+      float pm = -INFINITY;
+      if (ok) {
+        tc::fence_after_sync();
+        const uint32_t sa = tmem + lane_base + C::kColS + bi * kPBN + 64 * half;
+        tc::ld32(sa, s[0]);
+        tc::ld32(sa + 32, s[1]);
+        tc::wait_ld();
+        // keys [0, vis) of this thread's 64 are visible to the row (0 for rows past the request end)
+        const int64_t rem = row_valid ? klim - (int64_t)j * kPBN - 64 * half : 0;
+        const int vis = rem <= 0 ? 0 : (rem >= 64 ? 64 : (int)rem);
+        if (vis < 64) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
+          for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            if (hh * 32 + k >= vis) s[hh][k] = -INFINITY;
+            for (int k = 0; k < 32; ++k)
+              if (hh * 32 + k >= vis) s[hh][k] = -INFINITY;
+        }
+        pm = max_of_64(s);
       }
-      const float tmax = max_of_64(s) * c2;
+      // the row max over both halves (raw scores; c2 > 0)
+      pmax[(bi * 2 + half) * kRows + r] = pm;
+      named_barrier(1 + (warp & 3), 64);
+      const float pm_other = pmax[(bi * 2 + (half ^ 1)) * kRows + r];
+      if (!ok) continue;
+      const float tmax = fmaxf(pm, pm_other) * c2;
       const bool need = tmax > m_used + kRescaleLog2 || (m_used == -INFINITY && tmax > -INFINITY);
       const float m_new = need ? tmax : m_used;
       const float alpha = need ? (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new)) : 1.f;
@@ -930,7 +945,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       l_sum *= alpha;
       if (j > 0 && __any_sync(0xffffffffu, need)) {  // rescale this thread's half of its O row
         ok = __all_sync(0xffffffffu, wait_l(o_done, (j - 1) & 1, abort, peer_abort));
-        if (!ok) break;
+        if (!ok) continue;
         tc::fence_after_sync();
 #pragma unroll 1
         for (int cc = 0; cc < kOHalf / 32; ++cc) {
@@ -944,9 +959,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
       }
       const float nmu = m_used == -INFINITY ? 0.f : -m_used;
-      float pk[16];
-      l_sum += half ? exp_pack(s[1], c2, nmu, pk) : exp_pack(s[0], c2, nmu, pk);
-      tc::st16(tmem + lane_base + C::kColP + bi * (kBN / 2) + half * (kBN / 4), pk);
+      float pk[32];
+      l_sum += exp_pack(s[0], c2, nmu, *reinterpret_cast<float(*)[16]>(&pk[0])) +
+               exp_pack(s[1], c2, nmu, *reinterpret_cast<float(*)[16]>(&pk[16]));
+      // P over the first 32 of this thread's 64 S columns: only this thread read them
+      tc::st32(tmem + lane_base + C::kColS + bi * kPBN + 64 * half, pk);
       tc::wait_st();
       tc::fence_before_sync();
       __syncwarp();
@@ -969,7 +986,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // and output stores are full coalesced rows.  Every softmax thread reaches both barriers.
     float* l_part = reinterpret_cast<float*>(sbase + C::kOffRing + kRows * D * 2);  // after the O stage
     if (ok) l_part[half * kRows + r] = l_sum;
-    named_barrier(1, kSmWarps * 32);
+    named_barrier(5, kSmWarps * 32);
     const float l_tot = ok ? l_part[r] + l_part[kRows + r] : 0.f;
     const uint32_t stage = base + C::kOffRing;
     if (ok) {
@@ -998,8 +1015,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
       }
     }
-    named_barrier(1, kSmWarps * 32);
-    named_barrier(2, (kSmWarps + kProducerWarps) * 32);  // gate rows are staged
+    named_barrier(5, kSmWarps * 32);
+    named_barrier(6, (kSmWarps + kProducerWarps) * 32);  // gate rows are staged
     // (cold code, run once per CTA: kept compact, since it is fetched after the main loop has
     // filled the instruction cache)
     if (ok && vec) {
