@@ -407,6 +407,377 @@ __global__ void __launch_bounds__(2 * DV) recurrent_extend_kernel(tf_gdn_args a,
   store_state<DK, DV>(S, st);
 }
 
+// ---------------------------------------------------------------------------------------------
+// a7: chunked gated delta rule (qwen3_8/linear_attention.py:194-240), one CTA per (request, v-head)
+// over the request's tokens in chunks of C = 64, everything in fp32 on CUDA cores (the reference is
+// fp32 end to end; the state products keep full fp32 precision).  Per chunk, with gamma the in-chunk
+// cumulative log decay:
+//   Mk = strict_tril(beta_i e^(gamma_i - gamma_j)) o K K^T,  Mq = tril(e^(gamma_i - gamma_j)) o Q K^T
+//   U  = beta (V - e^gamma K S)            then  (I + Mk) U' = U   (forward substitution)
+//   O  = e^gamma Q S + Mq U'
+//   S  = e^gamma_C S + (K o e^(gamma_C - gamma))^T U'
+// The state, the chunk's Q/K/U rows and the two C x C matrices live in shared memory with padded
+// rows (float4 accesses stay conflict-free); the output goes through the fused gated RMSNorm.
+// ---------------------------------------------------------------------------------------------
+template <int D>
+struct ChunkLay {
+  static constexpr int C = 64;
+  static constexpr int kThreads = 256;
+  static constexpr int P = D + 4;        // row pitch of [*, D] tiles, floats
+  static constexpr int MP = C + 4;       // row pitch of the C x C tiles
+  static constexpr int oS = 0;           // state [D][P]
+  static constexpr int oQ = oS + D * P;  // Q rows, then O rows [C][P]
+  static constexpr int oK = oQ + C * P;  // K rows [C][P]
+  static constexpr int oU = oK + C * P;  // V -> rhs -> U' rows [C][P]
+  static constexpr int oMk = oU + C * P; // [C][MP]
+  static constexpr int oMq = oMk + C * MP;
+  static constexpr int oG = oMq + C * MP;  // gamma [C]
+  static constexpr int oB = oG + C;        // beta [C]
+  static constexpr int oEnd = oB + C;
+  static constexpr size_t kBytes = (size_t)oEnd * 4;
+  static constexpr int NCG = D / 4;            // float4 column groups
+  static constexpr int NRG = kThreads / NCG;   // row groups
+  static_assert(kThreads % NCG == 0 && C % NRG == 0 && D % NRG == 0, "chunk tiling");
+};
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void sts4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+  return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc))));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256, 1) chunk_extend_kernel(tf_gdn_args a, const int64_t* start,
+                                                              const T* conv_out) {
+  using Y = ChunkLay<D>;
+  constexpr int C = Y::C, P = Y::P, MP = Y::MP, NCG = Y::NCG, NRG = Y::NRG;
+  const int b = blockIdx.x / a.num_v_heads;
+  const int vh = blockIdx.x - b * a.num_v_heads;
+  const int vpk = a.num_v_heads / a.num_k_heads;
+  const int kh = vh / vpk;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int key_dim = a.num_k_heads * D;
+  const int conv_dim = 2 * key_dim + a.num_v_heads * D;
+
+  extern __shared__ float4 sm4[];
+  float* sm = reinterpret_cast<float*>(sm4);
+  float* Ss = sm + Y::oS;
+  float* Qs = sm + Y::oQ;
+  float* Ks = sm + Y::oK;
+  float* Us = sm + Y::oU;
+  float* Mk = sm + Y::oMk;
+  float* Mq = sm + Y::oMq;
+  float* gam = sm + Y::oG;
+  float* bet = sm + Y::oB;
+
+  const int64_t slot = a.req_pool_indices[b];
+  if (slot < 0 || slot >= a.num_slots) return;  // recorded by the conv kernel
+  const int64_t E = a.extend_lens[b];
+  if (E <= 0) return;
+  const int64_t t0 = start[b];
+  float* st = a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * D * D;
+  for (int e = tid; e < D * NCG; e += Y::kThreads) {
+    const int r = e / NCG, cg = e - (e / NCG) * NCG;
+    sts4(Ss + r * P + 4 * cg, __ldcs(reinterpret_cast<const float4*>(st + (size_t)r * D) + cg));
+  }
+  const float qscale = rsqrtf((float)D);
+  const int rg = tid / NCG, cg = tid - (tid / NCG) * NCG;
+
+  for (int64_t c0 = 0; c0 < E; c0 += C) {
+    const int c = (int)(E - c0 < C ? E - c0 : C);
+    // ---- load the chunk: raw q, k, v rows into shared memory (every load in flight at once),
+    // g and beta of token t by thread t; then each warp normalises whole q / k rows in place
+    {
+      constexpr int EPV = 16 / (int)sizeof(T);        // elements per 16-byte load
+      constexpr int VPR = D / EPV;                     // vectors per row part
+      constexpr int NV = C * 3 * VPR / Y::kThreads;    // vectors per thread
+      static_assert(C * 3 * VPR % Y::kThreads == 0, "load tiling");
+      uint4 raw[NV];
+#pragma unroll
+      for (int n = 0; n < NV; ++n) {  // all loads of the chunk in flight before any use
+        const int e = tid + n * Y::kThreads;
+        const int i = e / (3 * VPR), rem = e - (e / (3 * VPR)) * (3 * VPR);
+        const int part = rem / VPR, vi = rem - (rem / VPR) * VPR;
+        const int col = part == 0 ? kh * D : (part == 1 ? key_dim + kh * D : 2 * key_dim + vh * D);
+        raw[n] = i < c ? *reinterpret_cast<const uint4*>(conv_out + (t0 + c0 + i) * conv_dim + col + vi * EPV)
+                       : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int n = 0; n < NV; ++n) {
+        const int e = tid + n * Y::kThreads;
+        const int i = e / (3 * VPR), rem = e - (e / (3 * VPR)) * (3 * VPR);
+        const int part = rem / VPR, vi = rem - (rem / VPR) * VPR;
+        float* dst = (part == 0 ? Qs : (part == 1 ? Ks : Us)) + i * P + vi * EPV;
+        const T* src = reinterpret_cast<const T*>(&raw[n]);
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) dst[q] = to_f(src[q]);
+      }
+    }
+    if (tid < C) {
+      float g = 0.f, be = 0.f;
+      if (tid < c) gate_values<T>(a, t0 + c0 + tid, vh, &g, &be);
+      gam[tid] = g;
+      bet[tid] = be;
+    }
+    __syncthreads();
+    for (int i = warp; i < c; i += Y::kThreads / 32) {
+      float sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int k = 0; k < D / 32; ++k) {
+        const float qv = Qs[i * P + lane + 32 * k], kv = Ks[i * P + lane + 32 * k];
+        sq = fmaf(qv, qv, sq);
+        sk = fmaf(kv, kv, sk);
+      }
+      sq = warp_sum(sq);
+      sk = warp_sum(sk);
+      const float iq = qscale / fmaxf(sqrtf(sq), 1e-12f), ik = 1.0f / fmaxf(sqrtf(sk), 1e-12f);
+#pragma unroll
+      for (int k = 0; k < D / 32; ++k) {
+        Qs[i * P + lane + 32 * k] *= iq;
+        Ks[i * P + lane + 32 * k] *= ik;
+      }
+    }
+    if (warp == 0) {  // gamma = inclusive cumulative sum of g over the chunk
+      float g0 = gam[2 * lane], g1 = gam[2 * lane + 1];
+      float incl = g0 + g1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const float excl = incl - (g0 + g1);
+      gam[2 * lane] = excl + g0;
+      gam[2 * lane + 1] = incl;
+    }
+    __syncthreads();
+
+    // ---- Mk = strict_tril(beta_i e^(gi-gj)) K K^T,  Mq = tril(e^(gi-gj)) Q K^T
+    {
+      const int ti = tid >> 4, tj = tid & 15;
+      float ak[4][4], aq[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) ak[r][s2] = aq[r][s2] = 0.f;
+#pragma unroll 2
+      for (int d = 0; d < D; d += 4) {
+        float4 kr[4], qr[4], kc[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          kr[r] = lds4(Ks + (ti + 16 * r) * P + d);
+          qr[r] = lds4(Qs + (ti + 16 * r) * P + d);
+          kc[r] = lds4(Ks + (tj + 16 * r) * P + d);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int s2 = 0; s2 < 4; ++s2) {
+            ak[r][s2] = dot4(kr[r], kc[s2], ak[r][s2]);
+            aq[r][s2] = dot4(qr[r], kc[s2], aq[r][s2]);
+          }
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int i = ti + 16 * r;
+        const float gi = gam[i], bi = bet[i];
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) {
+          const int j = tj + 16 * s2;
+          const float dec = j <= i ? expf(gi - gam[j]) : 0.f;
+          Mk[i * MP + j] = j < i ? bi * dec * ak[r][s2] : 0.f;
+          Mq[i * MP + j] = dec * aq[r][s2];
+        }
+      }
+    }
+    // ---- K S and Q S for rows [rg*C/NRG, ...): rhs into U, e^gamma Q S into the Q rows
+    {
+      constexpr int RPT = C / NRG;
+      float4 aks[RPT], aqs[RPT];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) aks[r] = aqs[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int i0 = rg * RPT;
+#pragma unroll 1
+      for (int d = 0; d < D; d += 4) {
+        const float4 s0 = lds4(Ss + (d + 0) * P + 4 * cg), s1 = lds4(Ss + (d + 1) * P + 4 * cg);
+        const float4 s2v = lds4(Ss + (d + 2) * P + 4 * cg), s3 = lds4(Ss + (d + 3) * P + 4 * cg);
+#pragma unroll
+        for (int r = 0; r < RPT; ++r) {
+          const float4 kk = lds4(Ks + (i0 + r) * P + d), qq = lds4(Qs + (i0 + r) * P + d);
+          aks[r].x = fmaf(kk.x, s0.x, fmaf(kk.y, s1.x, fmaf(kk.z, s2v.x, fmaf(kk.w, s3.x, aks[r].x))));
+          aks[r].y = fmaf(kk.x, s0.y, fmaf(kk.y, s1.y, fmaf(kk.z, s2v.y, fmaf(kk.w, s3.y, aks[r].y))));
+          aks[r].z = fmaf(kk.x, s0.z, fmaf(kk.y, s1.z, fmaf(kk.z, s2v.z, fmaf(kk.w, s3.z, aks[r].z))));
+          aks[r].w = fmaf(kk.x, s0.w, fmaf(kk.y, s1.w, fmaf(kk.z, s2v.w, fmaf(kk.w, s3.w, aks[r].w))));
+          aqs[r].x = fmaf(qq.x, s0.x, fmaf(qq.y, s1.x, fmaf(qq.z, s2v.x, fmaf(qq.w, s3.x, aqs[r].x))));
+          aqs[r].y = fmaf(qq.x, s0.y, fmaf(qq.y, s1.y, fmaf(qq.z, s2v.y, fmaf(qq.w, s3.y, aqs[r].y))));
+          aqs[r].z = fmaf(qq.x, s0.z, fmaf(qq.y, s1.z, fmaf(qq.z, s2v.z, fmaf(qq.w, s3.z, aqs[r].z))));
+          aqs[r].w = fmaf(qq.x, s0.w, fmaf(qq.y, s1.w, fmaf(qq.z, s2v.w, fmaf(qq.w, s3.w, aqs[r].w))));
+        }
+      }
+      __syncthreads();  // every thread is done reading Q before its rows are overwritten with O
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        const int i = i0 + r;
+        const float eg = expf(gam[i]), bi = bet[i];
+        float4 u = lds4(Us + i * P + 4 * cg);
+        u.x = bi * (u.x - eg * aks[r].x);
+        u.y = bi * (u.y - eg * aks[r].y);
+        u.z = bi * (u.z - eg * aks[r].z);
+        u.w = bi * (u.w - eg * aks[r].w);
+        sts4(Us + i * P + 4 * cg, u);
+        sts4(Qs + i * P + 4 * cg, make_float4(eg * aqs[r].x, eg * aqs[r].y, eg * aqs[r].z, eg * aqs[r].w));
+      }
+    }
+    __syncthreads();
+    // ---- (I + Mk) U' = U: forward substitution.  Two lanes per column; lane parity p keeps rows
+    // j = 2m + p of its column in registers.  Mk is strictly lower triangular, so both parities
+    // sum over the same compile-time range of m (the entries with j >= i are zero).
+    if (c > 1) {
+      const int col = tid >> 1, par = tid & 1;
+      const bool has_col = col < D;  // D = 64: warps 4-7 only keep the shuffles matched
+      float ur[C / 2];
+#pragma unroll
+      for (int m = 0; m < C / 2; ++m) ur[m] = has_col ? Us[(2 * m + par) * P + col] : 0.f;
+#pragma unroll
+      for (int i = 1; i < C; ++i) {
+        float acc0 = 0.f, acc1 = 0.f;
+        const float* mrow = Mk + i * MP + par;
+#pragma unroll
+        for (int m = 0; m < (i + 1) / 2; ++m) {
+          if (m & 1) acc1 = fmaf(mrow[2 * m], ur[m], acc1);
+          else acc0 = fmaf(mrow[2 * m], ur[m], acc0);
+        }
+        float acc = acc0 + acc1;
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (par == (i & 1)) ur[i >> 1] -= acc;
+      }
+      __syncwarp();
+      if (has_col) {
+#pragma unroll
+        for (int m = 0; m < C / 2; ++m) Us[(2 * m + par) * P + col] = ur[m];
+      }
+    }
+    __syncthreads();
+    // ---- O += Mq U'  and  S = e^gC S + (K o e^(gC - g))^T U'
+    {
+      constexpr int RPT = C / NRG;
+      const int i0 = rg * RPT;
+      float4 ao[RPT];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) ao[r] = lds4(Qs + (i0 + r) * P + 4 * cg);
+#pragma unroll 1
+      for (int j = 0; j < C; j += 4) {
+        const float4 u0 = lds4(Us + (j + 0) * P + 4 * cg), u1 = lds4(Us + (j + 1) * P + 4 * cg);
+        const float4 u2 = lds4(Us + (j + 2) * P + 4 * cg), u3 = lds4(Us + (j + 3) * P + 4 * cg);
+#pragma unroll
+        for (int r = 0; r < RPT; ++r) {
+          const float4 m = lds4(Mq + (i0 + r) * MP + j);
+          ao[r].x = fmaf(m.x, u0.x, fmaf(m.y, u1.x, fmaf(m.z, u2.x, fmaf(m.w, u3.x, ao[r].x))));
+          ao[r].y = fmaf(m.x, u0.y, fmaf(m.y, u1.y, fmaf(m.z, u2.y, fmaf(m.w, u3.y, ao[r].y))));
+          ao[r].z = fmaf(m.x, u0.z, fmaf(m.y, u1.z, fmaf(m.z, u2.z, fmaf(m.w, u3.z, ao[r].z))));
+          ao[r].w = fmaf(m.x, u0.w, fmaf(m.y, u1.w, fmaf(m.z, u2.w, fmaf(m.w, u3.w, ao[r].w))));
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) sts4(Qs + (i0 + r) * P + 4 * cg, ao[r]);
+
+      constexpr int SPT = D / NRG;  // state rows per thread
+      const int d0 = rg * SPT;
+      const float gC = gam[C - 1];
+      const float eC = expf(gC);
+      float4 as[SPT];
+#pragma unroll
+      for (int r = 0; r < SPT; ++r) {
+        const float4 sv = lds4(Ss + (d0 + r) * P + 4 * cg);
+        as[r] = make_float4(eC * sv.x, eC * sv.y, eC * sv.z, eC * sv.w);
+      }
+#pragma unroll 1
+      for (int i = 0; i < c; ++i) {
+        const float w = expf(gC - gam[i]);
+        const float4 u = lds4(Us + i * P + 4 * cg);
+        const float4 uw = make_float4(w * u.x, w * u.y, w * u.z, w * u.w);
+#pragma unroll
+        for (int r4 = 0; r4 < SPT; r4 += 4) {
+          const float4 kk = lds4(Ks + i * P + d0 + r4);
+          const float kx[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            as[r4 + q].x = fmaf(kx[q], uw.x, as[r4 + q].x);
+            as[r4 + q].y = fmaf(kx[q], uw.y, as[r4 + q].y);
+            as[r4 + q].z = fmaf(kx[q], uw.z, as[r4 + q].z);
+            as[r4 + q].w = fmaf(kx[q], uw.w, as[r4 + q].w);
+          }
+        }
+      }
+      __syncthreads();  // every thread is done reading S (K S above) before it is rewritten
+#pragma unroll
+      for (int r = 0; r < SPT; ++r) sts4(Ss + (d0 + r) * P + 4 * cg, as[r]);
+    }
+    __syncthreads();
+    // ---- output rows: o rounded to T, then the fused gated RMSNorm (one warp per row); the z rows
+    // are staged first in the K region (free now), all loads in flight at once
+    const bool gated = a.z != nullptr;
+    if (gated) {
+      constexpr int EPV = 16 / (int)sizeof(T), VPR = D / EPV, NV = C * VPR / Y::kThreads;
+      static_assert(C * VPR % Y::kThreads == 0, "z tiling");
+      const T* zb = reinterpret_cast<const T*>(a.z) + (int64_t)vh * D;
+      const bool zvec = ((reinterpret_cast<uintptr_t>(zb) | (uintptr_t)(a.z_stride_tok * (int64_t)sizeof(T))) & 15) == 0;
+      if (zvec) {
+        uint4 raw[NV];
+#pragma unroll
+        for (int n = 0; n < NV; ++n) {
+          const int e = tid + n * Y::kThreads, i = e / VPR, vi = e - (e / VPR) * VPR;
+          raw[n] = i < c ? *reinterpret_cast<const uint4*>(zb + (t0 + c0 + i) * a.z_stride_tok + vi * EPV)
+                         : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int n = 0; n < NV; ++n) {
+          const int e = tid + n * Y::kThreads, i = e / VPR, vi = e - (e / VPR) * VPR;
+          const T* src = reinterpret_cast<const T*>(&raw[n]);
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) Ks[i * P + vi * EPV + q] = to_f(src[q]);
+        }
+      } else {
+#pragma unroll 4
+        for (int e = tid; e < c * D; e += Y::kThreads) {
+          const int i = e / D, d = e - (e / D) * D;
+          Ks[i * P + d] = to_f(zb[(t0 + c0 + i) * a.z_stride_tok + d]);
+        }
+      }
+      __syncthreads();
+    }
+    const T* wn = gated ? reinterpret_cast<const T*>(a.norm_weight) + (a.norm_weight_len == D ? 0 : (int64_t)vh * D)
+                        : nullptr;
+    for (int i = warp; i < c; i += Y::kThreads / 32) {
+      const int64_t t = t0 + c0 + i;
+      T* out = reinterpret_cast<T*>(a.out) + t * a.out_stride_tok + (int64_t)vh * D;
+      float x[D / 32];
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < D / 32; ++k) {
+        x[k] = round_to<T>(Qs[i * P + lane + 32 * k]);
+        ss = fmaf(x[k], x[k], ss);
+      }
+      if (!gated) {
+#pragma unroll
+        for (int k = 0; k < D / 32; ++k) out[lane + 32 * k] = from_f<T>(x[k]);
+        continue;
+      }
+      ss = warp_sum(ss);
+      const float rs = rsqrtf(ss / (float)D + a.norm_eps);
+#pragma unroll
+      for (int k = 0; k < D / 32; ++k) {
+        const int j = lane + 32 * k;
+        out[j] = from_f<T>(to_f(wn[j]) * (x[k] * rs) * silu_f(Ks[i * P + j]));
+      }
+    }
+    __syncthreads();  // the next chunk overwrites Q/K/U
+  }
+  for (int e = tid; e < D * NCG; e += Y::kThreads) {
+    const int r = e / NCG, c4 = e - (e / NCG) * NCG;
+    __stcs(reinterpret_cast<float4*>(st + (size_t)r * D) + c4, lds4(Ss + r * P + 4 * c4));
+  }
+}
+
 template <int DK, int DV>
 constexpr size_t decode_smem(int vpk) {
   return (size_t)(2 * DK + vpk * DV + 16 * DV + 2 * DV + 4 + 2 * vpk) * 4;
@@ -445,6 +816,15 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
   conv_extend_kernel<T><<<a.num_tokens, 256, 0, s>>>(a, w.start, (T*)w.conv_out);
   dim3 rg((conv_dim + 255) / 256, a.batch_size);
   conv_state_roll_kernel<T><<<rg, 256, 0, s>>>(a, w.start);
+  if constexpr (DK == DV && (DK == 64 || DK == 128)) {  // a7: chunked form
+    constexpr size_t csmem = ChunkLay<DK>::kBytes;
+    cudaError_t e = cudaFuncSetAttribute(chunk_extend_kernel<T, DK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
+    if (e != cudaSuccess) return e;
+    chunk_extend_kernel<T, DK><<<a.batch_size * a.num_v_heads, ChunkLay<DK>::kThreads, csmem, s>>>(
+        a, w.start, (const T*)w.conv_out);
+    return cudaGetLastError();
+  }
   const size_t smem = (size_t)(2 * DK + DV + 16 * DV + 2 * DV + 4 + 2) * 4;
   cudaError_t e = cudaFuncSetAttribute(recurrent_extend_kernel<T, DK, DV>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
