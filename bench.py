@@ -405,15 +405,15 @@ def bench_extend(args, rank, world, dev):
     from tokenfactory_b200 import ops
     from tokenfactory_b200.tp import head_shard
 
-    B, D = C4["B"], C4["D"]
+    B, D = args.requests, C4["D"]
     sh = head_shard(C4["Hq"], C4["Hkv"], C4["Hk"], C4["Hv"], rank, world)
     hq, hkv, hk, hv = len(sh.q_heads), len(sh.kv_heads), len(sh.k_heads), len(sh.v_heads)
     gen = torch.Generator().manual_seed(4)
-    P = torch.randint(0, C4["Pmax"] + 1, (B,), generator=gen)
-    E = torch.randint(C4["Emin"], C4["Emax"] + 1, (B,), generator=gen)
+    P = torch.randint(0, C4["Pmax"] + 1, (max(B, C4["B"]),), generator=gen)[:B]
+    E = torch.randint(C4["Emin"], C4["Emax"] + 1, (max(B, C4["B"]),), generator=gen)[:B]
     L = P + E
     T = int(E.sum())
-    S = C4["slots"]
+    S = args.ext_pool_slots
     perm = torch.randperm(S - 1, generator=gen)[: int(L.sum())] + 1
     Lmax = int(L.max())
     r2t = torch.full((B, Lmax), -1, dtype=torch.int64)
@@ -502,7 +502,7 @@ def bench_extend(args, rank, world, dev):
                      "traffic": _profile_traffic("paged_extend_config4.md")},
         "gdn_extend": {"tok_per_s": T / gdn_s, "ms_per_step": gdn_s * 1e3,
                        "tflops_min_count": T * gdn_flops_tok / gdn_s / 1e12,
-                       "kernel": "tf_gdn_extend (conv + recurrent state in registers)"},
+                       "kernel": "tf_gdn_extend (varlen conv + chunked WY delta rule, C=64, fp32)"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
@@ -608,6 +608,10 @@ def main():
                     help="profiling only: decode batch (default: config 2's 128)")
     ap.add_argument("--pool-slots", type=int, default=C2["slots"],
                     help="profiling only: KV pool slots (default: config 2's 1.2M)")
+    ap.add_argument("--requests", type=int, default=C4["B"],
+                    help="config 4: requests in the extend batch (smaller cases for ncu captures)")
+    ap.add_argument("--ext-pool-slots", type=int, default=C4["slots"],
+                    help="config 4: KV pool slots")
     ap.add_argument("--no-e2e", action="store_true",
                     help="profiling only: device-timed leg alone, short output")
     args = ap.parse_args()
