@@ -298,6 +298,16 @@ __device__ void find_request(int64_t t, const int64_t* ext, int B, int* b_out, i
   *start_out = 0;
 }
 
+// extend_len of request b, cut to the tokens the batch holds (a longer one is recorded)
+__device__ __forceinline__ int64_t clamp_extend(const tf_gdn_args& a, int b, int64_t t0) {
+  const int64_t E = a.extend_lens[b];
+  if (t0 + E > a.num_tokens) {
+    record_err(a.err, TF_KERR_REQ_RANGE);
+    return a.num_tokens - t0 > 0 ? a.num_tokens - t0 : 0;
+  }
+  return E;
+}
+
 // token offsets of every request (exclusive prefix of extend_lens), one CTA
 __global__ void offsets_kernel(const int64_t* ext, int B, int64_t* start) {
   if (threadIdx.x == 0) {
@@ -333,6 +343,108 @@ __global__ void __launch_bounds__(256) conv_extend_kernel(tf_gdn_args a, const i
     conv_out[t * conv_dim + c] = from_f<T>(conv_channel<T>(a, x0, i, st, c));
 }
 
+// Same conv for K = 4, tiled: one CTA per (64-token chunk of the packed batch, 512 channels); a
+// thread owns two adjacent channels, keeps their weights and the last three inputs of the current
+// request in registers and walks the chunk's tokens, reloading the window from conv_state (or from
+// the preceding tokens) where a request starts.  Every input element is read once.
+template <typename T>
+__device__ __forceinline__ void load_pair(const T* p, bool vec, float& x0, float& x1) {
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+      const T* h = reinterpret_cast<const T*>(&w);
+      x0 = to_f(h[0]);
+      x1 = to_f(h[1]);
+      return;
+    }
+  }
+  x0 = to_f(p[0]);
+  x1 = to_f(p[1]);
+}
+
+constexpr int kConvTok = 64;
+constexpr int kConvThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kConvThreads) conv4_tiled_kernel(tf_gdn_args a, const int64_t* start,
+                                                                   T* conv_out) {
+  const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
+  const int c = (blockIdx.x * kConvThreads + threadIdx.x) * 2;
+  const int64_t T_all = start[a.batch_size] < a.num_tokens ? start[a.batch_size] : a.num_tokens;
+  const int64_t t_begin = (int64_t)blockIdx.y * kConvTok;
+  if (t_begin >= T_all) return;
+  const int64_t t_end = t_begin + kConvTok < T_all ? t_begin + kConvTok : T_all;
+  // request of the chunk's first token: binary search over start[0..B]
+  __shared__ int s_b;
+  if (threadIdx.x == 0) {
+    int lo = 0, hi = a.batch_size - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (start[mid] <= t_begin) lo = mid; else hi = mid - 1;
+    }
+    s_b = lo;
+  }
+  __syncthreads();
+  if (c >= conv_dim) return;
+  const T* wt = reinterpret_cast<const T*>(a.conv_weight);
+  float w0[4], w1[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    w0[j] = to_f(wt[(int64_t)c * 4 + j]);
+    w1[j] = to_f(wt[(int64_t)(c + 1) * 4 + j]);
+  }
+  const T* cb = reinterpret_cast<const T*>(a.conv_bias);
+  const float b0 = cb ? to_f(cb[c]) : 0.f, b1 = cb ? to_f(cb[c + 1]) : 0.f;
+  const T* x = reinterpret_cast<const T*>(a.qkv);
+  const bool xvec = ((reinterpret_cast<uintptr_t>(x) & 3) == 0) && (a.qkv_stride_tok % 2 == 0);
+  int b = s_b;
+  int64_t rs = start[b], re = start[b + 1];
+  float h0[3], h1[3];  // inputs at positions i-3, i-2, i-1 of the current request
+  bool need_init = true;
+  for (int64_t t = t_begin; t < t_end; ++t) {
+    while (t >= re) {  // next request (uniform over the CTA)
+      ++b;
+      rs = re;
+      re = start[b + 1];
+      need_init = true;
+    }
+    if (need_init) {
+      const int64_t slot = a.req_pool_indices[b];
+      const bool ok = slot >= 0 && slot < a.num_slots;
+      const T* st = reinterpret_cast<const T*>(a.conv_state) + (ok ? slot : 0) * a.conv_stride_slot;
+      const int64_t i = t - rs;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int64_t p = i - 3 + j;
+        if (p >= 0) {
+          load_pair<T>(x + (rs + p) * a.qkv_stride_tok + c, xvec, h0[j], h1[j]);
+        } else {
+          h0[j] = ok ? to_f(st[(int64_t)c * 3 + 3 + p]) : 0.f;
+          h1[j] = ok ? to_f(st[(int64_t)(c + 1) * 3 + 3 + p]) : 0.f;
+        }
+      }
+      if (!ok && c == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+      need_init = false;
+    }
+    float x0, x1;
+    load_pair<T>(x + t * a.qkv_stride_tok + c, xvec, x0, x1);
+    float acc0 = fmaf(w0[0], h0[0], fmaf(w0[1], h0[1], fmaf(w0[2], h0[2], fmaf(w0[3], x0, b0))));
+    float acc1 = fmaf(w1[0], h1[0], fmaf(w1[1], h1[1], fmaf(w1[2], h1[2], fmaf(w1[3], x1, b1))));
+    acc0 = round_to<T>(silu_f(round_to<T>(acc0)));
+    acc1 = round_to<T>(silu_f(round_to<T>(acc1)));
+    T* o = conv_out + t * conv_dim + c;
+    if constexpr (sizeof(T) == 2) {
+      T pr[2] = {from_f<T>(acc0), from_f<T>(acc1)};
+      *reinterpret_cast<uint32_t*>(o) = *reinterpret_cast<uint32_t*>(pr);
+    } else {
+      o[0] = from_f<T>(acc0);
+      o[1] = from_f<T>(acc1);
+    }
+    h0[0] = h0[1]; h0[1] = h0[2]; h0[2] = x0;
+    h1[0] = h1[1]; h1[1] = h1[2]; h1[2] = x1;
+  }
+}
+
 // conv_state <- last K-1 columns of [state | x] per (request, channel)  (linear_attention.py:142-143)
 template <typename T>
 __global__ void conv_state_roll_kernel(tf_gdn_args a, const int64_t* start) {
@@ -343,7 +455,7 @@ __global__ void conv_state_roll_kernel(tf_gdn_args a, const int64_t* start) {
   const int64_t slot = a.req_pool_indices[b];
   if (slot < 0 || slot >= a.num_slots) return;
   const int K = a.conv_kernel;
-  const int64_t E = a.extend_lens[b];
+  const int64_t E = clamp_extend(a, b, start[b]);
   T* st = reinterpret_cast<T*>(a.conv_state) + slot * a.conv_stride_slot + (int64_t)c * (K - 1);
   const T* x0 = reinterpret_cast<const T*>(a.qkv) + start[b] * a.qkv_stride_tok + c;
   T nw[8];
@@ -378,9 +490,9 @@ __global__ void __launch_bounds__(2 * DV) recurrent_extend_kernel(tf_gdn_args a,
 
   const int64_t slot = a.req_pool_indices[b];
   if (slot < 0 || slot >= a.num_slots) return;  // recorded by the conv kernel
-  const int64_t E = a.extend_lens[b];
-  if (E <= 0) return;
   const int64_t t0 = start[b];
+  const int64_t E = clamp_extend(a, b, t0);
+  if (E <= 0) return;
   float* st = a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * DK * DV;
   float4 S[DK / 8];
   load_state<DK, DV>(S, st);
@@ -472,9 +584,9 @@ __global__ void __launch_bounds__(256, 1) chunk_extend_kernel(tf_gdn_args a, con
 
   const int64_t slot = a.req_pool_indices[b];
   if (slot < 0 || slot >= a.num_slots) return;  // recorded by the conv kernel
-  const int64_t E = a.extend_lens[b];
-  if (E <= 0) return;
   const int64_t t0 = start[b];
+  const int64_t E = clamp_extend(a, b, t0);
+  if (E <= 0) return;
   float* st = a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * D * D;
   for (int e = tid; e < D * NCG; e += Y::kThreads) {
     const int r = e / NCG, cg = e - (e / NCG) * NCG;
@@ -813,7 +925,13 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
   ExtWs w = carve_ext(ws, a);
   const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
   offsets_kernel<<<1, 32, 0, s>>>(a.extend_lens, a.batch_size, w.start);
-  conv_extend_kernel<T><<<a.num_tokens, 256, 0, s>>>(a, w.start, (T*)w.conv_out);
+  if (a.conv_kernel == 4 && conv_dim % 2 == 0) {
+    dim3 cg((conv_dim / 2 + kConvThreads - 1) / kConvThreads,
+            (unsigned)((a.num_tokens + kConvTok - 1) / kConvTok));
+    conv4_tiled_kernel<T><<<cg, kConvThreads, 0, s>>>(a, w.start, (T*)w.conv_out);
+  } else {
+    conv_extend_kernel<T><<<a.num_tokens, 256, 0, s>>>(a, w.start, (T*)w.conv_out);
+  }
   dim3 rg((conv_dim + 255) / 256, a.batch_size);
   conv_state_roll_kernel<T><<<rg, 256, 0, s>>>(a, w.start);
   if constexpr (DK == DV && (DK == 64 || DK == 128)) {  // a7: chunked form
