@@ -475,9 +475,27 @@ def bench_extend(args, rank, world, dev):
         _barrier(world)
         return _max_over_ranks(t0.elapsed_time(t1) / 1e3, world) / steps
 
+    # fused prologue of the same layer (q/k RMSNorm + partial RoPE + KV store), q read as the
+    # strided half of a [T, Hq, 2D] q_proj output as in the module
+    qg = torch.randn((T, hq, 2 * D), generator=g, device=dev, dtype=bf)
+    kp = torch.randn((T, hkv, D), generator=g, device=dev, dtype=bf)
+    vp = torch.randn((T, hkv, D), generator=g, device=dev, dtype=bf)
+    qnw = (1.0 + 0.1 * torch.randn((D,), generator=g, device=dev)).to(bf)
+    knw = (1.0 + 0.1 * torch.randn((D,), generator=g, device=dev)).to(bf)
+    rot = D // 4
+    inv_freq = 1.0 / (1e7 ** (torch.arange(0, rot, 2, dtype=torch.float32, device=dev) / rot))
+    pos_d = torch.cat([torch.arange(int(P[b]), int(L[b])) for b in range(B)]).to(dev)
+    q_pro = torch.empty((T, hq, D), dtype=bf, device=dev)
+
+    def pro_step():
+        ops.attn_prologue(qg[..., :D], kp, vp, qnw, knw, pos_d, inv_freq, kb, vb, loc_d,
+                          q_out=q_pro)
+
     with ClockSampler(torch.cuda.current_device()) as clk:
         attn_s = timed(attn_step, args.steps)
         gdn_s = timed(gdn_step, max(1, args.steps // 4))
+        pro_s = timed(pro_step, args.steps)
+    pro_bytes = 2 * T * (hq + 2 * hkv) * D * 2 + 2 * T * 8
     Pf, Ef = P.double(), E.double()
     flops = float((4 * C4["Hq"] * D * (Ef * Pf + Ef * (Ef + 1) / 2)).sum())  # whole job
     gdn_flops_tok = C4["Hv"] * (6 * dk * dv + 3 * 64 * dv) + C4["Hk"] * 4 * 64 * dk
@@ -503,6 +521,10 @@ def bench_extend(args, rank, world, dev):
         "gdn_extend": {"tok_per_s": T / gdn_s, "ms_per_step": gdn_s * 1e3,
                        "tflops_min_count": T * gdn_flops_tok / gdn_s / 1e12,
                        "kernel": "tf_gdn_extend (varlen conv + chunked WY delta rule, C=64, fp32)"},
+        "prologue": {"gb_per_s": pro_bytes / pro_s / 1e9, "ms_per_step": pro_s * 1e3,
+                     "frac_of_hbm_peak": pro_bytes / pro_s / 1e9 / _peaks()[0], "peak_kind": _peaks()[1],
+                     "bytes_per_launch": pro_bytes,
+                     "kernel": "tf_attn_prologue (q/k RMSNorm + partial RoPE + KV store)"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }

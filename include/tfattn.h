@@ -91,6 +91,54 @@ typedef struct tf_kv_store_args {
 TF_API tf_status tf_kv_store(const tf_kv_store_args* args, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Fused full-attention prologue: the q/k RMSNorm, the partial (M-)RoPE and the KV-pool store of
+ * Qwen3_8FullAttention.forward (qwen3_8/full_attention.py:142-149) in one pass over q, k and v:
+ *   y      = bf16(w * x * rsqrt(mean(x^2) + eps))            qwen3_8/rms_norm.py:19-24 (fp32 inside)
+ *   c, s   = bf16(cos(f)), bf16(sin(f)),  f_j = pos * inv_freq[j]   qwen3_8/rotary_embedding.py:46-76
+ *   out_d  = bf16(bf16(y_d c_d) + bf16(rot(y)_d s_d)) for d < rotary_dim, y_d beyond   (:78-95)
+ * q_out[t] gets the result for q; k_buffer[out_cache_loc[t]] the result for k and
+ * v_buffer[out_cache_loc[t]] the v row (negative locations wrap as torch indexing does; locations
+ * still out of range are recorded in *err and skipped).  positions is [T] (pos_rows 1) or the
+ * M-RoPE [3, T] (pos_rows 3, rows pos_stride elements apart) combined by mrope_section, interleaved
+ * (mrope_interleaved 1) or in consecutive sections.  inv_freq is the module's fp32 buffer.
+ * rotary_dim must be even, <= head_dim, with rotary_dim/2 a multiple of 32 or a power of two < 32.
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_attn_prologue_args {
+  const void* q;               /* [T, Hq, D] (may be a strided view of the q_proj output)   */
+  int64_t q_stride_tok, q_stride_head;
+  const void* k;               /* [T, Hkv, D]                                               */
+  int64_t k_stride_tok, k_stride_head;
+  const void* v;               /* [T, Hkv, D]                                               */
+  int64_t v_stride_tok, v_stride_head;
+  const void* q_norm_weight;   /* [D], dtype                                                */
+  const void* k_norm_weight;   /* [D], dtype                                                */
+  const int64_t* positions;    /* [T] or [3, T]                                             */
+  int64_t pos_stride;          /* elements between the rows of [3, T] positions             */
+  const float* inv_freq;       /* [rotary_dim / 2]                                          */
+  void* q_out;                 /* [T, Hq, D]                                                */
+  int64_t q_out_stride_tok, q_out_stride_head;
+  void* k_buffer;              /* [num_slots, Hkv, D] layer views                           */
+  void* v_buffer;
+  int64_t buf_stride_slot, buf_stride_head;
+  int64_t num_slots;
+  const int64_t* out_cache_loc;/* [T]                                                       */
+  int64_t num_tokens;
+  float eps;
+  int32_t pos_rows;            /* 1 or 3                                                    */
+  int32_t mrope_section[3];
+  int32_t mrope_interleaved;
+  int32_t rotary_dim;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t dtype;               /* of q, k, v, q_out and the pools                           */
+  int32_t norm_weight_dtype;   /* TF_DTYPE_F32 or dtype: the norms read w in this type      */
+  int32_t* err;                /* optional device word                                      */
+} tf_attn_prologue_args;
+
+TF_API tf_status tf_attn_prologue(const tf_attn_prologue_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * a2-a4. Paged (token-granular) GQA attention through req_to_token, with the fused output gate.
  *
  * Query token t of request b sits at absolute position P_b + i (P_b = seq_len_b - extend_len_b,

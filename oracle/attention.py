@@ -4,6 +4,8 @@ Restates qwen3_8/full_attention.py of yz29528/tokenFactory:
   kv_store             - :147-149   layer_k_buffer[out_cache_loc] = k (same for v)
   slot_based_attention - :163-283   the three branches of _slot_based_attention
   output_gate          - :157-158   attn_output * act(gate)
+  attn_prologue        - :142-149   q/k RMSNorm (qwen3_8/rms_norm.py:19-24), partial (M-)RoPE
+                                    (qwen3_8/rotary_embedding.py:46-95) and the pool write
 
 Arrays: bf16 tensors are uint16 bit patterns (see oracle.bf16); index tensors are int64.
 The attention itself is evaluated in float32 from the stored values (the "fp32 evaluation" the
@@ -128,3 +130,65 @@ def output_gate(attn: np.ndarray, gate: np.ndarray, mode: str, dtype: str) -> np
         raise ValueError(f"unknown gate mode {mode!r}")
     act = _bf.round_to(act.astype(np.float32), dtype)
     return _bf.round_to((attn.astype(np.float32) * act).astype(np.float32), dtype)
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float, dtype: str) -> np.ndarray:
+    """Qwen3_8RMSNorm.forward (qwen3_8/rms_norm.py:19-24): fp32 inside, one rounding to `dtype`.
+    x, weight float32 values; normalises over the last axis."""
+    xf = x.astype(np.float32)
+    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
+    xn = xf * (np.float32(1.0) / np.sqrt(var + np.float32(eps)))
+    return _bf.round_to((weight.astype(np.float32) * xn).astype(np.float32), dtype)
+
+
+def rope_cos_sin(positions: np.ndarray, inv_freq: np.ndarray, dtype: str,
+                 mrope_section: Sequence[int] = (11, 11, 10), interleaved: bool = True):
+    """PartialRotaryEmbedding._compute_cos_sin (qwen3_8/rotary_embedding.py:46-76): cos and sin
+    [T, rotary_dim] of positions [T] or [3, T], cast to `dtype` (returned as float32 values)."""
+    inv = inv_freq.astype(np.float32)
+    pos = np.asarray(positions)
+    if pos.ndim == 1:
+        freqs = pos.astype(np.float32)[:, None] * inv[None, :]
+    else:
+        f3 = pos.astype(np.float32)[:, :, None] * inv[None, None, :]
+        if interleaved:
+            freqs = f3[0].copy()
+            for dim_idx in (1, 2):
+                limit = mrope_section[dim_idx] * 3
+                freqs[:, dim_idx:limit:3] = f3[dim_idx, :, dim_idx:limit:3]
+        else:
+            edges = np.cumsum([0] + list(mrope_section))
+            freqs = np.concatenate([f3[i, :, edges[i]:edges[i + 1]] for i in range(3)], axis=-1)
+    emb = np.concatenate([freqs, freqs], axis=-1).astype(np.float32)
+    return _bf.round_to(np.cos(emb), dtype), _bf.round_to(np.sin(emb), dtype)
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, dtype: str) -> np.ndarray:
+    """PartialRotaryEmbedding.forward on one tensor (qwen3_8/rotary_embedding.py:78-95):
+    x [T, H, D] float32 values of `dtype`, cos/sin [T, rotary_dim]; each torch op rounds."""
+    rot = cos.shape[-1]
+    half = rot // 2
+    xr, xp = x[..., :rot], x[..., rot:]
+    rh = np.concatenate([-xr[..., half:], xr[..., :half]], axis=-1)
+    a = _bf.round_to((xr * cos[:, None, :]).astype(np.float32), dtype)
+    b = _bf.round_to((rh * sin[:, None, :]).astype(np.float32), dtype)
+    out = _bf.round_to((a + b).astype(np.float32), dtype)
+    return np.concatenate([out, xp], axis=-1)
+
+
+def attn_prologue(q: np.ndarray, k: np.ndarray, v: np.ndarray, q_norm_weight: np.ndarray,
+                  k_norm_weight: np.ndarray, positions: np.ndarray, inv_freq: np.ndarray,
+                  k_buf: np.ndarray, v_buf: np.ndarray, out_cache_loc: np.ndarray, dtype: str,
+                  eps: float = 1e-6, mrope_section: Sequence[int] = (11, 11, 10),
+                  interleaved: bool = True) -> np.ndarray:
+    """q/k RMSNorm, partial RoPE and the pool write of Qwen3_8FullAttention.forward
+    (qwen3_8/full_attention.py:142-149).  Tensors in storage form of `dtype`; the pools are
+    updated in place, the rotated q is returned in storage form."""
+    qv, kv = _bf.as_f32(q, dtype), _bf.as_f32(k, dtype)
+    qn = rms_norm(qv, _bf.as_f32(q_norm_weight, dtype), eps, dtype)
+    kn = rms_norm(kv, _bf.as_f32(k_norm_weight, dtype), eps, dtype)
+    cos, sin = rope_cos_sin(positions, inv_freq, dtype, mrope_section, interleaved)
+    qo = apply_rope(qn, cos, sin, dtype)
+    ko = apply_rope(kn, cos, sin, dtype)
+    kv_store(k_buf, v_buf, out_cache_loc, _bf.store(ko, dtype), v)
+    return _bf.store(qo, dtype)

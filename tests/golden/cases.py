@@ -216,3 +216,53 @@ def module_inputs(spec: dict) -> dict:
         out["conv_state"] = _normal(rng, (spec["slots"], conv_dim, m["kc"] - 1))
         out["ssm_state"] = _normal(rng, (spec["slots"], m["nv"], m["dk"], m["dv"]), 0.05)
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# fused attention prologue: q/k RMSNorm + partial (M-)RoPE + KV store
+# (qwen3_8/full_attention.py:142-149, qwen3_8/rms_norm.py, qwen3_8/rotary_embedding.py)
+# ---------------------------------------------------------------------------------------------
+PROLOGUE_CASES: Dict[str, dict] = {
+    "pro_bf16_d256": dict(dtype="bf16", hq=8, hkv=2, d=256, t=37, slots=64, pos_max=40000,
+                          mrope=None, seed=70),
+    "pro_bf16_d256_mrope": dict(dtype="bf16", hq=4, hkv=1, d=256, t=21, slots=32, pos_max=5000,
+                                mrope=([11, 11, 10], True), seed=71),
+    "pro_bf16_d256_mrope_chunked": dict(dtype="bf16", hq=4, hkv=2, d=256, t=9, slots=16,
+                                        pos_max=300, mrope=([11, 11, 10], False), seed=72),
+    "pro_bf16_d128_gqa_strided": dict(dtype="bf16", hq=16, hkv=1, d=128, t=29, slots=48,
+                                      pos_max=200000, mrope=None, strided=True, neg=[3, 10],
+                                      seed=73),
+    "pro_f32_d64": dict(dtype="f32", hq=4, hkv=4, d=64, t=13, slots=20, pos_max=1000, mrope=None,
+                        seed=74),
+}
+PROLOGUE_THETA = 10000000.0
+PROLOGUE_EPS = 1e-6
+
+
+def prologue_inputs(spec: dict) -> dict:
+    """q (inside a [T, Hq, 2D] q_proj output when spec['strided']), k, v, the two norm weights,
+    positions ([T] or [3, T]), the pools and out_cache_loc of a prologue case."""
+    rng = np.random.default_rng(spec["seed"])
+    dt = spec["dtype"]
+    hq, hkv, d, t, s = spec["hq"], spec["hkv"], spec["d"], spec["t"], spec["slots"]
+    qg = _bf.store(_normal(rng, (t, hq, 2 * d if spec.get("strided") else d)), dt)
+    k = _bf.store(_normal(rng, (t, hkv, d)), dt)
+    v = _bf.store(_normal(rng, (t, hkv, d)), dt)
+    qw = _bf.store((1.0 + 0.1 * _normal(rng, (d,))).astype(np.float32), dt)
+    kw = _bf.store((1.0 + 0.1 * _normal(rng, (d,))).astype(np.float32), dt)
+    rows = 3 if spec["mrope"] else 1
+    pos = rng.integers(0, spec["pos_max"], (rows, t), dtype=np.int64)
+    if rows == 1:
+        pos = pos[0]
+    k_buf = _bf.store(_normal(rng, (s, hkv, d)), dt)
+    v_buf = _bf.store(_normal(rng, (s, hkv, d)), dt)
+    loc = rng.permutation(np.arange(1, s, dtype=np.int64))[:t]
+    for i in spec.get("neg", []):
+        loc[i] = loc[i] - s  # the same slot through a negative index
+    return dict(qg=qg, k=k, v=v, q_norm_weight=qw, k_norm_weight=kw, positions=pos,
+                k_buf=k_buf, v_buf=v_buf, out_cache_loc=loc)
+
+
+def prologue_q(inp: dict, spec: dict) -> np.ndarray:
+    """The q view of the case: the first half of each head's q_proj row when strided."""
+    return inp["qg"][..., :spec["d"]] if spec.get("strided") else inp["qg"]

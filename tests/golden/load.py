@@ -44,3 +44,12 @@ def module_case(name: str):
     assert bytes(z[f"{name}/checksum"]).decode() == C.checksum({**w, **inp}), f"input drift in {name}"
     gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
     return spec, w, inp, gold
+
+
+def prologue_case(name: str):
+    spec = C.PROLOGUE_CASES[name]
+    inp = C.prologue_inputs(spec)
+    z = _npz("prologue_golden.npz")
+    assert bytes(z[f"{name}/checksum"]).decode() == C.checksum(inp), f"input drift in {name}"
+    gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
+    return spec, inp, gold

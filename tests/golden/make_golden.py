@@ -16,6 +16,9 @@ Reference functions exercised (paths inside the reference project):
   Qwen3_8RMSNormGated.forward                  qwen3_8/rms_norm_gated.py:26-40
   Qwen3_8FullAttention.forward                 qwen3_8/full_attention.py:112-161
   Qwen3_8LinearAttention.forward               qwen3_8/linear_attention.py:300-364
+  Qwen3_8RMSNorm.forward (q_norm / k_norm)     qwen3_8/rms_norm.py:19-24
+  PartialRotaryEmbedding.forward               qwen3_8/rotary_embedding.py:46-95
+  the pool write of Qwen3_8FullAttention       qwen3_8/full_attention.py:147-149
 """
 
 import argparse
@@ -223,6 +226,39 @@ def module_golden(ref) -> dict:
     return out
 
 
+def prologue_golden(ref) -> dict:
+    """q/k RMSNorm, partial (M-)RoPE and the pool write, through the reference's own modules
+    (the steps of Qwen3_8FullAttention.forward, qwen3_8/full_attention.py:142-149)."""
+    from qwen3_8.rms_norm import Qwen3_8RMSNorm
+    from qwen3_8.rotary_embedding import PartialRotaryEmbedding
+
+    out = {}
+    for name, spec in C.PROLOGUE_CASES.items():
+        inp = C.prologue_inputs(spec)
+        dt, d = spec["dtype"], spec["d"]
+        sec, inter = spec["mrope"] if spec["mrope"] else ([11, 11, 10], True)
+        qn, kn = Qwen3_8RMSNorm(d, eps=C.PROLOGUE_EPS), Qwen3_8RMSNorm(d, eps=C.PROLOGUE_EPS)
+        rope = PartialRotaryEmbedding(head_dim=d, partial_rotary_factor=0.25,
+                                      rope_theta=C.PROLOGUE_THETA, mrope_section=list(sec),
+                                      mrope_interleaved=inter)
+        with torch.inference_mode():
+            qn.weight.copy_(_t(inp["q_norm_weight"], dt).float())
+            kn.weight.copy_(_t(inp["k_norm_weight"], dt).float())
+            q = _t(C.prologue_q(inp, spec), dt)
+            k, v = _t(inp["k"], dt), _t(inp["v"], dt)
+            q, k = rope(qn(q), kn(k), torch.from_numpy(inp["positions"]))
+            kb, vb = _t(inp["k_buf"], dt), _t(inp["v_buf"], dt)
+            loc = torch.from_numpy(inp["out_cache_loc"])
+            kb[loc] = k
+            vb[loc] = v
+        out[f"{name}/q_out"] = _np(q)
+        out[f"{name}/k_buf"] = _np(kb)
+        out[f"{name}/v_buf"] = _np(vb)
+        out[f"{name}/inv_freq"] = rope.inv_freq.numpy().astype(np.float32)
+        out[f"{name}/checksum"] = np.frombuffer(C.checksum(inp).encode(), dtype=np.uint8)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True,
@@ -233,7 +269,8 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "attention_golden.npz"), **attention_golden(args))
     np.savez_compressed(os.path.join(HERE, "gdn_golden.npz"), **gdn_golden(args))
     np.savez_compressed(os.path.join(HERE, "module_golden.npz"), **module_golden(args))
-    for f in ("attention_golden.npz", "gdn_golden.npz", "module_golden.npz"):
+    np.savez_compressed(os.path.join(HERE, "prologue_golden.npz"), **prologue_golden(args))
+    for f in ("attention_golden.npz", "gdn_golden.npz", "module_golden.npz", "prologue_golden.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

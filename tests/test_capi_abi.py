@@ -49,10 +49,15 @@ def test_invalid_arguments_fail_without_a_gpu():
     assert b"NULL" in lib.tf_last_error()
     g = _capi.GdnArgs(batch_size=1, num_tokens=1)
     assert lib.tf_gdn_decode(ctypes.byref(g), None) == _capi.TF_ERR_INVALID_ARG
+    p = _capi.AttnPrologueArgs(num_tokens=4, num_q_heads=8, num_kv_heads=2, head_dim=256,
+                               rotary_dim=64, pos_rows=1, dtype=1)
+    assert lib.tf_attn_prologue(ctypes.byref(p), None) == _capi.TF_ERR_INVALID_ARG
+    assert b"NULL" in lib.tf_last_error()
 
 
 _STRUCTS = {
     "tf_kv_store_args": "KVStoreArgs",
+    "tf_attn_prologue_args": "AttnPrologueArgs",
     "tf_paged_attn_args": "PagedAttnArgs",
     "tf_gdn_args": "GdnArgs",
     "tf_gated_rmsnorm_args": "GatedRMSNormArgs",
@@ -79,3 +84,23 @@ def test_ctypes_layout_matches_c(tmp_path):
         st = getattr(_capi, pyname)
         got = ctypes.sizeof(st) if field == "size" else getattr(st, field).offset
         assert got == int(value), f"{pyname}.{field}: ctypes {got} != C {value}"
+
+
+def test_prologue_rejects_unbuilt_rotary_dims_without_a_gpu():
+    """Argument checks of tf_attn_prologue run before any CUDA call (fake non-NULL pointers)."""
+    from tokenfactory_b200 import _capi
+    lib = _capi.load()
+    fake = 0x1000
+    p = _capi.AttnPrologueArgs(
+        q=fake, k=fake, v=fake, q_norm_weight=fake, k_norm_weight=fake, positions=fake,
+        inv_freq=fake, q_out=fake, k_buffer=fake, v_buffer=fake, out_cache_loc=fake,
+        num_slots=8, num_tokens=4, num_q_heads=8, num_kv_heads=2, head_dim=256, rotary_dim=48,
+        pos_rows=1, dtype=1)
+    assert lib.tf_attn_prologue(ctypes.byref(p), None) == _capi.TF_ERR_UNSUPPORTED
+    assert b"rotary_dim 48" in lib.tf_last_error()
+    p.rotary_dim, p.pos_rows = 64, 2
+    assert lib.tf_attn_prologue(ctypes.byref(p), None) == _capi.TF_ERR_INVALID_ARG
+    p.pos_rows = 3
+    p.mrope_section[0], p.mrope_section[1], p.mrope_section[2] = 11, 11, 11
+    assert lib.tf_attn_prologue(ctypes.byref(p), None) == _capi.TF_ERR_INVALID_ARG
+    assert b"mrope_section" in lib.tf_last_error()

@@ -122,3 +122,28 @@ def test_every_golden_fixture_matches_its_regenerated_inputs():
         gdn_case(name)
     for name in C.MODULE_CASES:
         module_case(name)
+    from tests.golden.load import prologue_case
+    for name in C.PROLOGUE_CASES:
+        prologue_case(name)
+
+
+@pytest.mark.parametrize("name", sorted(C.PROLOGUE_CASES))
+def test_prologue_oracle_matches_reference(name):
+    """q/k RMSNorm + partial (M-)RoPE + pool write: the oracle reproduces the reference's modules
+    bit for bit in bf16 (every torch op rounds where the oracle rounds) and to fp32 rounding in
+    fp32."""
+    from tests.golden.load import prologue_case
+    spec, inp, gold = prologue_case(name)
+    dt = spec["dtype"]
+    kb, vb = inp["k_buf"].copy(), inp["v_buf"].copy()
+    sec, inter = spec["mrope"] if spec["mrope"] else ([11, 11, 10], True)
+    qo = OA.attn_prologue(C.prologue_q(inp, spec), inp["k"], inp["v"], inp["q_norm_weight"],
+                          inp["k_norm_weight"], inp["positions"], gold["inv_freq"], kb, vb,
+                          inp["out_cache_loc"], dt, C.PROLOGUE_EPS, sec, inter)
+    np.testing.assert_array_equal(vb, gold["v_buf"])
+    if dt == "bf16":
+        np.testing.assert_array_equal(qo, gold["q_out"])
+        np.testing.assert_array_equal(kb, gold["k_buf"])
+    else:
+        np.testing.assert_allclose(qo, gold["q_out"], rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(kb, gold["k_buf"], rtol=1e-6, atol=1e-6)

@@ -39,6 +39,24 @@ class KVStoreArgs(ctypes.Structure):
     ]
 
 
+class AttnPrologueArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("q_stride_tok", _i64), ("q_stride_head", _i64),
+        ("k", _vp), ("k_stride_tok", _i64), ("k_stride_head", _i64),
+        ("v", _vp), ("v_stride_tok", _i64), ("v_stride_head", _i64),
+        ("q_norm_weight", _vp), ("k_norm_weight", _vp),
+        ("positions", _vp), ("pos_stride", _i64), ("inv_freq", _vp),
+        ("q_out", _vp), ("q_out_stride_tok", _i64), ("q_out_stride_head", _i64),
+        ("k_buffer", _vp), ("v_buffer", _vp),
+        ("buf_stride_slot", _i64), ("buf_stride_head", _i64), ("num_slots", _i64),
+        ("out_cache_loc", _vp), ("num_tokens", _i64),
+        ("eps", ctypes.c_float), ("pos_rows", _i32), ("mrope_section", _i32 * 3),
+        ("mrope_interleaved", _i32), ("rotary_dim", _i32),
+        ("num_q_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32), ("dtype", _i32),
+        ("norm_weight_dtype", _i32), ("err", _vp),
+    ]
+
+
 class PagedAttnArgs(ctypes.Structure):
     _fields_ = [
         ("q", _vp), ("q_stride_tok", _i64), ("q_stride_head", _i64),
@@ -92,6 +110,7 @@ SIGNATURES = [
     ("tf_status_string", ctypes.c_char_p, [_i32]),
     ("tf_last_error", ctypes.c_char_p, []),
     ("tf_kv_store", _i32, [ctypes.POINTER(KVStoreArgs), _vp]),
+    ("tf_attn_prologue", _i32, [ctypes.POINTER(AttnPrologueArgs), _vp]),
     ("tf_paged_decode_workspace_size", ctypes.c_size_t, [ctypes.POINTER(PagedAttnArgs)]),
     ("tf_paged_decode_attn", _i32, [ctypes.POINTER(PagedAttnArgs), _vp, ctypes.c_size_t, _vp]),
     ("tf_paged_decode_attn_noalloc", _i32, [ctypes.POINTER(PagedAttnArgs), _vp]),

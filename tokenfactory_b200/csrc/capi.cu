@@ -181,6 +181,38 @@ tf_status tf_kv_store(const tf_kv_store_args* a, void* stream) {
   return cuda_status(launch_kv_store(*a, s), "tf_kv_store");
 }
 
+tf_status tf_attn_prologue(const tf_attn_prologue_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->num_tokens < 0 || a->num_q_heads < 0 || a->num_kv_heads < 0 || a->head_dim < 0)
+    return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->num_tokens == 0) return TF_OK;
+  if (a->num_tokens > 0x7fffffff) return fail(TF_ERR_INVALID_ARG, "too many tokens for one launch");
+  if (!a->q || !a->k || !a->v || !a->q_out || !a->k_buffer || !a->v_buffer || !a->out_cache_loc ||
+      !a->q_norm_weight || !a->k_norm_weight || !a->positions || !a->inv_freq)
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  if (a->norm_weight_dtype != a->dtype && a->norm_weight_dtype != TF_DTYPE_F32)
+    return fail(TF_ERR_INVALID_ARG, "norm weights must be float32 or of the activation dtype");
+  if (a->num_q_heads <= 0 || a->num_kv_heads <= 0) return fail(TF_ERR_INVALID_ARG, "no heads");
+  if (a->num_slots <= 0) return fail(TF_ERR_INVALID_ARG, "empty pool");
+  if (a->pos_rows != 1 && a->pos_rows != 3)
+    return fail(TF_ERR_INVALID_ARG, "positions must have 1 or 3 rows, got %d", a->pos_rows);
+  if (a->pos_rows == 3) {
+    const int32_t* m = a->mrope_section;
+    if (m[0] < 0 || m[1] < 0 || m[2] < 0 || m[0] + m[1] + m[2] != a->rotary_dim / 2)
+      return fail(TF_ERR_INVALID_ARG, "mrope_section must sum to rotary_dim / 2");
+  }
+  if (!attn_prologue_supported(*a))
+    return fail(TF_ERR_UNSUPPORTED,
+                "prologue: head_dim %d with rotary_dim %d is not built (head_dim 64/128/256; "
+                "rotary_dim/2 a multiple of 32 or a power of two below 32)",
+                a->head_dim, a->rotary_dim);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_attn_prologue(*a, s), "tf_attn_prologue");
+}
+
 size_t tf_paged_decode_workspace_size(const tf_paged_attn_args* a) {
   if (a == nullptr || a->batch_size <= 0) return 0;
   if (!paged_decode_mma_supported(*a)) return 0;

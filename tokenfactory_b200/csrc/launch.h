@@ -10,6 +10,9 @@ namespace tf {
 
 // kv_store.cu
 cudaError_t launch_kv_store(const tf_kv_store_args& a, cudaStream_t s);
+// prologue.cu: fused q/k RMSNorm + partial RoPE + KV store
+bool attn_prologue_supported(const tf_attn_prologue_args& a);
+cudaError_t launch_attn_prologue(const tf_attn_prologue_args& a, cudaStream_t s);
 
 // paged_attn_simt.cu: any dtype / head_dim <= 256, decode and extend
 cudaError_t launch_paged_attn_simt(const tf_paged_attn_args& a, cudaStream_t s);

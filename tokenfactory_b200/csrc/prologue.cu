@@ -1,0 +1,289 @@
+// Fused full-attention prologue (qwen3_8/full_attention.py:142-149): q/k RMSNorm
+// (qwen3_8/rms_norm.py:19-24), partial (M-)RoPE (qwen3_8/rotary_embedding.py:46-95) and the KV-pool
+// store, one read of q/k/v and one write of q_out and the pool rows.  HBM-bound.
+//
+// One CTA per token: its threads first compute the token's cos/sin (rounded to the dtype, as the
+// reference casts them) into shared memory, then each warp takes whole rows — the Hq q-heads, the
+// Hkv k-heads (both normalised and rotated) and the Hkv v-heads (copied).  Lane l holds elements
+// d = l + 32 i of a row, so loads and stores are coalesced whatever the strides, and the rotation
+// partner d +- rotary_dim/2 is in the same lane (half a multiple of 32) or in lane l ^ half
+// (half a power of two below 32).
+#include "common.cuh"
+#include "launch.h"
+
+namespace tf {
+namespace prologue {
+
+constexpr int kThreads = 256;
+constexpr int kMaxD = 256;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) prologue_kernel(tf_attn_prologue_args a) {
+  constexpr int E = D / 32;  // elements per lane
+  __shared__ float cs[kMaxD / 2], sn[kMaxD / 2];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int half = a.rotary_dim / 2;
+  for (int j = tid; j < half; j += kThreads) {
+    int row = 0;
+    if (a.pos_rows == 3) {
+      if (a.mrope_interleaved) {
+        const int m = j % 3;
+        if (m == 1 && j < 3 * a.mrope_section[1]) row = 1;
+        else if (m == 2 && j < 3 * a.mrope_section[2]) row = 2;
+      } else {
+        row = j < a.mrope_section[0] ? 0 : (j < a.mrope_section[0] + a.mrope_section[1] ? 1 : 2);
+      }
+    }
+    const float f = (float)a.positions[row * a.pos_stride + t] * a.inv_freq[j];
+    cs[j] = round_to<T>(cosf(f));
+    sn[j] = round_to<T>(sinf(f));
+  }
+  __syncthreads();
+
+  int64_t loc = a.out_cache_loc[t];
+  if (loc < 0) loc += a.num_slots;  // torch index semantics
+  const bool loc_ok = loc >= 0 && loc < a.num_slots;
+  if (!loc_ok && tid == 0) record_err(a.err, TF_KERR_SLOT_RANGE);
+
+  const int Hq = a.num_q_heads, Hkv = a.num_kv_heads;
+  const int nrows = Hq + 2 * Hkv;
+  const bool wf32 = a.norm_weight_dtype == TF_DTYPE_F32;
+  for (int r = warp; r < nrows; r += kThreads / 32) {
+    const T* src;
+    T* dst;
+    if (r < Hq) {
+      src = reinterpret_cast<const T*>(a.q) + t * a.q_stride_tok + (int64_t)r * a.q_stride_head;
+      dst = reinterpret_cast<T*>(a.q_out) + t * a.q_out_stride_tok + (int64_t)r * a.q_out_stride_head;
+    } else {
+      if (!loc_ok) continue;
+      const int h = r < Hq + Hkv ? r - Hq : r - Hq - Hkv;
+      const bool isk = r < Hq + Hkv;
+      src = reinterpret_cast<const T*>(isk ? a.k : a.v) + t * (isk ? a.k_stride_tok : a.v_stride_tok) +
+            (int64_t)h * (isk ? a.k_stride_head : a.v_stride_head);
+      dst = reinterpret_cast<T*>(isk ? a.k_buffer : a.v_buffer) + loc * a.buf_stride_slot +
+            (int64_t)h * a.buf_stride_head;
+    }
+    float x[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) x[i] = to_f(src[lane + 32 * i]);
+    if (r >= Hq + Hkv) {  // v: copied as is
+#pragma unroll
+      for (int i = 0; i < E; ++i) dst[lane + 32 * i] = from_f<T>(x[i]);
+      continue;
+    }
+    const void* w = r < Hq ? a.q_norm_weight : a.k_norm_weight;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss = fmaf(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / (float)D + a.eps);
+    float y[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const int d = lane + 32 * i;
+      const float wv = wf32 ? reinterpret_cast<const float*>(w)[d] : to_f(reinterpret_cast<const T*>(w)[d]);
+      y[i] = round_to<T>(wv * (x[i] * rs));
+    }
+    // rotate the first rotary_dim dims: out = bf16(bf16(y c) + bf16(rot(y) s)),
+    // rot(y)_d = -y_(d+half) for d < half, y_(d-half) for half <= d < 2 half
+    float o[E];
+    if (half >= 32) {
+      const int hi = half / 32;  // the partner sits hi elements further in the same lane
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const int d = lane + 32 * i;
+        if (d < 2 * half) {
+          const int j = d < half ? d : d - half;
+          const float pr = d < half ? -y[i + hi < E ? i + hi : i] : y[i - hi >= 0 ? i - hi : i];
+          o[i] = round_to<T>(round_to<T>(y[i] * cs[j]) + round_to<T>(pr * sn[j]));
+        } else {
+          o[i] = y[i];
+        }
+      }
+    } else {
+      // half < 32 (a power of two): only element 0 of lanes [0, 2 half) rotates
+#pragma unroll
+      for (int i = 0; i < E; ++i) o[i] = y[i];
+      const float partner = __shfl_xor_sync(0xffffffffu, y[0], half);
+      if (lane < 2 * half) {
+        const int j = lane < half ? lane : lane - half;
+        const float pr = lane < half ? -partner : partner;
+        o[0] = round_to<T>(round_to<T>(y[0] * cs[j]) + round_to<T>(pr * sn[j]));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[lane + 32 * i] = from_f<T>(o[i]);
+  }
+}
+
+// Vector form: lane l holds the E = D/32 contiguous elements [E l, E l + E) of a row (one 16-byte
+// access at D 256 in bf16), so the rotation partner d +- half sits in lane l ^ (half / E) at the
+// same position.  Needs rows aligned to E elements and half a multiple of E with half / E a power
+// of two below 32 (rotary_dim = D/4 at D 64/128/256).
+template <int BYTES> struct VecT;
+template <> struct VecT<4> { using type = uint32_t; };
+template <> struct VecT<8> { using type = uint2; };
+template <> struct VecT<16> { using type = uint4; };
+struct alignas(32) Vec32 { uint4 lo, hi; };  // fp32 at D 256: takes the strided path (vec_ok)
+template <> struct VecT<32> { using type = Vec32; };
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) prologue_vec_kernel(tf_attn_prologue_args a) {
+  constexpr int E = D / 32;
+  constexpr int NW = kThreads / 32;
+  using V = typename VecT<E * (int)sizeof(T)>::type;
+  __shared__ float cs[kMaxD / 2], sn[kMaxD / 2];
+  __shared__ int64_t s_loc;
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hq = a.num_q_heads, Hkv = a.num_kv_heads;
+  const int nrows = Hq + 2 * Hkv;
+  const int d0 = lane * E;
+  auto src_of = [&](int r) -> const T* {
+    if (r < Hq) return reinterpret_cast<const T*>(a.q) + t * a.q_stride_tok + (int64_t)r * a.q_stride_head;
+    const bool isk = r < Hq + Hkv;
+    const int h = isk ? r - Hq : r - Hq - Hkv;
+    return reinterpret_cast<const T*>(isk ? a.k : a.v) + t * (isk ? a.k_stride_tok : a.v_stride_tok) +
+           (int64_t)h * (isk ? a.k_stride_head : a.v_stride_head);
+  };
+  // this warp's first row is loading while the token's cos/sin and slot are prepared
+  V cur = warp < nrows ? *reinterpret_cast<const V*>(src_of(warp) + d0) : V();
+  const int half = a.rotary_dim / 2;
+  for (int j = tid; j < half; j += kThreads) {
+    int prow = 0;
+    if (a.pos_rows == 3) {
+      if (a.mrope_interleaved) {
+        const int m = j % 3;
+        if (m == 1 && j < 3 * a.mrope_section[1]) prow = 1;
+        else if (m == 2 && j < 3 * a.mrope_section[2]) prow = 2;
+      } else {
+        prow = j < a.mrope_section[0] ? 0 : (j < a.mrope_section[0] + a.mrope_section[1] ? 1 : 2);
+      }
+    }
+    const float f = (float)a.positions[prow * a.pos_stride + t] * a.inv_freq[j];
+    cs[j] = round_to<T>(cosf(f));
+    sn[j] = round_to<T>(sinf(f));
+  }
+  if (tid == 32) {
+    int64_t loc = a.out_cache_loc[t];
+    if (loc < 0) loc += a.num_slots;  // torch index semantics
+    if (loc < 0 || loc >= a.num_slots) {
+      record_err(a.err, TF_KERR_SLOT_RANGE);
+      loc = -1;
+    }
+    s_loc = loc;
+  }
+  __syncthreads();
+  const int64_t loc = s_loc;
+  const bool wf32 = a.norm_weight_dtype == TF_DTYPE_F32;
+  const int pmask = half / E;  // rotation partner: lane ^ pmask
+  const bool rotates = d0 < 2 * half, lower = d0 < half;
+  for (int r = warp; r < nrows; r += NW) {
+    const V nxt = r + NW < nrows ? *reinterpret_cast<const V*>(src_of(r + NW) + d0) : V();
+    T* dst;
+    bool isv = false;
+    if (r < Hq) {
+      dst = reinterpret_cast<T*>(a.q_out) + t * a.q_out_stride_tok + (int64_t)r * a.q_out_stride_head;
+    } else {
+      const bool isk = r < Hq + Hkv;
+      const int h = isk ? r - Hq : r - Hq - Hkv;
+      dst = loc < 0 ? nullptr
+                    : reinterpret_cast<T*>(isk ? a.k_buffer : a.v_buffer) + loc * a.buf_stride_slot +
+                          (int64_t)h * a.buf_stride_head;
+      isv = !isk;
+    }
+    if (dst != nullptr) {
+      if (isv) {
+        *reinterpret_cast<V*>(dst + d0) = cur;  // v: copied as is
+      } else {
+        const T* xe = reinterpret_cast<const T*>(&cur);
+        float x[E];
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          x[e] = to_f(xe[e]);
+          ss = fmaf(x[e], x[e], ss);
+        }
+        ss = warp_sum(ss);
+        const float rs = rsqrtf(ss / (float)D + a.eps);
+        const void* w = r < Hq ? a.q_norm_weight : a.k_norm_weight;
+        V outv;
+        T* oe = reinterpret_cast<T*>(&outv);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float wv = wf32 ? reinterpret_cast<const float*>(w)[d0 + e]
+                                : to_f(reinterpret_cast<const T*>(w)[d0 + e]);
+          const float y = round_to<T>(wv * (x[e] * rs));
+          const float p = __shfl_xor_sync(0xffffffffu, y, pmask);
+          float o = y;
+          if (rotates) {
+            const int j = (lower ? d0 : d0 - half) + e;
+            o = round_to<T>(round_to<T>(y * cs[j]) + round_to<T>((lower ? -p : p) * sn[j]));
+          }
+          oe[e] = from_f<T>(o);
+        }
+        *reinterpret_cast<V*>(dst + d0) = outv;
+      }
+    }
+    cur = nxt;
+  }
+}
+
+template <typename T>
+static bool vec_ok(const tf_attn_prologue_args& a) {
+  const int E = a.head_dim / 32;
+  const int vb = E * (int)sizeof(T);
+  if (vb != 4 && vb != 8 && vb != 16) return false;
+  const int half = a.rotary_dim / 2;
+  if (half % E || half / E >= 32 || ((half / E) & (half / E - 1))) return false;
+  auto al = [vb](const void* p) { return (reinterpret_cast<uintptr_t>(p) % vb) == 0; };
+  if (!al(a.q) || !al(a.k) || !al(a.v) || !al(a.q_out) || !al(a.k_buffer) || !al(a.v_buffer))
+    return false;
+  const int64_t st[] = {a.q_stride_tok, a.q_stride_head, a.k_stride_tok, a.k_stride_head,
+                        a.v_stride_tok, a.v_stride_head, a.q_out_stride_tok, a.q_out_stride_head,
+                        a.buf_stride_slot, a.buf_stride_head};
+  for (int64_t x : st)
+    if (x % E) return false;
+  return true;
+}
+
+template <typename T>
+static cudaError_t launch_t(const tf_attn_prologue_args& a, cudaStream_t s) {
+  const unsigned g = (unsigned)a.num_tokens;
+  if (vec_ok<T>(a)) {
+    switch (a.head_dim) {
+      case 64: prologue_vec_kernel<T, 64><<<g, kThreads, 0, s>>>(a); break;
+      case 128: prologue_vec_kernel<T, 128><<<g, kThreads, 0, s>>>(a); break;
+      default: prologue_vec_kernel<T, 256><<<g, kThreads, 0, s>>>(a); break;
+    }
+    return cudaGetLastError();
+  }
+  switch (a.head_dim) {
+    case 64: prologue_kernel<T, 64><<<g, kThreads, 0, s>>>(a); break;
+    case 128: prologue_kernel<T, 128><<<g, kThreads, 0, s>>>(a); break;
+    default: prologue_kernel<T, 256><<<g, kThreads, 0, s>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace prologue
+
+bool attn_prologue_supported(const tf_attn_prologue_args& a) {
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return false;
+  const int half = a.rotary_dim / 2;
+  if (a.rotary_dim < 2 || a.rotary_dim % 2 || a.rotary_dim > a.head_dim) return false;
+  if (half >= 32) return half % 32 == 0;
+  return (half & (half - 1)) == 0;
+}
+
+cudaError_t launch_attn_prologue(const tf_attn_prologue_args& a, cudaStream_t s) {
+  if (a.num_tokens == 0) return cudaSuccess;
+  switch (a.dtype) {
+    case TF_DTYPE_F32: return prologue::launch_t<float>(a, s);
+    case TF_DTYPE_BF16: return prologue::launch_t<__nv_bfloat16>(a, s);
+    default: return prologue::launch_t<__half>(a, s);
+  }
+}
+
+}  // namespace tf

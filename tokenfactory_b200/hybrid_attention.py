@@ -106,6 +106,30 @@ def linear_attention_core(qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a
 # ---------------------------------------------------------------------------------------------
 
 
+def _prologue_fusable(layer, q: torch.Tensor, positions: torch.Tensor) -> bool:
+    """Whether tf_attn_prologue builds this layer's q/k norm + RoPE: equal q/k eps, head_dim
+    64/128/256, rotary_dim/2 a multiple of 32 or a power of two below 32, 1-D positions or M-RoPE
+    sections that cover rotary_dim/2, norm weights in fp32 or the activation dtype.  Other layers
+    run their own modules (torch on the same device) before the fused attention."""
+    rot, qn, kn = layer.rotary_emb, layer.q_norm, layer.k_norm
+    if not all(hasattr(rot, x) for x in ("inv_freq", "rotary_dim", "mrope_section",
+                                         "mrope_interleaved")):
+        return False
+    if getattr(qn, "eps", None) != getattr(kn, "eps", None) or qn.eps is None:
+        return False
+    if layer.head_dim not in (64, 128, 256) or rot.inv_freq.dtype != torch.float32:
+        return False
+    half = rot.rotary_dim // 2
+    if rot.rotary_dim % 2 or rot.rotary_dim > layer.head_dim or half < 1 or \
+            not (half % 32 == 0 or (half < 32 and half & (half - 1) == 0)):
+        return False
+    if positions.dim() == 2 and (positions.shape[0] != 3 or sum(rot.mrope_section) != half):
+        return False
+    if positions.dim() not in (1, 2):
+        return False
+    return qn.weight.dtype in (q.dtype, torch.float32) and qn.weight.dtype == kn.weight.dtype
+
+
 class FullAttentionHotPath:
     """Overrides Qwen3_8FullAttention.forward / _slot_based_attention.
 
@@ -128,10 +152,21 @@ class FullAttentionHotPath:
             gate = None
         k = self.k_proj(hidden_states).view(num_tokens, self.num_kv_heads, d)
         v = self.v_proj(hidden_states).view(num_tokens, self.num_kv_heads, d)
+        layer_k_buffer, layer_v_buffer = cache_pool.get_full_kv_buffers(self.layer_idx)
+        if _prologue_fusable(self, q, positions):
+            # q/k RMSNorm + partial RoPE + pool write in one pass (:142-149)
+            rot = self.rotary_emb
+            q = ops.attn_prologue(q, k, v, self.q_norm.weight, self.k_norm.weight, positions,
+                                  rot.inv_freq, layer_k_buffer, layer_v_buffer,
+                                  forward_batch.out_cache_loc, eps=self.q_norm.eps,
+                                  mrope_section=tuple(rot.mrope_section),
+                                  mrope_interleaved=rot.mrope_interleaved)
+            out = _attend(q, layer_k_buffer, layer_v_buffer, forward_batch, self.scaling, gate,
+                          self.output_gate_mode).reshape(num_tokens, self.num_heads * d)
+            return self.o_proj(out)
         q = self.q_norm(q)
         k = self.k_norm(k)
         q, k = self.rotary_emb(q, k, positions)
-        layer_k_buffer, layer_v_buffer = cache_pool.get_full_kv_buffers(self.layer_idx)
         out = full_attention_core(q.contiguous(), k, v.contiguous(), gate, layer_k_buffer,
                                   layer_v_buffer, forward_batch, self.scaling,
                                   self.output_gate_mode)

@@ -99,6 +99,75 @@ def kv_store(k_buffer: torch.Tensor, v_buffer: torch.Tensor, out_cache_loc: torc
         C.check("tf_kv_store", C.load().tf_kv_store(ctypes.byref(a), _stream(dev)))
 
 
+def attn_prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_weight: torch.Tensor,
+                  k_norm_weight: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+                  k_buffer: torch.Tensor, v_buffer: torch.Tensor, out_cache_loc: torch.Tensor,
+                  eps: float = 1e-6, mrope_section=(11, 11, 10), mrope_interleaved: bool = True,
+                  q_out: Optional[torch.Tensor] = None,
+                  err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused q/k RMSNorm + partial (M-)RoPE + KV-pool store of Qwen3_8FullAttention.forward
+    (qwen3_8/full_attention.py:142-149, qwen3_8/rms_norm.py:19-24,
+    qwen3_8/rotary_embedding.py:46-95).  q [T, Hq, D], k/v [T, Hkv, D] (strided views allowed),
+    positions [T] or [3, T] int64, inv_freq the rotary module's fp32 buffer [rotary_dim/2].
+    Writes k/v into k_buffer/v_buffer at out_cache_loc and returns the rotated q [T, Hq, D]."""
+    dev = _need_cuda(q, k, v, q_norm_weight, k_norm_weight, positions, inv_freq, k_buffer,
+                     v_buffer, out_cache_loc)
+    if q.dim() != 3 or k.dim() != 3 or k.shape != v.shape or k_buffer.shape != v_buffer.shape:
+        raise ValueError(f"attn_prologue shapes: q {tuple(q.shape)} k {tuple(k.shape)} "
+                         f"v {tuple(v.shape)} pool {tuple(k_buffer.shape)}")
+    t, hq, d = q.shape
+    if k.shape[0] != t or k.shape[2] != d or k.shape[1:] != k_buffer.shape[1:]:
+        raise ValueError("attn_prologue: k/v rows must be [T, Hkv, D] matching the pool")
+    if q.stride(2) != 1 or k.stride(2) != 1 or v.stride(2) != 1 or k_buffer.stride(2) != 1 or \
+            k_buffer.stride() != v_buffer.stride():
+        raise ValueError("attn_prologue needs unit stride on head_dim and equal pool strides")
+    if len({q.dtype, k.dtype, v.dtype, k_buffer.dtype}) != 1:
+        raise TypeError("attn_prologue: q, k, v and the pools share a dtype")
+    if q_norm_weight.dtype != k_norm_weight.dtype or q_norm_weight.dtype not in (q.dtype,
+                                                                                torch.float32):
+        raise TypeError("attn_prologue: norm weights are float32 or of the activation dtype")
+    if q_norm_weight.numel() != d or k_norm_weight.numel() != d:
+        raise ValueError("norm weights must have head_dim entries")
+    if inv_freq.dtype != torch.float32 or inv_freq.dim() != 1 or not inv_freq.is_contiguous():
+        raise TypeError("inv_freq must be a contiguous float32 vector")
+    pos = _i64(positions, "positions")
+    if pos.dim() == 1:
+        rows, pstride = 1, 0
+        if pos.shape[0] != t:
+            raise ValueError("positions must have one entry per token")
+    elif pos.dim() == 2 and pos.shape[0] == 3 and pos.shape[1] == t:
+        if pos.stride(1) != 1:
+            pos = pos.contiguous()
+        rows, pstride = 3, pos.stride(0)
+    else:
+        raise ValueError(f"positions must be [T] or [3, T], got {tuple(pos.shape)}")
+    loc = _i64(out_cache_loc, "out_cache_loc")
+    if loc.numel() != t:
+        raise ValueError("out_cache_loc must have one entry per token")
+    if q_out is None:
+        q_out = torch.empty((t, hq, d), dtype=q.dtype, device=q.device)
+    qw, kw = q_norm_weight.contiguous(), k_norm_weight.contiguous()
+    a = C.AttnPrologueArgs(
+        q=q.data_ptr(), q_stride_tok=q.stride(0), q_stride_head=q.stride(1),
+        k=k.data_ptr(), k_stride_tok=k.stride(0), k_stride_head=k.stride(1),
+        v=v.data_ptr(), v_stride_tok=v.stride(0), v_stride_head=v.stride(1),
+        q_norm_weight=qw.data_ptr(), k_norm_weight=kw.data_ptr(),
+        positions=pos.data_ptr(), pos_stride=pstride, inv_freq=inv_freq.data_ptr(),
+        q_out=q_out.data_ptr(), q_out_stride_tok=q_out.stride(0),
+        q_out_stride_head=q_out.stride(1),
+        k_buffer=k_buffer.data_ptr(), v_buffer=v_buffer.data_ptr(),
+        buf_stride_slot=k_buffer.stride(0), buf_stride_head=k_buffer.stride(1),
+        num_slots=k_buffer.shape[0], out_cache_loc=loc.data_ptr(), num_tokens=t,
+        eps=float(eps), pos_rows=rows, mrope_section=(ctypes.c_int32 * 3)(*mrope_section),
+        mrope_interleaved=int(bool(mrope_interleaved)), rotary_dim=2 * inv_freq.numel(),
+        num_q_heads=hq, num_kv_heads=k.shape[1], head_dim=d, dtype=_dtype(q),
+        norm_weight_dtype=_dtype(qw), err=_ptr(err))
+    with torch.cuda.device(dev):
+        C.check("tf_attn_prologue", C.load().tf_attn_prologue(ctypes.byref(a), _stream(dev)))
+    del pos, loc, qw, kw
+    return q_out
+
+
 # ---------------------------------------------------------------------------------------------
 # a2-a4. paged attention
 # ---------------------------------------------------------------------------------------------
