@@ -33,12 +33,26 @@ def values(t, dtype: str) -> np.ndarray:
     return BF.as_f32(to_numpy(t), dtype)
 
 
+def bf16_step(x: np.ndarray) -> np.ndarray:
+    """Distance between adjacent bf16 values at |x| (2^(e-7) for |x| in [2^e, 2^(e+1)))."""
+    e = np.floor(np.log2(np.maximum(np.abs(x.astype(np.float64)), 2.0 ** -126)))
+    return np.exp2(e - 7)
+
+
 def assert_close_bf16(got: np.ndarray, ref: np.ndarray, max_abs=2e-2, mean_abs=2e-3, what=""):
-    """The hot path's bf16 tolerance against an fp32 evaluation: max-abs 2e-2, mean-abs 2e-3."""
+    """The hot path's bf16 tolerance: max-abs 2e-2, mean-abs 2e-3.
+
+    For |ref| >= 4 one bf16 step (2^-5 and up) is itself above 2e-2, so an element there passes
+    when it is within one step of the reference value; everywhere else the absolute bound holds.
+    """
     assert got.shape == ref.shape, (got.shape, ref.shape)
     assert np.isfinite(got).all(), f"{what}: non-finite output"
-    d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
-    assert d.max() <= max_abs, f"{what}: max-abs {d.max():.3g} > {max_abs}"
+    r = ref.astype(np.float64)
+    d = np.abs(got.astype(np.float64) - r)
+    bound = np.maximum(max_abs, bf16_step(r))
+    worst = int(np.argmax(d - bound))
+    assert (d <= bound).all(), (f"{what}: |diff| {d.ravel()[worst]:.3g} > {bound.ravel()[worst]:.3g}"
+                                f" at ref {r.ravel()[worst]:.4g} (max-abs {d.max():.3g})")
     assert d.mean() <= mean_abs, f"{what}: mean-abs {d.mean():.3g} > {mean_abs}"
 
 

@@ -79,8 +79,10 @@ def test_decode_batch_through_extend_path(name):
     b = values(_run(spec, t2, True, force_extend=True), dt)
     assert_close(a, b, dt, what="decode vs extend")
     np.testing.assert_array_equal(to_numpy(t1["conv_state"]), to_numpy(t2["conv_state"]))
-    np.testing.assert_allclose(to_numpy(t1["ssm_state"]), to_numpy(t2["ssm_state"]), rtol=1e-5,
-                               atol=1e-7)
+    # the extend path may run the state products on the tensor cores as three bf16 products
+    # (about 2^-16 relative each): the same bound as the golden extend comparisons
+    np.testing.assert_allclose(to_numpy(t1["ssm_state"]), to_numpy(t2["ssm_state"]), rtol=1e-4,
+                               atol=1e-5)
 
 
 def test_state_after_256_decode_steps_within_1e3():

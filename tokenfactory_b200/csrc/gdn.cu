@@ -18,8 +18,11 @@
 //   workspace and a second kernel rolls conv_state; the recurrent kernel then runs one CTA per
 //   (request, v-head) over the request's tokens with the state resident in registers, so the state
 //   costs one read and one write per request instead of per token.
+#include <type_traits>
+
 #include "common.cuh"
 #include "launch.h"
+#include "tcgen05.cuh"
 
 namespace tf {
 namespace gdn {
@@ -906,6 +909,600 @@ cudaError_t launch_decode_t(const tf_gdn_args& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------
+// a7 on the 5th-generation tensor cores (dk = dv = 128, bf16 activations): the same chunked WY form,
+// transposed so that the v dimension (128) is the MMA's M and lives on the TMEM lanes:
+//   X   = [K; Q] K^T        (M128 N64: rows 0-63 K K^T, rows 64-127 Q K^T)
+//   KS' = S' K^T,  QS' = S' Q^T     with S' = S^T [dv x dk] resident in TMEM across chunks
+//   U'  = solve of (I + Mk) against beta (V - e^g KS)^T, one dv row per thread, in registers
+//   O'  = e^g QS' + U' Mq^T,   S' = e^gC S' + U' Kd        (Kd = K o e^(gC - g))
+// Every product of fp32 values is computed as three bf16 MMAs, hi.hi + hi.lo + lo.hi with
+// x = hi + lo (hi = bf16(x), lo = bf16(x - hi)): about 2^-16 relative per product, which keeps the
+// state within 1e-5 of the fp32 recurrence over thousands of tokens.  TMEM (512 columns): S' fp32
+// 128, S' hi/lo as bf16 pairs 64 + 64, X 64, KS' 64, QS'/O' 64, U' hi/lo 32 + 32.
+// Roles: warps 0-3 own TMEM lanes (solve, mask building, rescales, output with the fused gated
+// RMSNorm), warps 4-7 load and split the chunk's q/k (normalised) into a SWIZZLE_128B [K; Q] stack,
+// v, z and the gates, warp 8 allocates TMEM and one of its threads issues the MMAs.
+// ---------------------------------------------------------------------------------------------
+namespace tc_chunk {
+
+constexpr int C = 64, D = 128;
+constexpr int kThreads = 288;
+constexpr int kKQBlk = 128 * 128;             // one 64-dim block of the [K; Q] stack (128 rows)
+constexpr int oKQH = 0, oKQL = 2 * kKQBlk;    // hi / lo stacks, 32 KB each
+constexpr int oV = 4 * kKQBlk;                // T [64][128] v rows
+constexpr int oZ = oV + C * D * 2;            // bf16 [64][128] z rows
+constexpr int oOT = oZ + C * D * 2;           // T [64][128] output rows (O' transposed, rounded)
+constexpr int oMk = oOT + C * D * 2;          // fp32 [64 j][64 i]: Mk transposed
+constexpr int oMqH = oMk + C * C * 4;         // bf16 [64 rows][128 B] K-major (SWIZZLE_128B)
+constexpr int oMqL = oMqH + C * 128;
+constexpr int oG = oMqL + C * 128;            // gamma [64], log2 units
+constexpr int oGr = oG + C * 4;               // raw g [64]
+constexpr int oB = oGr + C * 4;               // beta [64]
+constexpr int oBar = oB + C * 4;              // in_full p1 l1 p2 tm_free z_full chunk_free fin
+constexpr int oWords = oBar + 64;             // tmem holder, abort
+constexpr int oRaw = (oWords + 16 + 1023) & ~1023;  // next chunk's raw q, k, v, z rows (T)
+constexpr int kRawPart = C * D * 2;           // one [64][128] part in a 16-bit T
+constexpr int kSmem = oRaw + 4 * kRawPart + 1024;
+static_assert(kSmem <= 232448, "shared memory per CTA");
+constexpr int cS = 0, cSH = 128, cSL = 192, cX = 256, cY = 320, cZ = 384, cUH = 448, cUL = 480;
+static_assert(oMqH % 1024 == 0 && oMqL % 1024 == 0, "SWIZZLE_128B tiles are 1024-byte aligned");
+
+// 2^x (ex2.approx.ftz: relative error about 2^-22)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.red.and.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ bool waitb(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kSpinLimitNs) { *abort = 1; return false; }
+    }
+  }
+}
+// x = hi + lo in bf16, packed as the pair (x0, x1) of one 32-bit column / word
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  __nv_bfloat162 l = __floats2bfloat162_rn(x0 - __low2float(h), x1 - __high2float(h));
+  hi = *reinterpret_cast<uint32_t*>(&h);
+  lo = *reinterpret_cast<uint32_t*>(&l);
+}
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void sts_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, bool acc) {
+  tc::mma_bf16_ts(d, a, b, idesc, acc);
+}
+__device__ __forceinline__ void st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  float f[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]);
+  tc::st16(taddr, f);
+}
+
+// four consecutive 16-bit elements of a staged row (8-byte aligned) as floats, or zeros
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, bool live, float (&f)[4]) {
+  static_assert(sizeof(T) == 2, "16-bit rows");
+  uint2 u = live ? *reinterpret_cast<const uint2*>(p) : make_uint2(0u, 0u);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) f[j] = to_f(e[j]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, const int64_t* start,
+                                                               const T* conv_out) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023) & ~1023u;
+  unsigned char* sb = smem_raw + (base - raw_base);
+  float* MkT = reinterpret_cast<float*>(sb + oMk);
+  float* gam = reinterpret_cast<float*>(sb + oG);
+  float* graw = reinterpret_cast<float*>(sb + oGr);
+  float* bet = reinterpret_cast<float*>(sb + oB);
+  uint64_t* in_full = reinterpret_cast<uint64_t*>(sb + oBar);
+  uint64_t* p1 = in_full + 1;
+  uint64_t* l1 = in_full + 2;
+  uint64_t* p2 = in_full + 3;
+  uint64_t* tm_free = in_full + 4;     // S' hi / lo written and O' read out: phase 1 may run
+  uint64_t* z_full = in_full + 5;      // the chunk's z rows are in place
+  uint64_t* chunk_free = in_full + 6;  // the output rows are written: z may be replaced
+  uint64_t* fin = in_full + 7;         // every MMA of the CTA has completed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
+  volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
+
+  const int b = blockIdx.x / a.num_v_heads;
+  const int vh = blockIdx.x - b * a.num_v_heads;
+  const int kh = vh / (a.num_v_heads / a.num_k_heads);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int key_dim = a.num_k_heads * D;
+  const int conv_dim = 2 * key_dim + a.num_v_heads * D;
+  const int64_t slot = a.req_pool_indices[b];
+  if (slot < 0 || slot >= a.num_slots) return;  // recorded by the conv kernel
+  const int64_t t0 = start[b];
+  const int64_t E = clamp_extend(a, b, t0);
+  if (E <= 0) return;
+  const int nchunks = (int)((E + C - 1) / C);
+  float* st_g = a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * D * D;
+
+  if (tid == 0) {
+    mbar_init(in_full, 128);
+    mbar_init(p1, 1);
+    mbar_init(l1, 4);
+    mbar_init(p2, 1);
+    mbar_init(tm_free, 4);
+    mbar_init(z_full, 4);
+    mbar_init(chunk_free, 4);
+    mbar_init(fin, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) tc::tmem_alloc(tmem_holder, 512);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp >= 4 && warp < 8) {
+    // ============ loaders: the chunk's q/k (normalised, split), v, z and gates ============
+    // The next chunk's raw rows are copied into a staging area with cp.async (every copy in
+    // flight at once) while the current chunk computes; the split into the MMA layouts starts as
+    // soon as the lane warps release the working buffers.
+    const int lt = tid - 128, lw = warp - 4;
+    const float qscale = rsqrtf((float)D);
+    const T* zb = a.z ? reinterpret_cast<const T*>(a.z) + (int64_t)vh * D : nullptr;
+    const bool zvec = zb && ((reinterpret_cast<uintptr_t>(zb) | (uintptr_t)(a.z_stride_tok * 2)) & 15) == 0;
+    float g_next = 0.f, b_next = 0.f;
+    auto prefetch = [&](int ci) {
+      const int64_t c0 = (int64_t)ci * C;
+      const int c = (int)(E - c0 < C ? E - c0 : C);
+      // 64 rows x 4 parts x 16 pieces of 16 bytes, 32 per loader thread
+#pragma unroll 4
+      for (int n = 0; n < 32; ++n) {
+        const int e = lt + 128 * n;
+        const int i = e >> 6, part = (e >> 4) & 3, pc = e & 15;
+        const uint32_t dst = base + oRaw + part * kRawPart + (i * D + pc * 8) * 2;
+        if (i < c) {
+          const int64_t t = t0 + c0 + i;
+          if (part < 3) {
+            const int col = part == 0 ? kh * D : (part == 1 ? key_dim + kh * D : 2 * key_dim + vh * D);
+            cp_async16(dst, conv_out + t * conv_dim + col + pc * 8);
+          } else if (zvec) {
+            cp_async16(dst, zb + t * a.z_stride_tok + pc * 8);
+          } else if (zb) {
+            T* d = reinterpret_cast<T*>(sb + oRaw + part * kRawPart + (i * D + pc * 8) * 2);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) d[q] = zb[t * a.z_stride_tok + pc * 8 + q];
+          }
+        }
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (lt < C) {
+        g_next = 0.f;
+        b_next = 0.f;
+        if (lt < c) gate_values<T>(a, t0 + c0 + lt, vh, &g_next, &b_next);
+      }
+    };
+    prefetch(0);
+    bool ok = true;
+    for (int ci = 0; ci < nchunks && ok; ++ci) {
+      const int64_t c0 = (int64_t)ci * C;
+      const int c = (int)(E - c0 < C ? E - c0 : C);
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      // the stack, v rows and gates of the previous chunk are consumed once its last MMAs ran
+      ok = bar_and(2, 128, ci == 0 || waitb(p2, (ci - 1) & 1, abort));  // and the staging landed
+      if (!ok) break;
+      if (lt < C) {
+        graw[lt] = g_next;
+        bet[lt] = b_next;
+      }
+      const T* rq = reinterpret_cast<const T*>(sb + oRaw);
+      const T* rk = reinterpret_cast<const T*>(sb + oRaw + kRawPart);
+      const T* rv = reinterpret_cast<const T*>(sb + oRaw + 2 * kRawPart);
+      const T* rz = reinterpret_cast<const T*>(sb + oRaw + 3 * kRawPart);
+      const int d = 4 * lane;               // this lane's 4 elements of a row
+      const int blk = lane >> 4, ch = (lane & 15) >> 1, e8 = (lane & 1) * 4;
+#pragma unroll 4
+      for (int m = 0; m < 16; ++m) {
+        const int i = lw + 4 * m;
+        const bool live = i < c;
+        float q[4], k[4];
+        load4(rq + i * D + d, live, q);
+        load4(rk + i * D + d, live, k);
+        const uint2 v = live ? *reinterpret_cast<const uint2*>(rv + i * D + d) : make_uint2(0u, 0u);
+        float sq = 0.f, sk = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) { sq = fmaf(q[e], q[e], sq); sk = fmaf(k[e], k[e], sk); }
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        const float iq = qscale / fmaxf(sqrtf(sq), 1e-12f), ik = 1.0f / fmaxf(sqrtf(sk), 1e-12f);
+        uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
+        split2(k[0] * ik, k[1] * ik, kh0, kl0);
+        split2(k[2] * ik, k[3] * ik, kh1, kl1);
+        split2(q[0] * iq, q[1] * iq, qh0, ql0);
+        split2(q[2] * iq, q[3] * iq, qh1, ql1);
+        const int rk_ = i, rq_ = 64 + i;
+        const uint32_t ok_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rk_ & 7)) << 4) + e8 * 2;
+        const uint32_t oq_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rq_ & 7)) << 4) + e8 * 2;
+        sts_v2(base + oKQH + rk_ * 128 + ok_, kh0, kh1);
+        sts_v2(base + oKQL + rk_ * 128 + ok_, kl0, kl1);
+        sts_v2(base + oKQH + rq_ * 128 + oq_, qh0, qh1);
+        sts_v2(base + oKQL + rq_ * 128 + oq_, ql0, ql1);
+        sts_v2(base + oV + (i * D + d) * 2, v.x, v.y);
+      }
+      named_barrier(2, 128);  // graw complete
+      if (lw == 0) {  // gamma = inclusive cumulative sum of g over the chunk, in log2 units
+        const float g0 = graw[2 * lane] * kLog2e, g1 = graw[2 * lane + 1] * kLog2e;
+        float incl = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        gam[2 * lane] = incl - g1;
+        gam[2 * lane + 1] = incl;
+      }
+      tc::fence_proxy_async_smem();  // the [K; Q] stack is read by the tensor core
+      mbar_arrive(in_full);
+      // z rows once the previous chunk's output rows are written
+      if (!waitb(chunk_free, ci & 1, abort)) { ok = false; }
+      ok = bar_and(2, 128, ok);
+      if (!ok) break;
+#pragma unroll 4
+      for (int m = 0; m < 16; ++m) {
+        const int i = lw + 4 * m;
+        float z[4];
+        load4(rz + i * D + d, i < c && zb, z);
+        __nv_bfloat162 z01 = __floats2bfloat162_rn(z[0], z[1]), z23 = __floats2bfloat162_rn(z[2], z[3]);
+        sts_v2(base + oZ + (i * D + d) * 2, *reinterpret_cast<uint32_t*>(&z01), *reinterpret_cast<uint32_t*>(&z23));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(z_full);
+      named_barrier(2, 128);  // the staging is consumed before it is refilled
+      if (ci + 1 < nchunks) prefetch(ci + 1);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 8) {
+    // ============ MMA issue (one thread) ============
+    if (lane == 0) {
+      constexpr uint32_t idX = tc::idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idO = tc::idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, true);
+      const uint32_t kqh = base + oKQH, kql = base + oKQL;
+      for (int ci = 0; ci < nchunks; ++ci) {
+        if (!waitb(tm_free, ci & 1, abort) || !waitb(in_full, ci & 1, abort)) break;
+        tc::fence_proxy_async_smem();
+        tc::fence_after_sync();
+        // X = [K; Q] K^T, KS' = S' K^T, QS' = S' Q^T: each as hi.hi + hi.lo + lo.hi
+#pragma unroll 1
+        for (int part = 0; part < 3; ++part) {
+          const uint32_t aS = part == 2 ? kql : kqh;   // A of X (the stack)
+          const uint32_t bS = part == 1 ? kql : kqh;   // B (K or Q rows)
+          const uint32_t aT = tmem + (part == 2 ? cSL : cSH);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kKQBlk + (kk & 3) * 32;
+            const bool acc = part > 0 || kk > 0;
+            const uint64_t bK = tc::sw128_desc(bS + off, 16, 1024);
+            const uint64_t bQ = tc::sw128_desc(bS + off + 64 * 128, 16, 1024);
+            tc::mma_bf16(tmem + cX, tc::sw128_desc(aS + off, 16, 1024), bK, idX, acc);
+            mma_ts(tmem + cY, aT + kk * 8, bK, idX, acc);
+            mma_ts(tmem + cZ, aT + kk * 8, bQ, idX, acc);
+          }
+        }
+        tc::commit(p1);
+        if (!waitb(l1, ci & 1, abort)) break;
+        tc::fence_after_sync();
+        tc::fence_proxy_async_smem();
+        // O' += U' Mq^T (N = 64 tokens) and S' += U' Kd (N = 128 dk, Kd MN-major over the K rows)
+#pragma unroll 1
+        for (int part = 0; part < 3; ++part) {
+          const uint32_t aT = tmem + (part == 2 ? cUL : cUH);
+          const uint32_t mq = base + (part == 1 ? oMqL : oMqH);
+          const uint32_t kd = part == 1 ? kql : kqh;
+#pragma unroll
+          for (int kk = 0; kk < C / 16; ++kk) {
+            mma_ts(tmem + cZ, aT + kk * 8, tc::sw128_desc(mq + kk * 32, 16, 1024), idO, true);
+            mma_ts(tmem + cS, aT + kk * 8, tc::sw128_desc(kd + kk * 2048, kKQBlk, 1024), idS, true);
+          }
+        }
+        tc::commit(p2);
+      }
+      // every MMA issued has completed before TMEM is read for the last time or released
+      tc::commit(fin);
+    }
+    __syncwarp();
+  } else {
+    // ============ TMEM-lane warps: thread l owns dv row l of S', KS', O', U' ============
+    const int l = tid;
+    const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    {  // S' = S^T into TMEM, with its bf16 hi / lo split
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float sv[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) sv[k] = __ldcs(st_g + (size_t)(cc * 32 + k) * D + l);
+        tc::st32(lb + cS + cc * 32, sv);
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) split2(sv[2 * k], sv[2 * k + 1], hi[k], lo[k]);
+        st16u(lb + cSH + cc * 16, hi);
+        st16u(lb + cSL + cc * 16, lo);
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(tm_free);
+        mbar_arrive(chunk_free);
+      }
+    }
+    const T* wn = a.z ? reinterpret_cast<const T*>(a.norm_weight) + (a.norm_weight_len == D ? 0 : (int64_t)vh * D)
+                      : nullptr;
+    float wv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (wn) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wv[e] = to_f(wn[4 * lane + e]);
+    }
+    for (int ci = 0; ci < nchunks; ++ci) {
+      const int64_t c0 = (int64_t)ci * C;
+      const int c = (int)(E - c0 < C ? E - c0 : C);
+      ok = bar_and(1, 128, ok && waitb(in_full, ci & 1, abort) && waitb(p1, ci & 1, abort));
+      if (!ok) break;
+      tc::fence_after_sync();
+      // ---- rows of X: Mk (l < 64, stored transposed) or Mq (l >= 64, bf16 hi / lo K-major rows)
+      {
+        float x[64];
+        tc::ld32(lb + cX, *reinterpret_cast<float(*)[32]>(&x[0]));
+        tc::ld32(lb + cX + 32, *reinterpret_cast<float(*)[32]>(&x[32]));
+        tc::wait_ld();
+        const int i = l & 63;
+        const float gi = gam[i];
+        const float4* g4 = reinterpret_cast<const float4*>(gam);
+        if (l < 64) {
+          const float bi = bet[i];
+#pragma unroll
+          for (int j4 = 0; j4 < 16; ++j4) {
+            const float4 g = g4[j4];
+            const float gj[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 4 * j4 + e;
+              MkT[j * C + i] = j < i ? bi * ex2(gi - gj[e]) * x[j] : 0.f;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const float4 ga = g4[2 * c8], gb = g4[2 * c8 + 1];
+            const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+            uint32_t h[4], lo_[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j0 = 8 * c8 + 2 * e, j1 = j0 + 1;
+              const float m0 = j0 <= i ? ex2(gi - gj[2 * e]) * x[j0] : 0.f;
+              const float m1 = j1 <= i ? ex2(gi - gj[2 * e + 1]) * x[j1] : 0.f;
+              split2(m0, m1, h[e], lo_[e]);
+            }
+            const uint32_t off = i * 128 + ((uint32_t)(c8 ^ (i & 7)) << 4);
+            sts_v4(base + oMqH + off, h[0], h[1], h[2], h[3]);
+            sts_v4(base + oMqL + off, lo_[0], lo_[1], lo_[2], lo_[3]);
+          }
+        }
+      }
+      named_barrier(1, 128);
+      // ---- U' row l: (I + Mk) u = beta (v - e^g KS), right-looking: once u_j is final, every
+      //      later row takes its term at once (independent FMAs; column j of Mk is contiguous)
+      {
+        float u[64];
+        tc::ld32(lb + cY, *reinterpret_cast<float(*)[32]>(&u[0]));
+        tc::ld32(lb + cY + 32, *reinterpret_cast<float(*)[32]>(&u[32]));
+        tc::wait_ld();
+        const T* vr = reinterpret_cast<const T*>(sb + oV);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * D + l]) - ex2(gam[i]) * u[i]);
+#pragma unroll
+        for (int j = 0; j < 63; ++j) {
+          const float uj = u[j];
+#pragma unroll
+          for (int q4 = (j + 1) >> 2; q4 < 16; ++q4) {
+            const float4 m = *reinterpret_cast<const float4*>(MkT + j * C + 4 * q4);
+            if (4 * q4 + 0 > j) u[4 * q4 + 0] = fmaf(-m.x, uj, u[4 * q4 + 0]);
+            if (4 * q4 + 1 > j) u[4 * q4 + 1] = fmaf(-m.y, uj, u[4 * q4 + 1]);
+            if (4 * q4 + 2 > j) u[4 * q4 + 2] = fmaf(-m.z, uj, u[4 * q4 + 2]);
+            u[4 * q4 + 3] = fmaf(-m.w, uj, u[4 * q4 + 3]);
+          }
+        }
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) split2(u[32 * h + 2 * k], u[32 * h + 2 * k + 1], hi[k], lo[k]);
+          st16u(lb + cUH + 16 * h, hi);
+          st16u(lb + cUL + 16 * h, lo);
+        }
+      }
+      // ---- O' = e^g QS' (the MMA adds U' Mq^T), S' *= e^gC, Kd = K o e^(gC - g) in place
+      {
+        float zq[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tc::ld32(lb + cZ + 32 * h, zq);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) zq[k] *= ex2(gam[32 * h + k]);
+          tc::st32(lb + cZ + 32 * h, zq);
+        }
+        const float gC = gam[C - 1], eC = ex2(gC);
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          tc::ld32(lb + cS + 32 * cc, zq);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) zq[k] *= eC;
+          tc::st32(lb + cS + 32 * cc, zq);
+        }
+        const int i = l & 63, hb = l >> 6;
+        const float w = ex2(gC - gam[i]);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const uint32_t off = hb * kKQBlk + i * 128 + ((uint32_t)(c8 ^ (i & 7)) << 4);
+          const uint4 h4 = lds_v4(base + oKQH + off), l4 = lds_v4(base + oKQL + off);
+          const uint32_t hw[4] = {h4.x, h4.y, h4.z, h4.w}, lw4[4] = {l4.x, l4.y, l4.z, l4.w};
+          uint32_t nh[4], nl[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 hh = *reinterpret_cast<const __nv_bfloat162*>(&hw[e]);
+            const __nv_bfloat162 ll = *reinterpret_cast<const __nv_bfloat162*>(&lw4[e]);
+            split2((__low2float(hh) + __low2float(ll)) * w, (__high2float(hh) + __high2float(ll)) * w, nh[e], nl[e]);
+          }
+          sts_v4(base + oKQH + off, nh[0], nh[1], nh[2], nh[3]);
+          sts_v4(base + oKQL + off, nl[0], nl[1], nl[2], nl[3]);
+        }
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      tc::fence_proxy_async_smem();  // Mq and Kd are read by the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(l1);
+      ok = bar_and(1, 128, waitb(p2, ci & 1, abort));
+      if (!ok) break;
+      tc::fence_after_sync();
+      // ---- O' rounded to T into the transposed output rows, S' hi / lo for the next chunk; then
+      //      the next chunk's products may start while the output rows are written
+      T* ot = reinterpret_cast<T*>(sb + oOT);
+      {
+        float o[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tc::ld32(lb + cZ + 32 * h, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) ot[(32 * h + k) * D + l] = from_f<T>(o[k]);
+        }
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float sv[32];
+          tc::ld32(lb + cS + 32 * cc, sv);
+          tc::wait_ld();
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) split2(sv[2 * k], sv[2 * k + 1], hi[k], lo[k]);
+          st16u(lb + cSH + 16 * cc, hi);
+          st16u(lb + cSL + 16 * cc, lo);
+        }
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tm_free);
+      // ---- output rows: gated RMSNorm per token, two rows per pass
+      ok = bar_and(1, 128, waitb(z_full, ci & 1, abort));  // also: every O' row is in place
+      if (!ok) break;
+      {
+        const __nv_bfloat16* zs = reinterpret_cast<const __nv_bfloat16*>(sb + oZ);
+        T* outb = reinterpret_cast<T*>(a.out) + (t0 + c0) * a.out_stride_tok + (int64_t)vh * D + 4 * lane;
+        const bool ovec = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)(a.out_stride_tok * 2)) & 7) == 0;
+#pragma unroll 1
+        for (int i0 = warp; i0 < c; i0 += 8) {
+          const int i1 = i0 + 4;
+          const bool has1 = i1 < c;
+          float x0[4], x1[4], y0[4], y1[4];
+          load4(ot + i0 * D + 4 * lane, true, x0);
+          load4(ot + i1 * D + 4 * lane, has1, x1);
+          if (wn) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { s0 = fmaf(x0[e], x0[e], s0); s1 = fmaf(x1[e], x1[e], s1); }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+              s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            }
+            const float r0 = rsqrtf(s0 / (float)D + a.norm_eps), r1 = rsqrtf(s1 / (float)D + a.norm_eps);
+            const uint2 z0 = *reinterpret_cast<const uint2*>(zs + i0 * D + 4 * lane);
+            const uint2 z1 = has1 ? *reinterpret_cast<const uint2*>(zs + i1 * D + 4 * lane) : z0;
+            const __nv_bfloat16* z0e = reinterpret_cast<const __nv_bfloat16*>(&z0);
+            const __nv_bfloat16* z1e = reinterpret_cast<const __nv_bfloat16*>(&z1);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              y0[e] = wv[e] * (x0[e] * r0) * silu_f(__bfloat162float(z0e[e]));
+              y1[e] = wv[e] * (x1[e] * r1) * silu_f(__bfloat162float(z1e[e]));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { y0[e] = x0[e]; y1[e] = x1[e]; }
+          }
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            if (r == 1 && !has1) break;
+            const float* y = r == 0 ? y0 : y1;
+            T* out = outb + (int64_t)(r == 0 ? i0 : i1) * a.out_stride_tok;
+            if (ovec) {
+              T pk[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) pk[e] = from_f<T>(y[e]);
+              *reinterpret_cast<uint2*>(out) = *reinterpret_cast<const uint2*>(pk);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) out[e] = from_f<T>(y[e]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(chunk_free);
+    }
+    if (ok) {  // the state back to the pool
+      ok = waitb(fin, 0, abort);
+      tc::fence_after_sync();
+#pragma unroll 1
+      for (int cc = 0; cc < 4 && ok; ++cc) {
+        float sv[32];
+        tc::ld32(lb + cS + 32 * cc, sv);
+        tc::wait_ld();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) __stcs(st_g + (size_t)(cc * 32 + k) * D + l, sv[k]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && *abort) record_err(a.err, TF_KERR_TIMEOUT);
+  tc::fence_after_sync();
+  if (warp == 8) tc::tmem_dealloc(tmem, 512);
+}
+
+}  // namespace tc_chunk
+
 struct ExtWs {
   int64_t* start;  // [B+1]
   void* conv_out;  // [T, conv_dim] of T
@@ -934,6 +1531,15 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
   }
   dim3 rg((conv_dim + 255) / 256, a.batch_size);
   conv_state_roll_kernel<T><<<rg, 256, 0, s>>>(a, w.start);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && DK == 128 && DV == 128) {  // tcgen05
+    const size_t tsmem = tc_chunk::kSmem;
+    cudaError_t e = cudaFuncSetAttribute(tc_chunk::chunk_tc_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
+    if (e != cudaSuccess) return e;
+    tc_chunk::chunk_tc_kernel<T><<<a.batch_size * a.num_v_heads, tc_chunk::kThreads, tsmem, s>>>(
+        a, w.start, (const T*)w.conv_out);
+    return cudaGetLastError();
+  }
   if constexpr (DK == DV && (DK == 64 || DK == 128)) {  // a7: chunked form
     constexpr size_t csmem = ChunkLay<DK>::kBytes;
     cudaError_t e = cudaFuncSetAttribute(chunk_extend_kernel<T, DK>,
