@@ -520,7 +520,7 @@ def bench_extend(args, rank, world, dev):
                      "traffic": _profile_traffic("paged_extend_config4.md")},
         "gdn_extend": {"tok_per_s": T / gdn_s, "ms_per_step": gdn_s * 1e3,
                        "tflops_min_count": T * gdn_flops_tok / gdn_s / 1e12,
-                       "kernel": "tf_gdn_extend (varlen conv + chunked WY delta rule, C=64, fp32)"},
+                       "kernel": "tf_gdn_extend (varlen conv + chunked WY delta rule, C=64, tcgen05 with bf16x3 split products, fp32 state)"},
         "prologue": {"gb_per_s": pro_bytes / pro_s / 1e9, "ms_per_step": pro_s * 1e3,
                      "frac_of_hbm_peak": pro_bytes / pro_s / 1e9 / _peaks()[0], "peak_kind": _peaks()[1],
                      "bytes_per_launch": pro_bytes,

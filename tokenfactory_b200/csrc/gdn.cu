@@ -955,6 +955,8 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 constexpr float kLog2e = 1.4426950408889634f;
+// x * sigmoid(x) with an approximate division (no slow path; 0 below x = -87, as the exact value is)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
   uint32_t r;
@@ -1142,7 +1144,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         for (int e = 0; e < 4; ++e) { sq = fmaf(q[e], q[e], sq); sk = fmaf(k[e], k[e], sk); }
         sq = warp_sum(sq);
         sk = warp_sum(sk);
-        const float iq = qscale / fmaxf(sqrtf(sq), 1e-12f), ik = 1.0f / fmaxf(sqrtf(sk), 1e-12f);
+        // x / max(|x|, 1e-12) as x * rsqrt(max(|x|^2, 1e-24)): no division on this path
+        const float iq = qscale * rsqrtf(fmaxf(sq, 1e-24f)), ik = rsqrtf(fmaxf(sk, 1e-24f));
         uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
         split2(k[0] * ik, k[1] * ik, kh0, kl0);
         split2(k[2] * ik, k[3] * ik, kh1, kl1);
@@ -1193,6 +1196,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     // ============ MMA issue (one thread) ============
     if (lane == 0) {
       constexpr uint32_t idX = tc::idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idYZ = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(128, 64, false, false);
       constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, true);
       const uint32_t kqh = base + oKQH, kql = base + oKQL;
@@ -1210,11 +1214,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * kKQBlk + (kk & 3) * 32;
             const bool acc = part > 0 || kk > 0;
-            const uint64_t bK = tc::sw128_desc(bS + off, 16, 1024);
-            const uint64_t bQ = tc::sw128_desc(bS + off + 64 * 128, 16, 1024);
-            tc::mma_bf16(tmem + cX, tc::sw128_desc(aS + off, 16, 1024), bK, idX, acc);
-            mma_ts(tmem + cY, aT + kk * 8, bK, idX, acc);
-            mma_ts(tmem + cZ, aT + kk * 8, bQ, idX, acc);
+            const uint64_t bKQ = tc::sw128_desc(bS + off, 16, 1024);  // K rows, then Q rows
+            tc::mma_bf16(tmem + cX, tc::sw128_desc(aS + off, 16, 1024), bKQ, idX, acc);
+            mma_ts(tmem + cY, aT + kk * 8, bKQ, idYZ, acc);  // [KS' | QS'] over cY, cZ
           }
         }
         tc::commit(p1);
@@ -1454,8 +1456,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
             const __nv_bfloat16* z1e = reinterpret_cast<const __nv_bfloat16*>(&z1);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              y0[e] = wv[e] * (x0[e] * r0) * silu_f(__bfloat162float(z0e[e]));
-              y1[e] = wv[e] * (x1[e] * r1) * silu_f(__bfloat162float(z1e[e]));
+              y0[e] = wv[e] * (x0[e] * r0) * silu_fast(__bfloat162float(z0e[e]));
+              y1[e] = wv[e] * (x1[e] * r1) * silu_fast(__bfloat162float(z1e[e]));
             }
           } else {
 #pragma unroll
