@@ -491,10 +491,29 @@ def bench_extend(args, rank, world, dev):
         ops.attn_prologue(qg[..., :D], kp, vp, qnw, knw, pos_d, inv_freq, kb, vb, loc_d,
                           q_out=q_pro)
 
+    # GDN state snapshots at admission: every request restores its prefix's snapshot into its
+    # working slot, all 48 linear layers of the 27B shape (ReqToStatePool, [L, slots, ...] pools)
+    n_lin = 48
+    snap_conv = torch.randn((n_lin, 2 * B, conv_dim, K - 1), generator=g, device=dev, dtype=bf)
+    snap_ssm = torch.randn((n_lin, 2 * B, hv, dk, dv), generator=g, device=dev)
+    snap_src = torch.arange(B, 2 * B, dtype=torch.int64, device=dev)
+    snap_dst = torch.arange(0, B, dtype=torch.int64, device=dev)
+    snap_bytes = 2 * B * n_lin * (conv_dim * (K - 1) * 2 + hv * dk * dv * 4)
+
+    def snap_step():
+        ops.state_slots_copy(snap_conv, snap_ssm, snap_src, snap_dst)
+
+    def snap_step_torch():  # the reference's restore_snapshot: two torch copies per request
+        for b in range(B):
+            snap_conv[:, b].copy_(snap_conv[:, B + b])
+            snap_ssm[:, b].copy_(snap_ssm[:, B + b])
+
     with ClockSampler(torch.cuda.current_device()) as clk:
         attn_s = timed(attn_step, args.steps)
         gdn_s = timed(gdn_step, max(1, args.steps // 4))
         pro_s = timed(pro_step, args.steps)
+        snap_s = timed(snap_step, args.steps)
+        snap_torch_s = timed(snap_step_torch, max(1, args.steps // 4))
     pro_bytes = 2 * T * (hq + 2 * hkv) * D * 2 + 2 * T * 8
     Pf, Ef = P.double(), E.double()
     flops = float((4 * C4["Hq"] * D * (Ef * Pf + Ef * (Ef + 1) / 2)).sum())  # whole job
@@ -525,6 +544,12 @@ def bench_extend(args, rank, world, dev):
                      "frac_of_hbm_peak": pro_bytes / pro_s / 1e9 / _peaks()[0], "peak_kind": _peaks()[1],
                      "bytes_per_launch": pro_bytes,
                      "kernel": "tf_attn_prologue (q/k RMSNorm + partial RoPE + KV store)"},
+        "state_snapshot": {"gb_per_s": snap_bytes / snap_s / 1e9, "ms_per_step": snap_s * 1e3,
+                           "frac_of_hbm_peak": snap_bytes / snap_s / 1e9 / _peaks()[0],
+                           "peak_kind": _peaks()[1], "bytes_per_launch": snap_bytes,
+                           "restores": B, "linear_layers": n_lin,
+                           "torch_copies_ms": snap_torch_s * 1e3,
+                           "kernel": "tf_state_slots_copy (all layers, both pools, one launch)"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }

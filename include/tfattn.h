@@ -267,6 +267,44 @@ typedef struct tf_gated_rmsnorm_args {
 
 TF_API tf_status tf_gated_rmsnorm(const tf_gated_rmsnorm_args* args, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * GDN state-slot copies of ReqToStatePool (req_to_state_pool.py:120-194) for every linear layer at
+ * once.  For each op i, the conv_state and ssm_state rows of slot dst_slots[i] in all num_layers
+ * layers become a copy of slot src_slots[i]:
+ *   capture_snapshot(req, snap)  (req_to_state_pool.py:160-176)  src = req,  dst = snap
+ *   restore_snapshot(snap, req)  (req_to_state_pool.py:178-194)  src = snap, dst = req
+ * or zeros when src_slots[i] == -1:
+ *   reset_working_state(req)     (req_to_state_pool.py:120-127)  dst = req
+ *   free_snapshot(snap)          (req_to_state_pool.py:140-153)  dst = snap (the tensor part)
+ * The pools keep the reference's layout: conv_state [L, num_slots, conv_dim, K-1] and ssm_state
+ * [L, num_slots, Hv, dk, dv], each slot's rows of one layer contiguous (slot_elems elements).
+ * Byte copies, bit-exact; one launch covers every op, both pools and all layers.  Either pool may
+ * be NULL (skipped).  A slot outside [0, num_slots) (or a src other than -1 below 0) is recorded in
+ * `err` and its op skipped; src == dst is a no-op.  The ops of one call run concurrently: a batch
+ * in which one op's dst is another op's src or dst has an order-dependent result (the Python front
+ * end rejects such batches).
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_state_copy_args {
+  void* conv_state;            /* [L, num_slots, conv_dim, K-1], conv_dtype              */
+  int64_t conv_stride_layer;   /* elements between layers                                */
+  int64_t conv_stride_slot;    /* elements between slots                                 */
+  int64_t conv_slot_elems;     /* contiguous elements of one slot in one layer           */
+  int32_t conv_dtype;
+  void* ssm_state;             /* [L, num_slots, Hv, dk, dv], ssm_dtype                  */
+  int64_t ssm_stride_layer;
+  int64_t ssm_stride_slot;
+  int64_t ssm_slot_elems;
+  int32_t ssm_dtype;
+  int32_t num_layers;
+  int64_t num_slots;
+  const int64_t* src_slots;    /* [num_ops]; -1 = zero the destination                   */
+  const int64_t* dst_slots;    /* [num_ops]                                              */
+  int32_t num_ops;
+  int32_t* err;                /* optional device word                                   */
+} tf_state_copy_args;
+
+TF_API tf_status tf_state_slots_copy(const tf_state_copy_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

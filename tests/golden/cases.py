@@ -8,7 +8,7 @@ dimensions (heads 4/1, head_dim 32, GDN 2/6 heads with dk=dv=16; tests/test_hybr
 """
 
 import hashlib
-from typing import Dict
+from typing import Dict, List
 
 import numpy as np
 
@@ -266,3 +266,36 @@ def prologue_inputs(spec: dict) -> dict:
 def prologue_q(inp: dict, spec: dict) -> np.ndarray:
     """The q view of the case: the first half of each head's q_proj row when strided."""
     return inp["qg"][..., :spec["d"]] if spec.get("strided") else inp["qg"]
+
+
+# ---------------------------------------------------------------------------------------------
+# GDN state-slot snapshots (ReqToStatePool, req_to_state_pool.py:120-194)
+# ---------------------------------------------------------------------------------------------
+# A small pool (3 linear layers, 4 working + 3 snapshot slots) filled with seeded values, then a
+# script of the pool's calls.  ("alloc",) records the slot alloc_snapshot() returns; the others
+# name the method and its arguments as the scheduler and radix tree pass them.
+STATE_POOL_SCRIPT: List[tuple] = [
+    ("alloc",), ("capture", 0, 4, "node_A"), ("alloc",), ("capture", 1, 5, None),
+    ("restore", 4, 2), ("reset", 1), ("alloc",), ("capture", 2, 6, None), ("free", 5),
+    ("restore", 6, 3), ("free", 4), ("alloc",), ("capture", 3, 4, "node_B"), ("reset", 0),
+    ("restore", 4, 1),
+]
+
+STATE_POOL_CASES: Dict[str, dict] = {
+    "pool_bf16_conv_f32_ssm": dict(max_reqs=4, max_snapshots=3, layers=3, nk=2, nv=4, dk=16,
+                                   dv=16, kc=4, dtype="bf16", seed=80),
+}
+
+
+def state_pool_inputs(spec: dict) -> dict:
+    """Initial contents of the pool's two tensors: conv_state [L, slots, conv_dim, K-1] in the
+    pool dtype and ssm_state [L, slots, Hv, dk, dv] fp32 (the reference allocates them zeroed;
+    the cases fill every slot so that copies and resets are visible)."""
+    rng = np.random.default_rng(spec["seed"])
+    slots = spec["max_reqs"] + spec["max_snapshots"]
+    conv_dim = 2 * spec["nk"] * spec["dk"] + spec["nv"] * spec["dv"]
+    return dict(
+        conv_state=_bf.store(_normal(rng, (spec["layers"], slots, conv_dim, spec["kc"] - 1)),
+                             spec["dtype"]),
+        ssm_state=_normal(rng, (spec["layers"], slots, spec["nv"], spec["dk"], spec["dv"]), 0.02),
+    )

@@ -53,3 +53,12 @@ def prologue_case(name: str):
     assert bytes(z[f"{name}/checksum"]).decode() == C.checksum(inp), f"input drift in {name}"
     gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
     return spec, inp, gold
+
+
+def state_pool_case(name: str):
+    spec = C.STATE_POOL_CASES[name]
+    inp = C.state_pool_inputs(spec)
+    z = _npz("state_pool_golden.npz")
+    assert bytes(z[f"{name}/checksum"]).decode() == C.checksum(inp), f"input drift in {name}"
+    gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
+    return spec, inp, gold

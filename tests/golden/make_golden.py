@@ -3,7 +3,7 @@
     python tests/golden/make_golden.py --reference <path to a yz29528/tokenFactory checkout>
 
 Needs the reference's Python package importable on the CPU (torch only); writes
-tests/golden/attention_golden.npz and tests/golden/gdn_golden.npz.  Inputs come from
+tests/golden/*_golden.npz.  Inputs come from
 tests/golden/cases.py (seeded numpy), so the fixtures store outputs and an input checksum only.
 
 Reference functions exercised (paths inside the reference project):
@@ -19,6 +19,7 @@ Reference functions exercised (paths inside the reference project):
   Qwen3_8RMSNorm.forward (q_norm / k_norm)     qwen3_8/rms_norm.py:19-24
   PartialRotaryEmbedding.forward               qwen3_8/rotary_embedding.py:46-95
   the pool write of Qwen3_8FullAttention       qwen3_8/full_attention.py:147-149
+  ReqToStatePool snapshot calls                req_to_state_pool.py:34-194
 """
 
 import argparse
@@ -259,19 +260,58 @@ def prologue_golden(ref) -> dict:
     return out
 
 
+def state_pool_golden(ref) -> dict:
+    """ReqToStatePool built from a Qwen3_8Config, its tensors filled with the case's values, then
+    STATE_POOL_SCRIPT applied through the reference's own methods (req_to_state_pool.py:34-194)."""
+    from qwen3_8 import Qwen3_8Config
+    from req_to_state_pool import ReqToStatePool
+
+    from oracle.state_pool import bookkeeping, run_script
+
+    out = {}
+    for name, spec in C.STATE_POOL_CASES.items():
+        inp = C.state_pool_inputs(spec)
+        cfg = Qwen3_8Config(num_hidden_layers=spec["layers"] + 1,
+                            layer_types=["linear_attention"] * spec["layers"] + ["full_attention"],
+                            linear_num_key_heads=spec["nk"], linear_num_value_heads=spec["nv"],
+                            linear_key_head_dim=spec["dk"], linear_value_head_dim=spec["dv"],
+                            linear_conv_kernel_dim=spec["kc"])
+        pool = ReqToStatePool(spec["max_reqs"], spec["max_snapshots"], config=cfg, device="cpu",
+                              dtype=_tdt(spec["dtype"]))
+        assert tuple(pool.conv_state.shape) == inp["conv_state"].shape
+        assert tuple(pool.ssm_state.shape) == inp["ssm_state"].shape
+        with torch.inference_mode():
+            pool.conv_state.copy_(_t(inp["conv_state"], spec["dtype"]))
+            pool.ssm_state.copy_(_t(inp["ssm_state"], "f32"))
+        allocs = run_script(pool, C.STATE_POOL_SCRIPT)
+        free, occ, tags = bookkeeping(pool)
+        out[f"{name}/conv_state"] = _np(pool.conv_state)
+        out[f"{name}/ssm_state"] = _np(pool.ssm_state)
+        out[f"{name}/allocs"] = np.asarray([-1 if a is None else a for a in allocs], np.int64)
+        out[f"{name}/free_slots"] = np.asarray(free, np.int64)
+        out[f"{name}/occupied"] = np.asarray(occ, np.bool_)
+        out[f"{name}/tags"] = np.asarray(tags)
+        out[f"{name}/checksum"] = np.frombuffer(C.checksum(inp).encode(), dtype=np.uint8)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True,
                     help="root of a yz29528/tokenFactory checkout (its qwen3_8 package)")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="fixture names to regenerate (attention gdn module prologue state_pool)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.manual_seed(0)
-    np.savez_compressed(os.path.join(HERE, "attention_golden.npz"), **attention_golden(args))
-    np.savez_compressed(os.path.join(HERE, "gdn_golden.npz"), **gdn_golden(args))
-    np.savez_compressed(os.path.join(HERE, "module_golden.npz"), **module_golden(args))
-    np.savez_compressed(os.path.join(HERE, "prologue_golden.npz"), **prologue_golden(args))
-    for f in ("attention_golden.npz", "gdn_golden.npz", "module_golden.npz", "prologue_golden.npz"):
-        print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+    makers = dict(attention=attention_golden, gdn=gdn_golden, module=module_golden,
+                  prologue=prologue_golden, state_pool=state_pool_golden)
+    for name, make in makers.items():
+        if args.only is not None and name not in args.only:
+            continue
+        f = os.path.join(HERE, f"{name}_golden.npz")
+        np.savez_compressed(f, **make(args))
+        print(os.path.basename(f), os.path.getsize(f), "bytes")
 
 
 if __name__ == "__main__":

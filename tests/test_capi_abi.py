@@ -61,6 +61,7 @@ _STRUCTS = {
     "tf_paged_attn_args": "PagedAttnArgs",
     "tf_gdn_args": "GdnArgs",
     "tf_gated_rmsnorm_args": "GatedRMSNormArgs",
+    "tf_state_copy_args": "StateCopyArgs",
 }
 
 
@@ -104,3 +105,29 @@ def test_prologue_rejects_unbuilt_rotary_dims_without_a_gpu():
     p.mrope_section[0], p.mrope_section[1], p.mrope_section[2] = 11, 11, 11
     assert lib.tf_attn_prologue(ctypes.byref(p), None) == _capi.TF_ERR_INVALID_ARG
     assert b"mrope_section" in lib.tf_last_error()
+
+
+def test_state_slots_copy_checks_without_a_gpu():
+    """tf_state_slots_copy validates before any CUDA call (fake non-NULL pointers): missing slot
+    lists, overlapping slot rows and unknown dtypes are rejected; empty work is a no-op."""
+    from tokenfactory_b200 import _capi
+    lib = _capi.load()
+    fake = 0x1000
+    base = dict(conv_state=fake, conv_stride_layer=7 * 96, conv_stride_slot=96, conv_slot_elems=96,
+                conv_dtype=1, ssm_state=fake, ssm_stride_layer=7 * 1024, ssm_stride_slot=1024,
+                ssm_slot_elems=1024, ssm_dtype=0, num_layers=3, num_slots=7, num_ops=2)
+    a = _capi.StateCopyArgs(**base)
+    assert lib.tf_state_slots_copy(ctypes.byref(a), None) == _capi.TF_ERR_INVALID_ARG
+    assert b"slot lists" in lib.tf_last_error()
+    a = _capi.StateCopyArgs(**{**base, "src_slots": fake, "dst_slots": fake,
+                               "ssm_stride_layer": 2048})
+    assert lib.tf_state_slots_copy(ctypes.byref(a), None) == _capi.TF_ERR_INVALID_ARG
+    assert b"overlap" in lib.tf_last_error()
+    a = _capi.StateCopyArgs(**{**base, "src_slots": fake, "dst_slots": fake, "conv_dtype": 9})
+    assert lib.tf_state_slots_copy(ctypes.byref(a), None) == _capi.TF_ERR_INVALID_ARG
+    assert b"dtype" in lib.tf_last_error()
+    a = _capi.StateCopyArgs(**{**base, "src_slots": fake, "dst_slots": fake, "conv_slot_elems": 97})
+    assert lib.tf_state_slots_copy(ctypes.byref(a), None) == _capi.TF_ERR_INVALID_ARG
+    for empty in ({"num_ops": 0}, {"num_layers": 0}, {"conv_state": None, "ssm_state": None}):
+        a = _capi.StateCopyArgs(**{**base, **empty})
+        assert lib.tf_state_slots_copy(ctypes.byref(a), None) == _capi.TF_OK

@@ -104,6 +104,18 @@ class GatedRMSNormArgs(ctypes.Structure):
     ]
 
 
+class StateCopyArgs(ctypes.Structure):
+    _fields_ = [
+        ("conv_state", _vp), ("conv_stride_layer", _i64), ("conv_stride_slot", _i64),
+        ("conv_slot_elems", _i64), ("conv_dtype", _i32),
+        ("ssm_state", _vp), ("ssm_stride_layer", _i64), ("ssm_stride_slot", _i64),
+        ("ssm_slot_elems", _i64), ("ssm_dtype", _i32),
+        ("num_layers", _i32), ("num_slots", _i64),
+        ("src_slots", _vp), ("dst_slots", _vp), ("num_ops", _i32),
+        ("err", _vp),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point, in header order
 SIGNATURES = [
     ("tf_abi_version", ctypes.c_int, []),
@@ -120,6 +132,7 @@ SIGNATURES = [
     ("tf_gdn_extend_workspace_size", ctypes.c_size_t, [ctypes.POINTER(GdnArgs)]),
     ("tf_gdn_extend", _i32, [ctypes.POINTER(GdnArgs), _vp, ctypes.c_size_t, _vp]),
     ("tf_gated_rmsnorm", _i32, [ctypes.POINTER(GatedRMSNormArgs), _vp]),
+    ("tf_state_slots_copy", _i32, [ctypes.POINTER(StateCopyArgs), _vp]),
 ]
 
 _lib = None

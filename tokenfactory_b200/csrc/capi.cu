@@ -148,6 +148,20 @@ static tf_status check_gdn(const tf_gdn_args* a, bool decode) {
 
 using namespace tf;
 
+// One pool of tf_state_copy_args: each (layer, slot) block of `elems` elements must be disjoint
+// from every other, which holds for the layer-major and the slot-major layouts.
+static const char* state_pool_problem(const void* base, int64_t stride_layer, int64_t stride_slot,
+                                      int64_t elems, int32_t dtype, int32_t layers, int64_t slots) {
+  if (!base) return nullptr;
+  if (!dtype_ok(dtype)) return "unknown dtype";
+  if (elems <= 0 || stride_layer <= 0 || stride_slot <= 0) return "non-positive extent or stride";
+  if (stride_slot < elems || stride_layer < elems) return "a stride is smaller than a slot's rows";
+  const bool layer_major = stride_layer >= slots * stride_slot;
+  const bool slot_major = stride_slot >= (int64_t)layers * stride_layer;
+  if (layers > 1 && slots > 1 && !layer_major && !slot_major) return "slot rows overlap";
+  return nullptr;
+}
+
 extern "C" {
 
 int tf_abi_version(void) { return TFATTN_ABI_VERSION; }
@@ -325,6 +339,27 @@ tf_status tf_gated_rmsnorm(const tf_gated_rmsnorm_args* a, void* stream) {
   DeviceGuard g(s);
   if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
   return cuda_status(launch_gated_rmsnorm(*a, s), "tf_gated_rmsnorm");
+}
+
+tf_status tf_state_slots_copy(const tf_state_copy_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->num_ops < 0 || a->num_layers < 0 || a->num_slots < 0)
+    return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->num_ops == 0 || a->num_layers == 0 || (!a->conv_state && !a->ssm_state)) return TF_OK;
+  if (!a->src_slots || !a->dst_slots) return fail(TF_ERR_INVALID_ARG, "slot lists are NULL");
+  if (a->num_slots == 0) return fail(TF_ERR_INVALID_ARG, "empty pool");
+  if (const char* e = state_pool_problem(a->conv_state, a->conv_stride_layer, a->conv_stride_slot,
+                                         a->conv_slot_elems, a->conv_dtype, a->num_layers,
+                                         a->num_slots))
+    return fail(TF_ERR_INVALID_ARG, "conv_state: %s", e);
+  if (const char* e = state_pool_problem(a->ssm_state, a->ssm_stride_layer, a->ssm_stride_slot,
+                                         a->ssm_slot_elems, a->ssm_dtype, a->num_layers,
+                                         a->num_slots))
+    return fail(TF_ERR_INVALID_ARG, "ssm_state: %s", e);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_state_slots_copy(*a, s), "tf_state_slots_copy");
 }
 
 }  // extern "C"

@@ -40,6 +40,9 @@ cudaError_t launch_gdn_extend(const tf_gdn_args& a, void* ws, size_t ws_bytes, c
 // rmsnorm.cu
 cudaError_t launch_gated_rmsnorm(const tf_gated_rmsnorm_args& a, cudaStream_t s);
 
+// state_copy.cu: GDN state-slot snapshot copies / resets for all layers in one launch
+cudaError_t launch_state_slots_copy(const tf_state_copy_args& a, cudaStream_t s);
+
 // capi.cu
 int device_sm_count();
 

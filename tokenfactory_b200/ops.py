@@ -373,3 +373,78 @@ def gated_rmsnorm(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, head_d
     with torch.cuda.device(dev):
         C.check("tf_gated_rmsnorm", C.load().tf_gated_rmsnorm(ctypes.byref(args), _stream(dev)))
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# GDN state-slot snapshots: copies / resets of every linear layer's rows in one launch
+# ---------------------------------------------------------------------------------------------
+def _slot_rows(pool: Optional[torch.Tensor], name: str):
+    """(pointer, layer stride, slot stride, elements per slot, dtype) of a [L, slots, ...] pool."""
+    if pool is None:
+        return None, 0, 0, 0, C.TF_DTYPE_F32
+    if pool.dim() < 2:
+        raise ValueError(f"{name} must be [layers, slots, ...], got {tuple(pool.shape)}")
+    if pool.numel() and not pool[0, 0].is_contiguous():
+        raise ValueError(f"{name}: the rows of one slot in one layer must be contiguous")
+    elems = 1
+    for d in pool.shape[2:]:
+        elems *= d
+    return pool.data_ptr(), pool.stride(0), pool.stride(1), elems, _dtype(pool)
+
+
+def state_slot_ops_valid(src, dst) -> None:
+    """The ops of one state_slots_copy call run concurrently: reject a batch whose result would
+    depend on their order (a destination written twice, or read by another op)."""
+    if len(src) != len(dst):
+        raise ValueError("src and dst lists differ in length")
+    dsts = [int(d) for d in dst]
+    if len(set(dsts)) != len(dsts):
+        raise ValueError(f"a destination slot appears twice: {dsts}")
+    for i, s in enumerate(src):
+        if s is not None and int(s) != dsts[i] and int(s) in set(dsts):
+            raise ValueError(f"slot {int(s)} is both read and written in one batch")
+
+
+def state_slots_copy(conv_state: Optional[torch.Tensor], ssm_state: Optional[torch.Tensor],
+                     src_slots, dst_slots, err: Optional[torch.Tensor] = None) -> None:
+    """For each op i: every layer's rows of slot dst_slots[i] in both pools become a copy of slot
+    src_slots[i] (ReqToStatePool.capture_snapshot / restore_snapshot,
+    req_to_state_pool.py:160-194), or zeros where the source is None / -1 (reset_working_state,
+    free_snapshot, req_to_state_pool.py:120-153).  One launch for all ops, layers and both pools.
+
+    conv_state [L, slots, conv_dim, K-1] and ssm_state [L, slots, Hv, dk, dv] as the reference
+    allocates them (either may be None).  The slot lists are host sequences (checked for order
+    dependence here, then copied to the device) or int64 CUDA tensors (used as they are)."""
+    pools = [p for p in (conv_state, ssm_state) if p is not None]
+    if not pools:
+        return
+    dev = _need_cuda(*pools)
+    L, S = pools[0].shape[0], pools[0].shape[1]
+    for p in pools[1:]:
+        if p.shape[0] != L or p.shape[1] != S:
+            raise ValueError("conv_state and ssm_state disagree on layers or slots")
+    if isinstance(src_slots, torch.Tensor) or isinstance(dst_slots, torch.Tensor):
+        src_t = _i64(src_slots, "src_slots")
+        dst_t = _i64(dst_slots, "dst_slots")
+        _need_cuda(src_t, dst_t)
+        if src_t.numel() != dst_t.numel():
+            raise ValueError("src_slots and dst_slots differ in length")
+    else:
+        state_slot_ops_valid(src_slots, dst_slots)
+        if not dst_slots:
+            return
+        host = torch.tensor([[-1 if s is None else int(s) for s in src_slots],
+                             [int(d) for d in dst_slots]], dtype=torch.int64).pin_memory()
+        both = host.to(dev, non_blocking=True)
+        src_t, dst_t = both[0], both[1]
+    n = dst_t.numel()
+    if n == 0:
+        return
+    cp, cl, cs, ce, cd = _slot_rows(conv_state, "conv_state")
+    sp, sl, ss, se, sd = _slot_rows(ssm_state, "ssm_state")
+    args = C.StateCopyArgs(
+        conv_state=cp, conv_stride_layer=cl, conv_stride_slot=cs, conv_slot_elems=ce,
+        conv_dtype=cd, ssm_state=sp, ssm_stride_layer=sl, ssm_stride_slot=ss, ssm_slot_elems=se,
+        ssm_dtype=sd, num_layers=L, num_slots=S, src_slots=src_t.data_ptr(),
+        dst_slots=dst_t.data_ptr(), num_ops=n, err=_ptr(err))
+    C.check("tf_state_slots_copy", C.load().tf_state_slots_copy(ctypes.byref(args), _stream(dev)))
