@@ -305,6 +305,48 @@ typedef struct tf_state_copy_args {
 
 TF_API tf_status tf_state_slots_copy(const tf_state_copy_args* args, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * Incremental sync of the device req_to_token table (ModelRunner._prepare_forward_batch,
+ * engine/model_runner.py:147-166): for each segment i, given as four int64 (row, col, len, src),
+ *   req_to_token[row, col : col + len] = values[src : src + len]
+ * One launch for every request of a step (the reference issues one host->device copy and one
+ * slice assignment per request).  Segments outside the table or the values array are recorded
+ * in `err` and skipped; segments must not overlap one another.
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_r2t_sync_args {
+  int64_t* req_to_token;       /* [r2t_rows, r2t_cols] int64                             */
+  int64_t r2t_stride;          /* elements between rows                                  */
+  int64_t r2t_rows, r2t_cols;
+  const int64_t* segments;     /* [num_segments, 4]: row, col, len, src                  */
+  int32_t num_segments;
+  const int64_t* values;       /* [num_values]                                           */
+  int64_t num_values;
+  int32_t* err;                /* optional device word                                   */
+} tf_r2t_sync_args;
+
+TF_API tf_status tf_req_to_token_sync(const tf_r2t_sync_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Batched next-token sampling (ModelRunner._sample / _sample_one, engine/model_runner.py:574-581)
+ * in one launch instead of one argmax or softmax + multinomial and one .item() per request.
+ * Row b: temperature[b] <= 1e-5 -> argmax of logits[b] (first maximum; a NaN counts as the
+ * maximum, as torch.argmax); otherwise the smallest index i with
+ *   sum_{j <= i} exp((x_j - max x) / T) > uniform[b] * sum_j exp((x_j - max x) / T)
+ * (inverse-CDF draw from softmax(x / T) with the caller's uniform in [0, 1); fp32 sums).
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_sample_args {
+  const void* logits;          /* [batch_size, vocab_size], dtype                        */
+  int64_t logits_stride;       /* elements between rows                                  */
+  int32_t batch_size;
+  int32_t vocab_size;
+  int32_t dtype;
+  const float* temperature;    /* [batch_size]                                           */
+  const float* uniform;        /* [batch_size]; NULL makes every row greedy              */
+  int64_t* out;                /* [batch_size] token ids                                 */
+} tf_sample_args;
+
+TF_API tf_status tf_sample_tokens(const tf_sample_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

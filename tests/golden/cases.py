@@ -299,3 +299,47 @@ def state_pool_inputs(spec: dict) -> dict:
                              spec["dtype"]),
         ssm_state=_normal(rng, (spec["layers"], slots, spec["nv"], spec["dk"], spec["dv"]), 0.02),
     )
+
+
+# ---------------------------------------------------------------------------------------------
+# per-step batch construction (ModelRunner._prepare_forward_batch, engine/model_runner.py:108-188)
+# ---------------------------------------------------------------------------------------------
+# Three steps over a 4-row req_to_token table: prefill chunks (row 2 starts after a 4-token radix
+# prefix the scheduler wrote into the host table), then decodes plus a new prefill, then a
+# rollback (dirty_from) that forces a stale prefix of row 0 to be re-synced.  Each request is
+# (req_pool_idx, cur_start_pos, chunk length, is_prefilled); token ids and slots are seeded.
+RUNNER_CASE = dict(max_reqs=4, max_ctx=48, seed=90, steps=[
+    dict(reqs=[(0, 0, 5, False), (2, 4, 3, False)], prefix={2: 4}),
+    dict(reqs=[(0, 5, 1, True), (2, 7, 1, True), (1, 0, 6, False)]),
+    dict(reqs=[(0, 6, 1, True), (1, 6, 1, True), (3, 0, 9, False)], dirty={0: 3},
+         rewrite={0: (3, 6)}),
+])
+
+
+def runner_script(case: dict = RUNNER_CASE):
+    """The steps as (requests, host req_to_token table before the step, dirty_from or None) with
+    the requests as plain dicts; the table evolves the way the scheduler writes it (prefix slots
+    before the step, the step's out_cache_loc after it, a rewrite for the rollback)."""
+    rng = np.random.default_rng(case["seed"])
+    table = [[-1] * case["max_ctx"] for _ in range(case["max_reqs"])]
+    steps = []
+    for st in case["steps"]:
+        for r, n in st.get("prefix", {}).items():
+            table[r][:n] = [int(x) for x in rng.integers(1, 10_000, n)]
+        for r, (a, b) in st.get("rewrite", {}).items():
+            table[r][a:b] = [int(x) for x in rng.integers(1, 10_000, b - a)]
+        reqs = []
+        for r, start, n, done in st["reqs"]:
+            reqs.append(dict(req_pool_idx=r, cur_start_pos=start, cur_seq_len=start + n,
+                             cur_chunk_tokens=[int(x) for x in rng.integers(0, 1000, n)],
+                             out_cache_loc=[int(x) for x in rng.integers(1, 10_000, n)],
+                             is_prefilled=done))
+        dirty = None
+        if "dirty" in st:
+            dirty = [10**9] * case["max_reqs"]
+            for r, p in st["dirty"].items():
+                dirty[r] = p
+        steps.append((reqs, [row[:] for row in table], dirty))
+        for q in reqs:
+            table[q["req_pool_idx"]][q["cur_start_pos"]:q["cur_seq_len"]] = q["out_cache_loc"]
+    return steps

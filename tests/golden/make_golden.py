@@ -20,6 +20,7 @@ Reference functions exercised (paths inside the reference project):
   PartialRotaryEmbedding.forward               qwen3_8/rotary_embedding.py:46-95
   the pool write of Qwen3_8FullAttention       qwen3_8/full_attention.py:147-149
   ReqToStatePool snapshot calls                req_to_state_pool.py:34-194
+  ModelRunner._prepare_forward_batch           engine/model_runner.py:108-188
 """
 
 import argparse
@@ -295,17 +296,50 @@ def state_pool_golden(ref) -> dict:
     return out
 
 
+def runner_golden(ref) -> dict:
+    """ModelRunner._prepare_forward_batch of the reference, run as an unbound method on a stand-in
+    holding the attributes it reads (device, req_to_token_tensor, _req_synced_lens)."""
+    from types import SimpleNamespace
+
+    from engine.model_runner import ModelRunner
+
+    case = C.RUNNER_CASE
+    me = SimpleNamespace(device="cpu", _req_synced_lens=[0] * case["max_reqs"],
+                         req_to_token_tensor=torch.full((case["max_reqs"], case["max_ctx"]), -1,
+                                                        dtype=torch.long))
+    out = {}
+    for i, (reqs, table, dirty) in enumerate(C.runner_script(case)):
+        objs = [SimpleNamespace(**r) for r in reqs]
+        d = None if dirty is None else list(dirty)
+        ids, pos, fb = ModelRunner._prepare_forward_batch(me, objs, table, d)
+        out[f"step{i}/input_ids"] = ids.numpy()
+        out[f"step{i}/positions"] = pos.numpy()
+        out[f"step{i}/out_cache_loc"] = fb.out_cache_loc.numpy()
+        out[f"step{i}/req_pool_indices"] = fb.req_pool_indices.numpy()
+        out[f"step{i}/seq_lens"] = fb.seq_lens.numpy()
+        out[f"step{i}/prefix_lens"] = fb.prefix_lens.numpy()
+        out[f"step{i}/extend_lens"] = fb.extend_lens_tensor.numpy()
+        out[f"step{i}/meta"] = np.asarray([fb.batch_size, int(fb.is_prefill), fb.max_seq_len,
+                                           fb.max_extend_len], np.int64)
+        out[f"step{i}/req_to_token"] = me.req_to_token_tensor.numpy().copy()
+        out[f"step{i}/synced_lens"] = np.asarray(me._req_synced_lens, np.int64)
+        if d is not None:
+            out[f"step{i}/dirty_from"] = np.asarray(d, np.int64)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True,
                     help="root of a yz29528/tokenFactory checkout (its qwen3_8 package)")
     ap.add_argument("--only", nargs="*", default=None,
-                    help="fixture names to regenerate (attention gdn module prologue state_pool)")
+                    help="fixture names to regenerate (attention gdn module prologue state_pool runner)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.manual_seed(0)
     makers = dict(attention=attention_golden, gdn=gdn_golden, module=module_golden,
-                  prologue=prologue_golden, state_pool=state_pool_golden)
+                  prologue=prologue_golden, state_pool=state_pool_golden,
+                  runner=runner_golden)
     for name, make in makers.items():
         if args.only is not None and name not in args.only:
             continue

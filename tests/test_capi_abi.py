@@ -62,6 +62,8 @@ _STRUCTS = {
     "tf_gdn_args": "GdnArgs",
     "tf_gated_rmsnorm_args": "GatedRMSNormArgs",
     "tf_state_copy_args": "StateCopyArgs",
+    "tf_r2t_sync_args": "R2TSyncArgs",
+    "tf_sample_args": "SampleArgs",
 }
 
 

@@ -116,6 +116,23 @@ class StateCopyArgs(ctypes.Structure):
     ]
 
 
+class R2TSyncArgs(ctypes.Structure):
+    _fields_ = [
+        ("req_to_token", _vp), ("r2t_stride", _i64), ("r2t_rows", _i64), ("r2t_cols", _i64),
+        ("segments", _vp), ("num_segments", _i32),
+        ("values", _vp), ("num_values", _i64),
+        ("err", _vp),
+    ]
+
+
+class SampleArgs(ctypes.Structure):
+    _fields_ = [
+        ("logits", _vp), ("logits_stride", _i64),
+        ("batch_size", _i32), ("vocab_size", _i32), ("dtype", _i32),
+        ("temperature", _vp), ("uniform", _vp), ("out", _vp),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point, in header order
 SIGNATURES = [
     ("tf_abi_version", ctypes.c_int, []),
@@ -133,6 +150,8 @@ SIGNATURES = [
     ("tf_gdn_extend", _i32, [ctypes.POINTER(GdnArgs), _vp, ctypes.c_size_t, _vp]),
     ("tf_gated_rmsnorm", _i32, [ctypes.POINTER(GatedRMSNormArgs), _vp]),
     ("tf_state_slots_copy", _i32, [ctypes.POINTER(StateCopyArgs), _vp]),
+    ("tf_req_to_token_sync", _i32, [ctypes.POINTER(R2TSyncArgs), _vp]),
+    ("tf_sample_tokens", _i32, [ctypes.POINTER(SampleArgs), _vp]),
 ]
 
 _lib = None

@@ -33,10 +33,15 @@ tf_status cuda_status(cudaError_t e, const char* what) {
 // Runs the launch on the stream's device, restoring the caller's current device afterwards.
 class DeviceGuard {
  public:
+  // A stream being captured into a CUDA graph belongs to the capturing thread's current device,
+  // and cudaStreamGetDevice on it invalidates the capture: query it only when not capturing.
   explicit DeviceGuard(cudaStream_t s) {
     ok_ = cudaGetDevice(&prev_) == cudaSuccess;
     int dev = prev_;
-    if (ok_ && s != nullptr && cudaStreamGetDevice(s, &dev) == cudaSuccess && dev != prev_) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (ok_ && s != nullptr && cudaStreamIsCapturing(s, &cap) == cudaSuccess &&
+        cap == cudaStreamCaptureStatusNone && cudaStreamGetDevice(s, &dev) == cudaSuccess &&
+        dev != prev_) {
       ok_ = cudaSetDevice(dev) == cudaSuccess;
       switched_ = ok_;
     }
@@ -360,6 +365,35 @@ tf_status tf_state_slots_copy(const tf_state_copy_args* a, void* stream) {
   DeviceGuard g(s);
   if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
   return cuda_status(launch_state_slots_copy(*a, s), "tf_state_slots_copy");
+}
+
+tf_status tf_req_to_token_sync(const tf_r2t_sync_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->num_segments < 0 || a->num_values < 0) return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->num_segments == 0) return TF_OK;
+  if (!a->req_to_token || !a->segments || (a->num_values > 0 && !a->values))
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (a->r2t_rows <= 0 || a->r2t_cols <= 0 || a->r2t_stride < a->r2t_cols)
+    return fail(TF_ERR_INVALID_ARG, "bad req_to_token shape or stride");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_req_to_token_sync(*a, s), "tf_req_to_token_sync");
+}
+
+tf_status tf_sample_tokens(const tf_sample_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->batch_size < 0) return fail(TF_ERR_INVALID_ARG, "negative batch size");
+  if (a->batch_size == 0) return TF_OK;
+  if (a->vocab_size <= 0 || a->logits_stride < a->vocab_size)
+    return fail(TF_ERR_INVALID_ARG, "bad vocab size or row stride");
+  if (!a->logits || !a->temperature || !a->out)
+    return fail(TF_ERR_INVALID_ARG, "a required tensor pointer is NULL");
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_sample_tokens(*a, s), "tf_sample_tokens");
 }
 
 }  // extern "C"

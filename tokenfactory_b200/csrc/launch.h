@@ -43,6 +43,10 @@ cudaError_t launch_gated_rmsnorm(const tf_gated_rmsnorm_args& a, cudaStream_t s)
 // state_copy.cu: GDN state-slot snapshot copies / resets for all layers in one launch
 cudaError_t launch_state_slots_copy(const tf_state_copy_args& a, cudaStream_t s);
 
+// runtime.cu: per-step req_to_token sync and batched sampling
+cudaError_t launch_req_to_token_sync(const tf_r2t_sync_args& a, cudaStream_t s);
+cudaError_t launch_sample_tokens(const tf_sample_args& a, cudaStream_t s);
+
 // capi.cu
 int device_sm_count();
 

@@ -448,3 +448,49 @@ def state_slots_copy(conv_state: Optional[torch.Tensor], ssm_state: Optional[tor
         ssm_dtype=sd, num_layers=L, num_slots=S, src_slots=src_t.data_ptr(),
         dst_slots=dst_t.data_ptr(), num_ops=n, err=_ptr(err))
     C.check("tf_state_slots_copy", C.load().tf_state_slots_copy(ctypes.byref(args), _stream(dev)))
+
+
+# ---------------------------------------------------------------------------------------------
+# per-step runtime: req_to_token sync and batched sampling
+# ---------------------------------------------------------------------------------------------
+def req_to_token_sync(req_to_token: torch.Tensor, segments: torch.Tensor, values: torch.Tensor,
+                      err: Optional[torch.Tensor] = None) -> None:
+    """req_to_token[row, col:col+len] = values[src:src+len] for every (row, col, len, src) row of
+    segments [n, 4] int64 (the incremental sync of ModelRunner._prepare_forward_batch,
+    engine/model_runner.py:147-166), one launch."""
+    dev = _need_cuda(req_to_token, segments, values)
+    if req_to_token.dtype != torch.int64 or req_to_token.dim() != 2 or req_to_token.stride(1) != 1:
+        raise ValueError("req_to_token must be a row-major [rows, cols] int64 tensor")
+    segments, values = _i64(segments, "segments"), _i64(values, "values")
+    if segments.dim() != 2 or segments.shape[1] != 4:
+        raise ValueError("segments must be [n, 4] (row, col, len, src)")
+    args = C.R2TSyncArgs(
+        req_to_token=req_to_token.data_ptr(), r2t_stride=req_to_token.stride(0),
+        r2t_rows=req_to_token.shape[0], r2t_cols=req_to_token.shape[1],
+        segments=segments.data_ptr(), num_segments=segments.shape[0],
+        values=values.data_ptr(), num_values=values.numel(), err=_ptr(err))
+    C.check("tf_req_to_token_sync", C.load().tf_req_to_token_sync(ctypes.byref(args), _stream(dev)))
+
+
+def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor,
+                  uniform: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Next token of every row of logits [B, V] (ModelRunner._sample_one,
+    engine/model_runner.py:574-578): argmax where temperature <= 1e-5 (or uniform is None), else
+    the inverse-CDF draw of softmax(logits / T) at uniform[b] in [0, 1).  Returns int64 [B]."""
+    dev = _need_cuda(logits, temperature, uniform, out)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be [B, V] with contiguous rows")
+    B, V = logits.shape
+    if temperature.dtype != torch.float32 or temperature.numel() != B:
+        raise ValueError("temperature must be float32 [B]")
+    if uniform is not None and (uniform.dtype != torch.float32 or uniform.numel() != B):
+        raise ValueError("uniform must be float32 [B]")
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=dev)
+    args = C.SampleArgs(logits=logits.data_ptr(), logits_stride=logits.stride(0), batch_size=B,
+                        vocab_size=V, dtype=_dtype(logits),
+                        temperature=temperature.contiguous().data_ptr(), uniform=_ptr(uniform),
+                        out=out.data_ptr())
+    C.check("tf_sample_tokens", C.load().tf_sample_tokens(ctypes.byref(args), _stream(dev)))
+    return out
