@@ -92,14 +92,39 @@ _REASONS = {
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+    """SM clocks and throttle reasons sampled while the timed region runs: NVML read every
+    2 ms from a thread (so that even a region of a few milliseconds is covered), with
+    nvidia-smi at 100 ms as the fallback when NVML cannot be loaded.  Reads only."""
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _nvml_loop(self, handle, nv):
+        mx = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.lines.append(f"{sm}, {mx}, 0, {bits:#x}")
+            except Exception:  # noqa: BLE001 - a failed read is just a missing sample
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            idx = torch.cuda._get_nvml_device_index(self.gpu)
+            handle = nv.nvmlDeviceGetHandleByIndex(idx)
+            self._thread = threading.Thread(target=self._nvml_loop, args=(handle, nv), daemon=True)
+            self._thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - no NVML: fall back to nvidia-smi
+            self._thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu),
@@ -116,6 +141,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -292,6 +320,28 @@ def bench_decode(args, rank, world, dev):
     _barrier(world)
     e2e_s = _max_over_ranks(s0.elapsed_time(s1) / 1e3, world)
 
+    # the same e2e step captured once as a CUDA graph (runner.CapturedStep): the copies from the
+    # pinned host buffers, the KV store, the decode and the copy back replay as one graph
+    from tokenfactory_b200.runner import CapturedStep
+
+    def e2e_body():
+        e2e_step()
+        return None
+
+    cap = CapturedStep(lambda: e2e_body(), {}, warmup=max(3, args.warmup))
+    _barrier(world)
+    torch.cuda.synchronize()
+    s0.record(stream)
+    for _ in range(args.steps):
+        cap()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_graph_s = _max_over_ranks(s0.elapsed_time(s1) / 1e3, world)
+    del cap
+
+    rt = _step_runtime(B, dev, stream)
+
     traffic = _profile_traffic("paged_decode_config2.md")
     res = {
         "metric": METRIC, "value": B * args.steps / elapsed, "unit": "tok/s",
@@ -311,12 +361,82 @@ def bench_decode(args, rank, world, dev):
                      "bytes_per_launch": nbytes,
                      "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
                      "traffic": traffic},
-        "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "e2e": {"value": B * args.steps / e2e_graph_s, "unit": "tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "how": "per step: 7 copies from pinned host buffers, KV store, paged decode, "
+                       "copy of the output to pinned host memory, replayed as one CUDA graph "
+                       "(runner.CapturedStep)"},
+        "e2e_eager": {"value": B * args.steps / e2e_s, "unit": "tok/s",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "how": "the same step issued call by call from Python"},
+        "step_runtime": rt,
         "gpu_launches": 4 * args.steps,
         "clocks": clk.summary(),
     }
     return res
+
+
+def _step_runtime(B: int, dev, stream, vocab: int = 248320, reps: int = 20) -> dict:
+    """Host + device wall time of the per-step runtime at a decode batch of B requests: building
+    the ForwardBatch (runner.prepare_forward_batch: one packed copy + one sync launch) and
+    sampling B rows of a 27B-vocabulary logits matrix (runner.sample: one launch, one copy back),
+    each beside the reference's sequence restated in torch (engine/model_runner.py:108-188: one
+    torch.tensor copy per field and one slice assignment per request; :574-581: one argmax and
+    one .item() per row).  Wall clock, synchronised on both sides, median of `reps`."""
+    import time
+    from types import SimpleNamespace
+
+    from tokenfactory_b200 import runner as R
+
+    rng = np.random.default_rng(7)
+    max_ctx = 8192
+    r2t = torch.full((B, max_ctx), -1, dtype=torch.int64, device=dev)
+    lens = rng.integers(512, max_ctx - 1, B)
+    reqs = [SimpleNamespace(req_pool_idx=b, cur_start_pos=int(lens[b]), cur_seq_len=int(lens[b]) + 1,
+                            cur_chunk_tokens=[int(rng.integers(0, vocab))],
+                            out_cache_loc=[int(rng.integers(1, 1 << 20))], is_prefilled=True,
+                            temperature=0.0) for b in range(B)]
+    table = [[0] * max_ctx for _ in range(B)]
+
+    def ours():
+        synced = [int(l) for l in lens]
+        R.prepare_forward_batch(reqs, table, r2t, synced)
+
+    def torch_ref():
+        ids = torch.tensor([t for r in reqs for t in r.cur_chunk_tokens], dtype=torch.long, device=dev)
+        pos = torch.tensor([r.cur_start_pos for r in reqs], dtype=torch.long, device=dev)
+        loc = torch.tensor([l for r in reqs for l in r.out_cache_loc], dtype=torch.long, device=dev)
+        for i, r in enumerate(reqs):
+            r2t[r.req_pool_idx, r.cur_start_pos:r.cur_seq_len] = loc[i:i + 1]
+        for f in ("req_pool_idx", "cur_seq_len", "cur_start_pos"):
+            torch.tensor([getattr(r, f) for r in reqs], dtype=torch.long, device=dev)
+        torch.tensor([1] * B, dtype=torch.long, device=dev)
+        return ids, pos
+
+    g = torch.Generator(device=dev).manual_seed(9)
+    logits = torch.randn((B, vocab), generator=g, device=dev, dtype=torch.bfloat16)
+
+    def sample_ours():
+        R.sample(logits, [0.0] * B)
+
+    def sample_torch():
+        return [int(torch.argmax(logits[i], dim=-1).item()) for i in range(B)]
+
+    def wall(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        return float(np.median(ts)) * 1e3
+
+    return {"batch": B, "vocab": vocab, "prepare_ms": wall(ours), "prepare_torch_ms": wall(torch_ref),
+            "sample_ms": wall(sample_ours), "sample_torch_ms": wall(sample_torch),
+            "how": "wall clock with a synchronize on both sides, median of 20"}
 
 
 # ---------------------------------------------------------------------------------------------
