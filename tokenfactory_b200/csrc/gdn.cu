@@ -955,6 +955,17 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 constexpr float kLog2e = 1.4426950408889634f;
+// two fp32 values in one 64-bit register (x in the low half) and the paired fp32 FMA of sm_100
+__device__ __forceinline__ uint64_t pack2(float x, float y) {
+  return ((uint64_t)__float_as_uint(y) << 32) | __float_as_uint(x);
+}
+__device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 // x * sigmoid(x) with an approximate division (no slow path; 0 below x = -87, as the exact value is)
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
@@ -1324,30 +1335,37 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       // ---- U' row l: (I + Mk) u = beta (v - e^g KS), right-looking: once u_j is final, every
       //      later row takes its term at once (independent FMAs; column j of Mk is contiguous)
       {
-        float u[64];
-        tc::ld32(lb + cY, *reinterpret_cast<float(*)[32]>(&u[0]));
-        tc::ld32(lb + cY + 32, *reinterpret_cast<float(*)[32]>(&u[32]));
-        tc::wait_ld();
-        const T* vr = reinterpret_cast<const T*>(sb + oV);
+        // rows (2p, 2p+1) packed in one 64-bit register and updated by one fma.rn.f32x2; the
+        // term of row j itself is multiplied by Mk[j][j] = 0 (Mk is strictly lower)
+        uint64_t u2[32];
+        {
+          float u[64];
+          tc::ld32(lb + cY, *reinterpret_cast<float(*)[32]>(&u[0]));
+          tc::ld32(lb + cY + 32, *reinterpret_cast<float(*)[32]>(&u[32]));
+          tc::wait_ld();
+          const T* vr = reinterpret_cast<const T*>(sb + oV);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * D + l]) - ex2(gam[i]) * u[i]);
+          for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * D + l]) - ex2(gam[i]) * u[i]);
+#pragma unroll
+          for (int p = 0; p < 32; ++p) u2[p] = pack2(u[2 * p], u[2 * p + 1]);
+        }
 #pragma unroll
         for (int j = 0; j < 63; ++j) {
-          const float uj = u[j];
+          const float uj = (j & 1) ? hi_of(u2[j >> 1]) : lo_of(u2[j >> 1]);
+          const uint64_t nuj = pack2(-uj, -uj);
 #pragma unroll
           for (int q4 = (j + 1) >> 2; q4 < 16; ++q4) {
-            const float4 m = *reinterpret_cast<const float4*>(MkT + j * C + 4 * q4);
-            if (4 * q4 + 0 > j) u[4 * q4 + 0] = fmaf(-m.x, uj, u[4 * q4 + 0]);
-            if (4 * q4 + 1 > j) u[4 * q4 + 1] = fmaf(-m.y, uj, u[4 * q4 + 1]);
-            if (4 * q4 + 2 > j) u[4 * q4 + 2] = fmaf(-m.z, uj, u[4 * q4 + 2]);
-            u[4 * q4 + 3] = fmaf(-m.w, uj, u[4 * q4 + 3]);
+            const ulonglong2 m = *reinterpret_cast<const ulonglong2*>(MkT + j * C + 4 * q4);
+            if (4 * q4 + 1 > j) u2[2 * q4] = ffma2(m.x, nuj, u2[2 * q4]);
+            u2[2 * q4 + 1] = ffma2(m.y, nuj, u2[2 * q4 + 1]);
           }
         }
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int k = 0; k < 16; ++k) split2(u[32 * h + 2 * k], u[32 * h + 2 * k + 1], hi[k], lo[k]);
+          for (int k = 0; k < 16; ++k)
+            split2(lo_of(u2[16 * h + k]), hi_of(u2[16 * h + k]), hi[k], lo[k]);
           st16u(lb + cUH + 16 * h, hi);
           st16u(lb + cUL + 16 * h, lo);
         }
