@@ -448,6 +448,100 @@ __global__ void __launch_bounds__(kConvThreads) conv4_tiled_kernel(tf_gdn_args a
   }
 }
 
+// K = 4 conv for 16-bit activations with 8-byte rows: a thread takes 4 channels of a 16-token
+// block and issues the loads of the whole window (3 history rows + 16 rows) before any
+// arithmetic, so 19 independent loads are in flight per thread.  Same FMA order and roundings
+// as conv4_tiled_kernel; SiLU with a hardware exponential and an approximate division (the result
+// is rounded to the 16-bit type, where the two differ in rare last-place cases).
+constexpr int kConvVecTok = 16;
+constexpr int kConvVecThreads = 128;
+
+__device__ __forceinline__ float silu_rt(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+template <typename T>
+__global__ void __launch_bounds__(kConvVecThreads, 4) conv4_vec_kernel(tf_gdn_args a,
+                                                                       const int64_t* start,
+                                                                       T* conv_out) {
+  static_assert(sizeof(T) == 2, "16-bit activations");
+  const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
+  const int c = (blockIdx.x * kConvVecThreads + threadIdx.x) * 4;
+  const int64_t T_all = start[a.batch_size] < a.num_tokens ? start[a.batch_size] : a.num_tokens;
+  const int64_t t_begin = (int64_t)blockIdx.y * kConvVecTok;
+  if (t_begin >= T_all) return;
+  const int n = (int)(T_all - t_begin < kConvVecTok ? T_all - t_begin : kConvVecTok);
+  __shared__ int s_b;
+  if (threadIdx.x == 0) {  // request of the block's first token
+    int lo = 0, hi = a.batch_size - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (start[mid] <= t_begin) lo = mid; else hi = mid - 1;
+    }
+    s_b = lo;
+  }
+  __syncthreads();
+  if (c >= conv_dim) return;
+  const T* x = reinterpret_cast<const T*>(a.qkv) + c;
+  // window rows t_begin-3 .. t_begin+n-1 (rows before token 0 are never used)
+  uint2 win[kConvVecTok + 3];
+#pragma unroll
+  for (int r = 0; r < kConvVecTok + 3; ++r) {
+    const int64_t t = t_begin - 3 + r;
+    win[r] = (t >= 0 && r < n + 3) ? __ldcs(reinterpret_cast<const uint2*>(x + t * a.qkv_stride_tok))
+                                   : make_uint2(0u, 0u);
+  }
+  float w[4][4], bias[4];
+  const T* wt = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * 4;
+  const T* cb = reinterpret_cast<const T*>(a.conv_bias);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[e][j] = to_f(wt[e * 4 + j]);
+    bias[e] = cb ? to_f(cb[c + e]) : 0.f;
+  }
+  int b = s_b;
+  int64_t rs = start[b], re = start[b + 1];
+#pragma unroll
+  for (int i = 0; i < kConvVecTok; ++i) {
+    if (i >= n) break;
+    const int64_t t = t_begin + i;
+    while (t >= re) {  // next request (uniform over the CTA)
+      ++b;
+      rs = re;
+      re = start[b + 1];
+    }
+    float h[3][4];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {  // history rows t-3+k
+      const T* hv = reinterpret_cast<const T*>(&win[i + k]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[k][e] = to_f(hv[e]);
+    }
+    if (t - rs < 3) {  // the first tokens of a request read its conv_state
+      const int64_t slot = a.req_pool_indices[b];
+      const bool ok = slot >= 0 && slot < a.num_slots;
+      if (!ok && c == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+      const T* st = reinterpret_cast<const T*>(a.conv_state) + (ok ? slot : 0) * a.conv_stride_slot;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int64_t p = t - rs - 3 + k;  // position inside the request
+        if (p < 0) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) h[k][e] = ok ? to_f(st[(int64_t)(c + e) * 3 + 3 + p]) : 0.f;
+        }
+      }
+    }
+    const T* xv = reinterpret_cast<const T*>(&win[i + 3]);
+    T out[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float acc = fmaf(w[e][0], h[0][e], fmaf(w[e][1], h[1][e],
+                       fmaf(w[e][2], h[2][e], fmaf(w[e][3], to_f(xv[e]), bias[e]))));
+      out[e] = from_f<T>(round_to<T>(silu_rt(round_to<T>(acc))));
+    }
+    __stcs(reinterpret_cast<uint2*>(conv_out + t * conv_dim + c), *reinterpret_cast<const uint2*>(out));
+  }
+}
+
 // conv_state <- last K-1 columns of [state | x] per (request, channel)  (linear_attention.py:142-143)
 template <typename T>
 __global__ void conv_state_roll_kernel(tf_gdn_args a, const int64_t* start) {
@@ -1542,7 +1636,15 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
   ExtWs w = carve_ext(ws, a);
   const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
   offsets_kernel<<<1, 32, 0, s>>>(a.extend_lens, a.batch_size, w.start);
-  if (a.conv_kernel == 4 && conv_dim % 2 == 0) {
+  const bool conv_vec = sizeof(T) == 2 && a.conv_kernel == 4 && conv_dim % 4 == 0 &&
+                        a.qkv_stride_tok % 4 == 0 && (reinterpret_cast<uintptr_t>(a.qkv) & 7) == 0;
+  if (conv_vec) {
+    if constexpr (sizeof(T) == 2) {
+      dim3 cg((conv_dim / 4 + kConvVecThreads - 1) / kConvVecThreads,
+              (unsigned)((a.num_tokens + kConvVecTok - 1) / kConvVecTok));
+      conv4_vec_kernel<T><<<cg, kConvVecThreads, 0, s>>>(a, w.start, (T*)w.conv_out);
+    }
+  } else if (a.conv_kernel == 4 && conv_dim % 2 == 0) {
     dim3 cg((conv_dim / 2 + kConvThreads - 1) / kConvThreads,
             (unsigned)((a.num_tokens + kConvTok - 1) / kConvTok));
     conv4_tiled_kernel<T><<<cg, kConvThreads, 0, s>>>(a, w.start, (T*)w.conv_out);
