@@ -347,6 +347,56 @@ typedef struct tf_sample_args {
 
 TF_API tf_status tf_sample_tokens(const tf_sample_args* args, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * Block-FP8 linear (triton_block_fp8_linear, qwen3_8/fp8_triton.py:109-181, and its kernel :17-98;
+ * called by Qwen3_8FP8Linear._linear_op, qwen3_8/fp8_linear.py:181-201), as two calls:
+ * tf_fp8_quantize: dynamic per-tensor activation quantization, bit-exact with the wrapper's torch
+ *   lines:  x_scale = float(T(T(max(amax |x|, 1e-12)) / 448))   (T = the activation dtype)
+ *           q       = e4m3_rn(clamp(x / x_scale, -448, 448))    (IEEE fp32 division)
+ *   workspace: at least 16 bytes of device memory.
+ * tf_fp8_block_gemm:
+ *   out[m, n] = OUT( sum_kb (q . w^T)[m, n over K block kb] * w_scale[n / bh, kb * 128 / bw]
+ *                    * x_scale + bias[n] )
+ *   over 128-wide K blocks on the tensor cores (e4m3 products, fp32 accumulation within a block,
+ *   the block scale applied in fp32 between blocks); w_scale NULL means 1.  block_h and block_w
+ *   must be multiples of 128 (the reference's weight_block_size is [128, 128]; pass N and K
+ *   rounded up to 128 for a per-tensor scale); K a multiple of 16; q, w and their row strides
+ *   16-byte aligned.
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct tf_fp8_quant_args {
+  const void* x;               /* [M, K], dtype                                          */
+  int64_t x_stride;            /* elements between rows                                  */
+  int64_t M;
+  int32_t K;
+  int32_t dtype;
+  uint8_t* q;                  /* [M, K] e4m3, row stride K                              */
+  float* x_scale;              /* device scalar                                          */
+  void* workspace;             /* >= 16 bytes                                            */
+} tf_fp8_quant_args;
+
+TF_API tf_status tf_fp8_quantize(const tf_fp8_quant_args* args, void* stream);
+
+typedef struct tf_fp8_gemm_args {
+  const uint8_t* q;            /* [M, K] e4m3                                            */
+  int64_t q_stride;            /* bytes between rows                                     */
+  const float* x_scale;        /* device scalar                                          */
+  const uint8_t* w;            /* [N, K] e4m3                                            */
+  int64_t w_stride;            /* bytes between rows                                     */
+  const float* w_scale;        /* [ceil(N/block_h), ceil(K/block_w)] fp32, or NULL       */
+  int64_t ws_stride_n, ws_stride_k;
+  int32_t block_h, block_w;
+  const void* bias;            /* [N] or NULL                                            */
+  int32_t bias_dtype;
+  void* out;                   /* [M, N], out_dtype                                      */
+  int64_t out_stride;          /* elements between rows                                  */
+  int32_t out_dtype;
+  int64_t M;
+  int32_t N, K;
+  int32_t* err;                /* optional device word                                   */
+} tf_fp8_gemm_args;
+
+TF_API tf_status tf_fp8_block_gemm(const tf_fp8_gemm_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -343,3 +343,30 @@ def runner_script(case: dict = RUNNER_CASE):
         for q in reqs:
             table[q["req_pool_idx"]][q["cur_start_pos"]:q["cur_seq_len"]] = q["out_cache_loc"]
     return steps
+
+
+# ---------------------------------------------------------------------------------------------
+# block-FP8 linear (triton_block_fp8_linear, qwen3_8/fp8_triton.py:109-181)
+# ---------------------------------------------------------------------------------------------
+FP8_CASES: Dict[str, dict] = {
+    "fp8_bf16_blocks": dict(dtype="bf16", M=5, N=200, K=256, scales=True, bias=False, seed=100),
+    "fp8_bf16_bias_tail": dict(dtype="bf16", M=130, N=256, K=272, scales=True, bias=True, seed=101),
+    "fp8_f32_per_tensor": dict(dtype="f32", M=3, N=128, K=128, scales=False, bias=False, seed=102),
+    "fp8_bf16_m64": dict(dtype="bf16", M=64, N=384, K=512, scales=True, bias=True, seed=103),
+}
+
+
+def fp8_inputs(spec: dict) -> dict:
+    """Activations x [M, K] in the case dtype, an e4m3 weight [N, K] (bit patterns), its block
+    scales [ceil(N/128), ceil(K/128)] fp32 (when spec['scales']) and a bias [N] of the case dtype."""
+    from oracle.fp8 import e4m3_encode
+
+    rng = np.random.default_rng(spec["seed"])
+    M, N, K = spec["M"], spec["N"], spec["K"]
+    out = dict(x=_bf.store(_normal(rng, (M, K)), spec["dtype"]),
+               w=e4m3_encode(np.clip(_normal(rng, (N, K), 0.8), -448, 448)))
+    if spec["scales"]:
+        out["w_scale"] = rng.uniform(0.5, 1.5, ((N + 127) // 128, (K + 127) // 128)).astype(np.float32)
+    if spec["bias"]:
+        out["bias"] = _bf.store(_normal(rng, (N,), 0.1), spec["dtype"])
+    return out

@@ -62,3 +62,12 @@ def state_pool_case(name: str):
     assert bytes(z[f"{name}/checksum"]).decode() == C.checksum(inp), f"input drift in {name}"
     gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
     return spec, inp, gold
+
+
+def fp8_case(name: str):
+    spec = C.FP8_CASES[name]
+    inp = C.fp8_inputs(spec)
+    z = _npz("fp8_golden.npz")
+    assert bytes(z[f"{name}/checksum"]).decode() == C.checksum(inp), f"input drift in {name}"
+    gold = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(name + "/")}
+    return spec, inp, gold

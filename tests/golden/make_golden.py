@@ -21,11 +21,16 @@ Reference functions exercised (paths inside the reference project):
   the pool write of Qwen3_8FullAttention       qwen3_8/full_attention.py:147-149
   ReqToStatePool snapshot calls                req_to_state_pool.py:34-194
   ModelRunner._prepare_forward_batch           engine/model_runner.py:108-188
+  triton_block_fp8_linear (Triton interpreter) qwen3_8/fp8_triton.py:17-181
 """
 
 import argparse
 import os
 import sys
+
+# the reference's block-FP8 kernel is a Triton kernel: on this CPU-only host it runs in Triton's
+# interpreter (set before anything imports triton)
+os.environ.setdefault("TRITON_INTERPRET", "1")
 
 import numpy as np
 import torch
@@ -328,18 +333,54 @@ def runner_golden(ref) -> dict:
     return out
 
 
+def fp8_golden(ref) -> dict:
+    """triton_block_fp8_linear of the reference (its torch quantization lines and its Triton
+    kernel, interpreted) on CPU tensors; the quantized activations and scale are the arguments
+    the wrapper hands its kernel, recorded on the way through."""
+    import qwen3_8.fp8_triton as F8
+
+    real = F8._block_fp8_gemm_kernel
+    seen = {}
+
+    class Recorder:  # the launch `kernel[grid](x_fp8, w, out, x_scale, ...)`, recorded
+        def __getitem__(self, grid):
+            def launch(*args, **kw):
+                seen["q"], seen["x_scale"] = args[0].clone(), args[3].clone()
+                return real[grid](*args, **kw)
+            return launch
+
+    F8._block_fp8_gemm_kernel = Recorder()
+    out = {}
+    try:
+        for name, spec in C.FP8_CASES.items():
+            inp = C.fp8_inputs(spec)
+            dt = spec["dtype"]
+            x = _t(inp["x"], dt)
+            w = torch.from_numpy(inp["w"].copy()).view(torch.float8_e4m3fn)
+            ws = torch.from_numpy(inp["w_scale"]) if "w_scale" in inp else None
+            bias = _t(inp["bias"], dt) if "bias" in inp else None
+            y = F8.triton_block_fp8_linear(x, w, ws, bias, 128, 128)
+            out[f"{name}/out"] = _np(y)
+            out[f"{name}/q"] = seen["q"].view(torch.uint8).numpy().copy()
+            out[f"{name}/x_scale"] = seen["x_scale"].reshape(1).numpy().astype(np.float32)
+            out[f"{name}/checksum"] = np.frombuffer(C.checksum(inp).encode(), dtype=np.uint8)
+    finally:
+        F8._block_fp8_gemm_kernel = real
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True,
                     help="root of a yz29528/tokenFactory checkout (its qwen3_8 package)")
     ap.add_argument("--only", nargs="*", default=None,
-                    help="fixture names to regenerate (attention gdn module prologue state_pool runner)")
+                    help="fixture names to regenerate (attention gdn module prologue state_pool runner fp8)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.manual_seed(0)
     makers = dict(attention=attention_golden, gdn=gdn_golden, module=module_golden,
                   prologue=prologue_golden, state_pool=state_pool_golden,
-                  runner=runner_golden)
+                  runner=runner_golden, fp8=fp8_golden)
     for name, make in makers.items():
         if args.only is not None and name not in args.only:
             continue

@@ -64,6 +64,8 @@ _STRUCTS = {
     "tf_state_copy_args": "StateCopyArgs",
     "tf_r2t_sync_args": "R2TSyncArgs",
     "tf_sample_args": "SampleArgs",
+    "tf_fp8_quant_args": "FP8QuantArgs",
+    "tf_fp8_gemm_args": "FP8GemmArgs",
 }
 
 

@@ -133,6 +133,26 @@ class SampleArgs(ctypes.Structure):
     ]
 
 
+class FP8QuantArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("x_stride", _i64), ("M", _i64), ("K", _i32), ("dtype", _i32),
+        ("q", _vp), ("x_scale", _vp), ("workspace", _vp),
+    ]
+
+
+class FP8GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("q_stride", _i64), ("x_scale", _vp),
+        ("w", _vp), ("w_stride", _i64),
+        ("w_scale", _vp), ("ws_stride_n", _i64), ("ws_stride_k", _i64),
+        ("block_h", _i32), ("block_w", _i32),
+        ("bias", _vp), ("bias_dtype", _i32),
+        ("out", _vp), ("out_stride", _i64), ("out_dtype", _i32),
+        ("M", _i64), ("N", _i32), ("K", _i32),
+        ("err", _vp),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point, in header order
 SIGNATURES = [
     ("tf_abi_version", ctypes.c_int, []),
@@ -152,6 +172,8 @@ SIGNATURES = [
     ("tf_state_slots_copy", _i32, [ctypes.POINTER(StateCopyArgs), _vp]),
     ("tf_req_to_token_sync", _i32, [ctypes.POINTER(R2TSyncArgs), _vp]),
     ("tf_sample_tokens", _i32, [ctypes.POINTER(SampleArgs), _vp]),
+    ("tf_fp8_quantize", _i32, [ctypes.POINTER(FP8QuantArgs), _vp]),
+    ("tf_fp8_block_gemm", _i32, [ctypes.POINTER(FP8GemmArgs), _vp]),
 ]
 
 _lib = None

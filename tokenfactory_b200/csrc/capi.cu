@@ -396,4 +396,44 @@ tf_status tf_sample_tokens(const tf_sample_args* a, void* stream) {
   return cuda_status(launch_sample_tokens(*a, s), "tf_sample_tokens");
 }
 
+tf_status tf_fp8_quantize(const tf_fp8_quant_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->M < 0 || a->K < 0) return fail(TF_ERR_INVALID_ARG, "negative sizes");
+  if (a->M == 0 || a->K == 0) return TF_OK;
+  if (!a->x || !a->q || !a->x_scale || !a->workspace)
+    return fail(TF_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
+  if (a->K % 2 != 0 || a->x_stride < a->K) return fail(TF_ERR_INVALID_ARG, "K must be even, x_stride >= K");
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 3) != 0 || (reinterpret_cast<uintptr_t>(a->q) & 1) != 0)
+    return fail(TF_ERR_ALIGNMENT, "workspace must be 4-byte and q 2-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_fp8_quantize(*a, s), "tf_fp8_quantize");
+}
+
+tf_status tf_fp8_block_gemm(const tf_fp8_gemm_args* a, void* stream) {
+  if (a == nullptr) return fail(TF_ERR_INVALID_ARG, "args is NULL");
+  if (a->M < 0 || a->N < 0 || a->K <= 0) return fail(TF_ERR_INVALID_ARG, "bad sizes");
+  if (a->M == 0 || a->N == 0) return TF_OK;
+  if (a->M > (int64_t)65535 * 128) return fail(TF_ERR_INVALID_ARG, "M too large for one launch");
+  if (!a->q || !a->w || !a->x_scale || !a->out)
+    return fail(TF_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!dtype_ok(a->out_dtype) || (a->bias && !dtype_ok(a->bias_dtype)))
+    return fail(TF_ERR_INVALID_ARG, "unknown dtype");
+  if (a->K % 16 != 0) return fail(TF_ERR_UNSUPPORTED, "K must be a multiple of 16, got %d", a->K);
+  if (a->w_scale && (a->block_h <= 0 || a->block_w <= 0 || a->block_h % 128 || a->block_w % 128))
+    return fail(TF_ERR_UNSUPPORTED, "block_h and block_w must be multiples of 128 (got %d, %d)",
+                a->block_h, a->block_w);
+  if (a->q_stride < a->K || a->w_stride < a->K || a->out_stride < a->N)
+    return fail(TF_ERR_INVALID_ARG, "a row stride is shorter than its row");
+  if (((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->w) |
+        (uintptr_t)a->q_stride | (uintptr_t)a->w_stride) & 15) != 0)
+    return fail(TF_ERR_ALIGNMENT, "q, w and their row strides must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceGuard g(s);
+  if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
+  return cuda_status(launch_fp8_block_gemm(*a, s), "tf_fp8_block_gemm");
+}
+
 }  // extern "C"

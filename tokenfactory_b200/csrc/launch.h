@@ -47,6 +47,10 @@ cudaError_t launch_state_slots_copy(const tf_state_copy_args& a, cudaStream_t s)
 cudaError_t launch_req_to_token_sync(const tf_r2t_sync_args& a, cudaStream_t s);
 cudaError_t launch_sample_tokens(const tf_sample_args& a, cudaStream_t s);
 
+// fp8_gemm.cu: block-FP8 linear (activation quantization + tcgen05 kind::f8f6f4 GEMM)
+cudaError_t launch_fp8_quantize(const tf_fp8_quant_args& a, cudaStream_t s);
+cudaError_t launch_fp8_block_gemm(const tf_fp8_gemm_args& a, cudaStream_t s);
+
 // capi.cu
 int device_sm_count();
 

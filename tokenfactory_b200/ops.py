@@ -494,3 +494,66 @@ def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor,
                         out=out.data_ptr())
     C.check("tf_sample_tokens", C.load().tf_sample_tokens(ctypes.byref(args), _stream(dev)))
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# block-FP8 linear
+# ---------------------------------------------------------------------------------------------
+def fp8_quantize(x2d: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(q [M, K] float8_e4m3fn, x_scale [1] float32) of the dynamic per-tensor activation
+    quantization of triton_block_fp8_linear (qwen3_8/fp8_triton.py:124-130), bit-exact."""
+    dev = _need_cuda(x2d)
+    if x2d.dim() != 2 or x2d.stride(1) != 1:
+        raise ValueError("fp8_quantize takes [M, K] with contiguous rows")
+    M, K = x2d.shape
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=dev)
+    scale = torch.empty(1, dtype=torch.float32, device=dev)
+    scratch = torch.empty(4, dtype=torch.int32, device=dev)
+    args = C.FP8QuantArgs(x=x2d.data_ptr(), x_stride=x2d.stride(0), M=M, K=K, dtype=_dtype(x2d),
+                          q=q.data_ptr(), x_scale=scale.data_ptr(), workspace=scratch.data_ptr())
+    with torch.cuda.device(dev):
+        C.check("tf_fp8_quantize", C.load().tf_fp8_quantize(ctypes.byref(args), _stream(dev)))
+    return q, scale
+
+
+def fp8_block_gemm(q: torch.Tensor, x_scale: torch.Tensor, weight: torch.Tensor,
+                   weight_scale_inv: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                   out_dtype: torch.dtype, block_h: int = 128, block_w: int = 128,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out [M, N] = (q @ weight^T per 128-wide K block * weight_scale_inv[n/bh, k/bw]) * x_scale
+    + bias, on the tensor cores (the kernel of qwen3_8/fp8_triton.py:17-98)."""
+    dev = _need_cuda(q, x_scale, weight, weight_scale_inv, bias)
+    M, K = q.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K or weight.stride(1) != 1 or q.stride(1) != 1:
+        raise ValueError("q [M, K] and weight [N, K] need contiguous rows of the same K")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=dev)
+    ws = None
+    if weight_scale_inv is not None:
+        ws = weight_scale_inv if weight_scale_inv.dtype == torch.float32 else weight_scale_inv.float()
+    args = C.FP8GemmArgs(
+        q=q.data_ptr(), q_stride=q.stride(0), x_scale=x_scale.data_ptr(),
+        w=weight.data_ptr(), w_stride=weight.stride(0),
+        w_scale=_ptr(ws), ws_stride_n=ws.stride(0) if ws is not None else 0,
+        ws_stride_k=ws.stride(1) if ws is not None else 0, block_h=block_h, block_w=block_w,
+        bias=_ptr(bias), bias_dtype=_dtype(bias) if bias is not None else 0,
+        out=out.data_ptr(), out_stride=out.stride(0), out_dtype=_dtype(out), M=M, N=N, K=K)
+    with torch.cuda.device(dev):
+        C.check("tf_fp8_block_gemm", C.load().tf_fp8_block_gemm(ctypes.byref(args), _stream(dev)))
+    return out
+
+
+def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor,
+                     weight_scale_inv: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                     block_h: int = 128, block_w: int = 128) -> torch.Tensor:
+    """triton_block_fp8_linear (qwen3_8/fp8_triton.py:109-181) with the same arguments and result:
+    dynamic per-tensor e4m3 activations, e4m3 weight [N, K] with block scales
+    weight_scale_inv [ceil(N/bh), ceil(K/bw)] (or None), output in x's dtype."""
+    N, K = weight.shape
+    x2d = x.reshape(-1, K)
+    if x2d.stride(1) != 1:
+        x2d = x2d.contiguous()
+    q, scale = fp8_quantize(x2d)
+    out = fp8_block_gemm(q, scale, weight, weight_scale_inv, bias, x.dtype, block_h, block_w)
+    return out.reshape(*x.shape[:-1], N)
