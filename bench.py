@@ -676,6 +676,87 @@ def bench_extend(args, rank, world, dev):
 
 
 # ---------------------------------------------------------------------------------------------
+# config 6: block-FP8 linear at a 27B projection shape
+# ---------------------------------------------------------------------------------------------
+C6 = dict(N=17408, K=5120, M_prefill=8192, M_decode=128)
+
+
+def bench_fp8(args, rank, world, dev):
+    """triton_block_fp8_linear's job (qwen3_8/fp8_triton.py:109-181) on the 27B MLP up projection
+    (hidden 5120 -> intermediate 17408, e4m3 weights with 128 x 128 block scales, bf16
+    activations): the activation quantization plus the tcgen05 GEMM, timed with CUDA events on
+    the launching stream.  Column-parallel under TP: each rank owns N / world output columns."""
+    from tokenfactory_b200 import ops
+
+    N, K = C6["N"] // world, C6["K"]
+    g = torch.Generator(device=dev).manual_seed(6 + rank)
+    w = (torch.randn((N, K), generator=g, device=dev) * 0.5).to(torch.float8_e4m3fn)
+    ws = torch.rand(((N + 127) // 128, (K + 127) // 128), generator=g, device=dev) + 0.5
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        _barrier(world)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        return _max_over_ranks(t0.elapsed_time(t1) / 1e3, world) / steps
+
+    res = {}
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for tag, M in (("prefill", C6["M_prefill"]), ("decode", C6["M_decode"])):
+            x = torch.randn((M, K), generator=g, device=dev, dtype=torch.bfloat16)
+            q, s = ops.fp8_quantize(x)
+            out = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+            full = timed(lambda: ops.block_fp8_linear(x, w, ws, None), args.steps)
+            gemm = timed(lambda: ops.fp8_block_gemm(q, s, w, ws, None, torch.bfloat16, out=out),
+                         args.steps)
+
+            def scaled_mm_loop():  # the reference's non-Triton path (fp8_linear.py:124-179), restated
+                acc = torch.zeros((M, N), dtype=torch.float32, device=dev)
+                one = torch.ones((1,), dtype=torch.float32, device=dev)
+                for kb, k0 in enumerate(range(0, K, 128)):
+                    blk = torch._scaled_mm(q[:, k0:k0 + 128].contiguous(),
+                                           w[:, k0:k0 + 128].contiguous().t(), scale_a=s,
+                                           scale_b=one, out_dtype=torch.float32)
+                    acc += blk * ws[:, kb].repeat_interleave(128)[:N].unsqueeze(0)
+                return acc.to(torch.bfloat16)
+
+            ref_s = timed(scaled_mm_loop, max(1, args.steps // 10))
+            flops = 2.0 * M * N * K
+            res[tag] = {"M": M, "ms_linear": full * 1e3, "ms_gemm": gemm * 1e3,
+                        "tflops_gemm": flops / gemm / 1e12, "tflops_linear": flops / full / 1e12,
+                        "weight_gb_per_s_gemm": N * K / gemm / 1e9,
+                        "torch_scaled_mm_loop_ms": ref_s * 1e3}
+    bf16_peak, peak_kind = _peak_tflops()
+    fp8_peak = 2 * bf16_peak
+    pre = res["prefill"]
+    return {
+        "metric": "block-FP8 linear TFLOP/s (27B MLP up projection 5120 -> 17408, 128x128 block scales)",
+        "value": pre["tflops_gemm"] * world, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": pre["ms_gemm"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8_e4m3",
+        "data": "synthetic",
+        "config": {"workload": "config6 block-FP8 GEMM (qwen3_8/fp8_triton.py)", "M": pre["M"],
+                   "N": C6["N"], "K": K, "parallelism": f"tp{world}",
+                   "l2": "weights (89 MB) and activations (84 MB) re-read from L2 across tiles"},
+        "roofline": {"bound": "tensor", "achieved": pre["tflops_gemm"], "peak": fp8_peak,
+                     "unit": "TFLOP/s", "frac": pre["tflops_gemm"] / fp8_peak,
+                     "peak_kind": f"2x {peak_kind} bf16 (the dense e4m3 rate is twice bf16's)",
+                     "kernel": "tf_fp8_block_gemm (tcgen05 kind::f8f6f4)"},
+        "prefill": pre, "decode": res["decode"],
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU baseline: the oracle (restatement of the reference's torch algorithm) on this host
 # ---------------------------------------------------------------------------------------------
 def _cpu_decode_sample(n_requests: int, seed: int = 0):
@@ -768,7 +849,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 6])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=C2["B"],
@@ -797,8 +878,8 @@ def main():
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     dev = torch.device("cuda", torch.cuda.current_device())
-    res = {2: bench_decode, 3: bench_gdn_decode, 4: bench_extend}[args.config](args, rank, world,
-                                                                              dev)
+    res = {2: bench_decode, 3: bench_gdn_decode, 4: bench_extend,
+           6: bench_fp8}[args.config](args, rank, world, dev)
     if rank == 0 and world == 1 and args.config == 2 and not args.no_e2e and \
             args.cpu_baseline_seconds > 0:
         threads = os.cpu_count() or 1

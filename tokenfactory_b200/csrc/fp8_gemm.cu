@@ -6,9 +6,14 @@
 //  * tf_fp8_block_gemm: out = (sum over 128-wide K blocks of (q . w^T)_block * w_scale[n/bh, k/bw])
 //    * x_scale + bias on the 5th-generation tensor cores (tcgen05.mma kind::f8f6f4, e4m3 x e4m3 ->
 //    fp32 in TMEM).  A 128 x 128 output tile meets one weight-scale block per K block (bh and bw
-//    are multiples of 128), so each K block's product goes to its own TMEM accumulator (two,
-//    alternating) and the epilogue warps add it, times its scale, into fp32 registers while the
-//    tensor core works on the next block.
+//    are multiples of 128), so each K block's product goes to its own TMEM accumulator (four in
+//    rotation) and eight epilogue warps add it, times its scale, into fp32 registers while the
+//    tensor core works on the next blocks.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.h"
 #include "tcgen05.cuh"
@@ -68,13 +73,13 @@ constexpr int kBM = 128, kBN = 128, kBK = 128;  // a K block is one 128-byte SW1
 constexpr int kStages = 4;
 constexpr int kTile = kBM * kBK;                // 16 KB per operand per stage
 constexpr int kStageBytes = 2 * kTile;
-constexpr int kThreads = 256;                   // warps 0-3 epilogue, 4 MMA, 5-7 loads
-constexpr int kLoaders = 96;
-constexpr int kChunks = 2 * kBM * kBK / 16;     // 16-byte pieces per stage (A and B)
+constexpr int kThreads = 320;                   // warps 0-7 epilogue, 8 MMA, 9 TMA loads
+constexpr int kMmaWarp = 8, kLoadWarp = 9;
+constexpr int kAcc = 4;                         // TMEM accumulators of 128 columns (all 512)
 constexpr int kSmem = kStages * kStageBytes + 256 + 1024;
 
 struct Bars {
-  uint64_t full[kStages], empty[kStages], pfull[2], pfree[2];
+  uint64_t full[kStages], empty[kStages], pfull[kAcc], pfree[kAcc];
   uint32_t tmem;
   int abort;
 };
@@ -92,8 +97,20 @@ __device__ __forceinline__ bool wait_b(uint64_t* bar, uint32_t parity, volatile 
   }
 }
 
+// 2-D tiled TMA load of one 128 x 128-byte box (SWIZZLE_128B) into this CTA's shared memory;
+// the source is this GPU's own memory and the x coordinate (bytes) is a multiple of 128
+__device__ __forceinline__ void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 template <typename TO>
-__global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_args a) {
+__global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_args a,
+                                                                 const __grid_constant__ CUtensorMap map_q,
+                                                                 const __grid_constant__ CUtensorMap map_w) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;
@@ -107,60 +124,45 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full[s], kLoaders);
+      mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       mbar_init(&bars->pfull[b], 1);
-      mbar_init(&bars->pfree[b], 4);
+      mbar_init(&bars->pfree[b], 8);
     }
     bars->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 4) tc::tmem_alloc(&bars->tmem, 256);
+  if (warp == kMmaWarp) tc::tmem_alloc(&bars->tmem, 512);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = bars->tmem;
 
-  if (warp >= 5) {
-    // ============ loads: 16-byte cp.async into the SW128 K-major layout ============
-    const int pt = tid - 160;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kStages;
-      if (kb >= kStages && !wait_b(&bars->empty[s], ((kb / kStages) - 1) & 1, abort)) break;
-      const uint32_t st = base + s * kStageBytes;
-#pragma unroll 4
-      for (int i = 0; i < (kChunks + kLoaders - 1) / kLoaders; ++i) {
-        const int qid = pt + kLoaders * i;
-        if (qid >= kChunks) break;
-        const int op = qid >> 10, r = (qid >> 3) & 127, c = qid & 7;
-        const int kbyte = kb * kBK + c * 16;
-        const uint32_t dst = st + op * kTile + r * 128 + ((uint32_t)(c ^ (r & 7)) << 4);
-        const bool live_k = kbyte < a.K;  // K is a multiple of 16: a chunk is all in or all out
-        if (op == 0) {
-          const bool live = live_k && m0 + r < a.M;
-          const uint8_t* src = a.q + (live ? (m0 + r) * a.q_stride + kbyte : 0);
-          cp_async16_zfill(dst, src, live ? 16u : 0u);
-        } else {
-          const bool live = live_k && n0 + r < a.N;
-          const uint8_t* src = a.w + (live ? (int64_t)(n0 + r) * a.w_stride + kbyte : 0);
-          cp_async16_zfill(dst, src, live ? 16u : 0u);
-        }
+  if (warp == kLoadWarp) {
+    // ============ loads: two TMA boxes (q rows, w rows; zero fill past M, N and K) per stage ============
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages && !wait_b(&bars->empty[s], ((kb / kStages) - 1) & 1, abort)) break;
+        const uint32_t st = base + s * kStageBytes;
+        mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+        tma_load_box(st, &map_q, kb * kBK, (int)m0, &bars->full[s]);
+        tma_load_box(st + kTile, &map_w, kb * kBK, n0, &bars->full[s]);
       }
-      cp_async_arrive_noinc(&bars->full[s]);
     }
-    cp_async_wait_all();
-  } else if (warp == 4) {
-    // ============ MMA issue (one thread): one K block into one of two TMEM accumulators ============
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ============ MMA issue (one thread): one K block into one of four TMEM accumulators ============
     if (lane == 0) {
       constexpr uint32_t idesc = (1u << 4)                       // D: f32
                                  | (0u << 7) | (0u << 10)         // A, B: e4m3
                                  | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kStages, b = kb & 1;
+        const int s = kb % kStages, b = kb % kAcc;
         if (!wait_b(&bars->full[s], (kb / kStages) & 1, abort)) break;
-        if (kb >= 2 && !wait_b(&bars->pfree[b], ((kb >> 1) - 1) & 1, abort)) break;
+        if (kb >= kAcc && !wait_b(&bars->pfree[b], ((kb / kAcc) - 1) & 1, abort)) break;
         tc::fence_proxy_async_smem();
         tc::fence_after_sync();
         const uint32_t st = base + s * kStageBytes;
@@ -181,48 +183,55 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
     __syncwarp();
   } else {
     // ============ epilogue: acc += w_scale * partial per K block, then out = acc * x_scale + bias ============
-    const int row = 32 * warp + lane;  // TMEM lane = output row of the tile
-    const uint32_t lb = tmem + ((uint32_t)(32 * warp) << 16);
-    float acc[kBN];
+    // warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and columns 64 (w / 4) .. +63
+    const int q = warp & 3, h = warp >> 2;
+    const int row = 32 * q + lane;
+    const uint32_t lb = tmem + ((uint32_t)(32 * q) << 16) + 64 * h;
+    const float* wsrow = a.w_scale ? a.w_scale + (int64_t)(n0 / a.block_h) * a.ws_stride_n : nullptr;
+    auto scale_of = [&](int kb) -> float {
+      return wsrow ? __ldg(wsrow + (int64_t)(kb * kBK / a.block_w) * a.ws_stride_k) : 1.f;
+    };
+    float acc[64];
 #pragma unroll
-    for (int j = 0; j < kBN; ++j) acc[j] = 0.f;
+    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
     bool ok = true;
+    float sc_next = scale_of(0);
     for (int kb = 0; kb < nkb && ok; ++kb) {
-      const int b = kb & 1;
-      ok = wait_b(&bars->pfull[b], (kb >> 1) & 1, abort);
+      const int b = kb % kAcc;
+      const float sc = sc_next;
+      if (kb + 1 < nkb) sc_next = scale_of(kb + 1);  // in flight while this block's MMAs finish
+      ok = wait_b(&bars->pfull[b], (kb / kAcc) & 1, abort);
       if (!ok) break;
       tc::fence_after_sync();
-      float sc = 1.f;
-      if (a.w_scale)
-        sc = a.w_scale[(int64_t)(n0 / a.block_h) * a.ws_stride_n + (int64_t)(kb * kBK / a.block_w) * a.ws_stride_k];
+      float p[64];
+      tc::ld32(lb + b * 128, *reinterpret_cast<float(*)[32]>(&p[0]));
+      tc::ld32(lb + b * 128 + 32, *reinterpret_cast<float(*)[32]>(&p[32]));
+      tc::wait_ld();
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        float p[32];
-        tc::ld32(lb + b * 128 + 32 * c, p);
-        tc::wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[32 * c + j] = fmaf(p[j], sc, acc[32 * c + j]);
-      }
+      for (int j = 0; j < 64; ++j) acc[j] = fmaf(p[j], sc, acc[j]);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->pfree[b]);
     }
     if (ok && m0 + row < a.M) {
       const float xs = *a.x_scale;
-      TO* out = reinterpret_cast<TO*>(a.out) + (m0 + row) * a.out_stride + n0;
-      const int ncol = a.N - n0 < kBN ? a.N - n0 : kBN;
-      const bool vec = ncol == kBN && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && sizeof(TO) == 2;
+      const int c0 = 64 * h;
+      TO* out = reinterpret_cast<TO*>(a.out) + (m0 + row) * a.out_stride + n0 + c0;
+      const int ncol = a.N - n0 - c0 < 64 ? a.N - n0 - c0 : 64;
+      const bool vec = ncol == 64 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && sizeof(TO) == 2;
 #pragma unroll
-      for (int c8 = 0; c8 < kBN / 8; ++c8) {
+      for (int c8 = 0; c8 < 8; ++c8) {
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int n = c8 * 8 + e;
           float bias = 0.f;
-          if (a.bias && n < ncol)
-            bias = a.bias_dtype == TF_DTYPE_F32 ? reinterpret_cast<const float*>(a.bias)[n0 + n]
-                 : a.bias_dtype == TF_DTYPE_BF16 ? to_f(reinterpret_cast<const __nv_bfloat16*>(a.bias)[n0 + n])
-                                                 : to_f(reinterpret_cast<const __half*>(a.bias)[n0 + n]);
+          if (a.bias && n < ncol) {
+            const int64_t bn = n0 + c0 + n;
+            bias = a.bias_dtype == TF_DTYPE_F32 ? reinterpret_cast<const float*>(a.bias)[bn]
+                 : a.bias_dtype == TF_DTYPE_BF16 ? to_f(reinterpret_cast<const __nv_bfloat16*>(a.bias)[bn])
+                                                 : to_f(reinterpret_cast<const __half*>(a.bias)[bn]);
+          }
           v[e] = fmaf(acc[n], xs, bias);
         }
         if (vec) {
@@ -242,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
   __syncthreads();
   if (tid == 0 && *abort && a.err) record_err(a.err, TF_KERR_TIMEOUT);
   tc::fence_after_sync();
-  if (warp == 4) tc::tmem_dealloc(tmem, 256);
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, 512);
 }
 
 }  // namespace fp8
@@ -280,8 +289,42 @@ cudaError_t launch_fp8_quantize(const tf_fp8_quant_args& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [rows, cols] bytes with a row stride, read in 128 x 128 boxes, SWIZZLE_128B, zero fill outside
+bool box_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t stride) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {(cuuint32_t)fp8::kBK, 128};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
 cudaError_t launch_fp8_block_gemm(const tf_fp8_gemm_args& a, cudaStream_t s) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
+  CUtensorMap mq, mw;
+  if (!box_map(&mq, a.q, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.q_stride) ||
+      !box_map(&mw, a.w, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.w_stride))
+    return cudaErrorNotSupported;
   dim3 grid((a.N + fp8::kBN - 1) / fp8::kBN, (unsigned)((a.M + fp8::kBM - 1) / fp8::kBM));
   cudaError_t e;
   switch (a.out_dtype) {
@@ -289,19 +332,19 @@ cudaError_t launch_fp8_block_gemm(const tf_fp8_gemm_args& a, cudaStream_t s) {
       e = cudaFuncSetAttribute(fp8::block_gemm_kernel<__nv_bfloat16>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
       if (e != cudaSuccess) return e;
-      fp8::block_gemm_kernel<__nv_bfloat16><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a);
+      fp8::block_gemm_kernel<__nv_bfloat16><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
       break;
     case TF_DTYPE_F16:
       e = cudaFuncSetAttribute(fp8::block_gemm_kernel<__half>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
       if (e != cudaSuccess) return e;
-      fp8::block_gemm_kernel<__half><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a);
+      fp8::block_gemm_kernel<__half><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
       break;
     default:
       e = cudaFuncSetAttribute(fp8::block_gemm_kernel<float>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
       if (e != cudaSuccess) return e;
-      fp8::block_gemm_kernel<float><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a);
+      fp8::block_gemm_kernel<float><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
   }
   return cudaGetLastError();
 }
