@@ -353,7 +353,7 @@ TF_API tf_status tf_sample_tokens(const tf_sample_args* args, void* stream);
  * tf_fp8_quantize: dynamic per-tensor activation quantization, bit-exact with the wrapper's torch
  *   lines:  x_scale = float(T(T(max(amax |x|, 1e-12)) / 448))   (T = the activation dtype)
  *           q       = e4m3_rn(clamp(x / x_scale, -448, 448))    (IEEE fp32 division)
- *   workspace: at least 16 bytes of device memory.
+ *   K a multiple of 16, x rows and q 16-byte aligned; workspace: at least 16 bytes of device memory.
  * tf_fp8_block_gemm:
  *   out[m, n] = OUT( sum_kb (q . w^T)[m, n over K block kb] * w_scale[n / bh, kb * 128 / bw]
  *                    * x_scale + bias[n] )

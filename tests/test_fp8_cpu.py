@@ -82,4 +82,7 @@ def test_gemm_argument_checks_without_a_gpu():
     assert lib.tf_fp8_block_gemm(ctypes.byref(a), None) == _capi.TF_OK
     qa = _capi.FP8QuantArgs(x=fake, x_stride=255, M=2, K=255, dtype=1, q=fake, x_scale=fake,
                             workspace=fake)
-    assert lib.tf_fp8_quantize(ctypes.byref(qa), None) == _capi.TF_ERR_INVALID_ARG
+    assert lib.tf_fp8_quantize(ctypes.byref(qa), None) == _capi.TF_ERR_UNSUPPORTED
+    qa = _capi.FP8QuantArgs(x=fake + 2, x_stride=256, M=2, K=256, dtype=1, q=fake, x_scale=fake,
+                            workspace=fake)
+    assert lib.tf_fp8_quantize(ctypes.byref(qa), None) == _capi.TF_ERR_ALIGNMENT

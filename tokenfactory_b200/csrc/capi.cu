@@ -403,9 +403,12 @@ tf_status tf_fp8_quantize(const tf_fp8_quant_args* a, void* stream) {
   if (!a->x || !a->q || !a->x_scale || !a->workspace)
     return fail(TF_ERR_INVALID_ARG, "a required pointer is NULL");
   if (!dtype_ok(a->dtype)) return fail(TF_ERR_INVALID_ARG, "unknown dtype %d", a->dtype);
-  if (a->K % 2 != 0 || a->x_stride < a->K) return fail(TF_ERR_INVALID_ARG, "K must be even, x_stride >= K");
-  if ((reinterpret_cast<uintptr_t>(a->workspace) & 3) != 0 || (reinterpret_cast<uintptr_t>(a->q) & 1) != 0)
-    return fail(TF_ERR_ALIGNMENT, "workspace must be 4-byte and q 2-byte aligned");
+  if (a->K % 16 != 0 || a->x_stride < a->K)
+    return fail(TF_ERR_UNSUPPORTED, "K must be a multiple of 16 and x_stride >= K");
+  const int eb = a->dtype == TF_DTYPE_F32 ? 4 : 2;
+  if (((reinterpret_cast<uintptr_t>(a->x) | (uintptr_t)(a->x_stride * eb)) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(a->workspace) & 3) != 0 || (reinterpret_cast<uintptr_t>(a->q) & 15) != 0)
+    return fail(TF_ERR_ALIGNMENT, "x rows and q must be 16-byte aligned, workspace 4-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DeviceGuard g(s);
   if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");

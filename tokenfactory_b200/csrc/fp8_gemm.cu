@@ -24,19 +24,6 @@ namespace fp8 {
 // ---------------------------------------------------------------------------------------------
 // activation quantization
 // ---------------------------------------------------------------------------------------------
-template <typename T>
-__global__ void amax_kernel(const T* x, int64_t stride, int64_t M, int K, unsigned int* amax_bits) {
-  float m = 0.f;
-  const int64_t n = M * (int64_t)K;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / K, c = i - r * K;
-    m = fmaxf(m, fabsf(to_f(x[r * stride + c])));
-  }
-  m = warp_max(m);
-  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(m));  // m >= 0: bit order = value order
-}
-
 // x_scale = float(T(max(amax, 1e-12) / 448)): the wrapper's `amax.clamp(min=1e-12)` and `/ fp8_max`
 // run on a tensor of the activation dtype (each rounded to it), then `.to(torch.float32)`
 template <typename T>
@@ -45,10 +32,84 @@ __device__ __forceinline__ float act_scale(float amax) {
   return round_to<T>(__fdiv_rn(c, 448.0f));
 }
 
+// two e4m3 values, round to nearest even (inputs already clamped to +-448); lo at the lower address
 __device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// 16-byte vectors of a row: 8 elements of a 16-bit type, 4 of fp32
+template <typename T> struct Vec { static constexpr int kN = 16 / sizeof(T); };
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* p, float (&v)[Vec<T>::kN]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int j = 0; j < Vec<T>::kN; ++j) v[j] = to_f(e[j]);
+}
+
+// A warp's unit of work: a row and a span of kSpan elements of it (lane-strided 16-byte vectors)
+constexpr int kSpan = 1024;
+
+// max |x| of this thread's share of the units warp0, warp0 + nwarps, ...
+template <typename T>
+__device__ __forceinline__ float thread_amax(const T* x, int64_t stride, int64_t M, int K,
+                                             int64_t warp0, int64_t nwarps, int lane) {
+  constexpr int V = Vec<T>::kN;
+  const int spans = (K + kSpan - 1) / kSpan;
+  float m = 0.f;
+  for (int64_t u = warp0; u < M * spans; u += nwarps) {
+    const int64_t r = u / spans;
+    const int c1 = (int)(u - r * spans) * kSpan, c2 = c1 + kSpan < K ? c1 + kSpan : K;
+    const T* row = x + r * stride;
+    for (int c = c1 + lane * V; c < c2; c += 32 * V) {
+      float v[V];
+      load_vec(row + c, v);
+#pragma unroll
+      for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(v[j]));
+    }
+  }
+  return warp_max(m);
+}
+
+template <typename T>
+__device__ __forceinline__ void quantize_rows(const T* x, int64_t stride, int64_t M, int K, float s,
+                                              uint8_t* q, int64_t warp0, int64_t nwarps, int lane) {
+  constexpr int V = Vec<T>::kN;
+  const int spans = (K + kSpan - 1) / kSpan;
+  for (int64_t u = warp0; u < M * spans; u += nwarps) {
+    const int64_t r = u / spans;
+    const int c1 = (int)(u - r * spans) * kSpan, c2 = c1 + kSpan < K ? c1 + kSpan : K;
+    const T* row = x + r * stride;
+    uint8_t* qr = q + r * K;
+    for (int c = c1 + lane * V; c < c2; c += 32 * V) {
+      float v[V];
+      load_vec(row + c, v);
+      uint16_t pk[V / 2];
+#pragma unroll
+      for (int j = 0; j < V / 2; ++j) {
+        const float a0 = fminf(fmaxf(__fdiv_rn(v[2 * j], s), -448.f), 448.f);
+        const float a1 = fminf(fmaxf(__fdiv_rn(v[2 * j + 1], s), -448.f), 448.f);
+        pk[j] = e4m3x2(a0, a1);
+      }
+      if constexpr (V == 8) {
+        *reinterpret_cast<uint2*>(qr + c) = *reinterpret_cast<const uint2*>(pk);
+      } else {
+        *reinterpret_cast<uint32_t*>(qr + c) = *reinterpret_cast<const uint32_t*>(pk);
+      }
+    }
+  }
+}
+
+// large inputs: amax over the grid (one atomic per warp; non-negative floats order as their bits)
+template <typename T>
+__global__ void amax_kernel(const T* x, int64_t stride, int64_t M, int K, unsigned int* amax_bits) {
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const float m = thread_amax(x, stride, M, K, warp0, nwarps, threadIdx.x & 31);
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(m));
 }
 
 template <typename T>
@@ -56,14 +117,25 @@ __global__ void quantize_kernel(const T* x, int64_t stride, int64_t M, int K,
                                 const unsigned int* amax_bits, uint8_t* q, float* x_scale) {
   const float s = act_scale<T>(__uint_as_float(*amax_bits));
   if (blockIdx.x == 0 && threadIdx.x == 0) *x_scale = s;
-  const int64_t pairs = M * (int64_t)(K / 2);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < pairs;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / (K / 2), c = 2 * (i - r * (K / 2));
-    const float a = fminf(fmaxf(__fdiv_rn(to_f(x[r * stride + c]), s), -448.f), 448.f);
-    const float b = fminf(fmaxf(__fdiv_rn(to_f(x[r * stride + c + 1]), s), -448.f), 448.f);
-    *reinterpret_cast<uint16_t*>(q + r * K + c) = e4m3x2(a, b);
-  }
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  quantize_rows(x, stride, M, K, s, q, warp0, nwarps, threadIdx.x & 31);
+}
+
+// small inputs (decode batches): one CTA computes the amax and quantizes, in one launch
+template <typename T>
+__global__ void __launch_bounds__(1024) quantize_small_kernel(const T* x, int64_t stride, int64_t M,
+                                                              int K, uint8_t* q, float* x_scale) {
+  __shared__ float red[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float m = thread_amax(x, stride, M, K, warp, nw, lane);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  t = warp_max(t);
+  const float s = act_scale<T>(t);
+  if (threadIdx.x == 0) *x_scale = s;
+  quantize_rows(x, stride, M, K, s, q, warp, nw, lane);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -258,35 +330,32 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
 
 size_t fp8_quantize_workspace() { return 256; }
 
-cudaError_t launch_fp8_quantize(const tf_fp8_quant_args& a, cudaStream_t s) {
-  if (a.M == 0 || a.K == 0) return cudaSuccess;
+template <typename T>
+cudaError_t quantize_t(const tf_fp8_quant_args& a, cudaStream_t s) {
+  const T* x = static_cast<const T*>(a.x);
+  const int64_t n = a.M * (int64_t)a.K;
+  if (n <= (int64_t)1 << 15) {  // up to 32K elements: one CTA, one launch
+    fp8::quantize_small_kernel<T><<<1, 1024, 0, s>>>(x, a.x_stride, a.M, a.K, a.q, a.x_scale);
+    return cudaGetLastError();
+  }
   unsigned int* amax = static_cast<unsigned int*>(a.workspace);
   cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(unsigned int), s);
   if (e != cudaSuccess) return e;
-  const int64_t n = a.M * (int64_t)a.K;
-  const int cap = device_sm_count() * 8;
-  const int g1 = (int)((n + 255) / 256 < cap ? (n + 255) / 256 : cap);
-  const int g2 = (int)((n / 2 + 255) / 256 < cap ? (n / 2 + 255) / 256 : cap);
-  switch (a.dtype) {
-    case TF_DTYPE_BF16: {
-      auto x = static_cast<const __nv_bfloat16*>(a.x);
-      fp8::amax_kernel<<<g1, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax);
-      fp8::quantize_kernel<<<g2, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax, a.q, a.x_scale);
-      break;
-    }
-    case TF_DTYPE_F16: {
-      auto x = static_cast<const __half*>(a.x);
-      fp8::amax_kernel<<<g1, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax);
-      fp8::quantize_kernel<<<g2, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax, a.q, a.x_scale);
-      break;
-    }
-    default: {
-      auto x = static_cast<const float*>(a.x);
-      fp8::amax_kernel<<<g1, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax);
-      fp8::quantize_kernel<<<g2, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax, a.q, a.x_scale);
-    }
-  }
+  const int64_t units = a.M * ((a.K + fp8::kSpan - 1) / fp8::kSpan);
+  const int64_t warps = units < (int64_t)device_sm_count() * 64 ? units : (int64_t)device_sm_count() * 64;
+  const int grid = (int)((warps * 32 + 255) / 256);
+  fp8::amax_kernel<T><<<grid, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax);
+  fp8::quantize_kernel<T><<<grid, 256, 0, s>>>(x, a.x_stride, a.M, a.K, amax, a.q, a.x_scale);
   return cudaGetLastError();
+}
+
+cudaError_t launch_fp8_quantize(const tf_fp8_quant_args& a, cudaStream_t s) {
+  if (a.M == 0 || a.K == 0) return cudaSuccess;
+  switch (a.dtype) {
+    case TF_DTYPE_BF16: return quantize_t<__nv_bfloat16>(a, s);
+    case TF_DTYPE_F16: return quantize_t<__half>(a, s);
+    default: return quantize_t<float>(a, s);
+  }
 }
 
 namespace {
