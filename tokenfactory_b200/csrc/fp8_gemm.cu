@@ -179,6 +179,22 @@ __device__ __forceinline__ void tma_load_box(uint32_t dst, const CUtensorMap* ma
       : "memory");
 }
 
+// the epilogue warps wait most of the time: back off so that their polling leaves the issue
+// slots to the MMA and TMA threads on the same SM sub-partitions
+__device__ __forceinline__ bool wait_b_backoff(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((it & 15u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kSpinLimitNs) { *abort = 1; return false; }
+    }
+  }
+}
+
 template <typename TO>
 __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_args a,
                                                                  const __grid_constant__ CUtensorMap map_q,
@@ -272,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
       const int b = kb % kAcc;
       const float sc = sc_next;
       if (kb + 1 < nkb) sc_next = scale_of(kb + 1);  // in flight while this block's MMAs finish
-      ok = wait_b(&bars->pfull[b], (kb / kAcc) & 1, abort);
+      ok = wait_b_backoff(&bars->pfull[b], (kb / kAcc) & 1, abort);
       if (!ok) break;
       tc::fence_after_sync();
       float p[64];
