@@ -1055,6 +1055,36 @@ __device__ __forceinline__ uint64_t pack2(float x, float y) {
 }
 __device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+// Warp reduce-scatter of N values per lane (N a power of two <= 32): halving exchanges at lane
+// offsets 16, 8, ... leave lane L with the sum over the warp of value L >> (5 - log2 N), in
+// N - 1 + (5 - log2 N) shuffles instead of 5 N; every lane of the value's group holds the total.
+template <int N, int O>
+__device__ __forceinline__ void rs_step(float* a, int lane) {
+  if constexpr (O >= 1) {
+    if constexpr (N > 1) {
+      const bool up = (lane & O) != 0;
+#pragma unroll
+      for (int j = 0; j < N / 2; ++j) {
+        const float keep = up ? a[j + N / 2] : a[j];
+        const float send = up ? a[j] : a[j + N / 2];
+        a[j] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+      }
+      rs_step<N / 2, O / 2>(a, lane);
+    } else {
+      a[0] += __shfl_xor_sync(0xffffffffu, a[0], O);
+      rs_step<1, O / 2>(a, lane);
+    }
+  }
+}
+template <int N>
+__device__ __forceinline__ float reduce_scatter(const float (&v)[N], int lane) {
+  float a[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) a[j] = v[j];
+  rs_step<N, 16>(a, lane);
+  return a[0];
+}
+
 __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
@@ -1236,34 +1266,46 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       const T* rz = reinterpret_cast<const T*>(sb + oRaw + 3 * kRawPart);
       const int d = 4 * lane;               // this lane's 4 elements of a row
       const int blk = lane >> 4, ch = (lane & 15) >> 1, e8 = (lane & 1) * 4;
-#pragma unroll 4
-      for (int m = 0; m < 16; ++m) {
-        const int i = lw + 4 * m;
-        const bool live = i < c;
-        float q[4], k[4];
-        load4(rq + i * D + d, live, q);
-        load4(rk + i * D + d, live, k);
-        const uint2 v = live ? *reinterpret_cast<const uint2*>(rv + i * D + d) : make_uint2(0u, 0u);
-        float sq = 0.f, sk = 0.f;
+      // 8 rows at a time: the 16 squared norms (8 q, 8 k) of the rows reduce-scattered over the
+      // warp, one rsqrt per lane, then each row's factor broadcast back
+#pragma unroll 1
+      for (int bt = 0; bt < 2; ++bt) {
+        float q[8][4], k[8][4], part[16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) { sq = fmaf(q[e], q[e], sq); sk = fmaf(k[e], k[e], sk); }
-        sq = warp_sum(sq);
-        sk = warp_sum(sk);
+        for (int j = 0; j < 8; ++j) {
+          const int i = lw + 4 * (8 * bt + j);
+          const bool live = i < c;
+          load4(rq + i * D + d, live, q[j]);
+          load4(rk + i * D + d, live, k[j]);
+          const uint2 v = live ? *reinterpret_cast<const uint2*>(rv + i * D + d) : make_uint2(0u, 0u);
+          sts_v2(base + oV + (i * D + d) * 2, v.x, v.y);
+          float sq = 0.f, sk = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) { sq = fmaf(q[j][e], q[j][e], sq); sk = fmaf(k[j][e], k[j][e], sk); }
+          part[j] = sq;
+          part[8 + j] = sk;
+        }
         // x / max(|x|, 1e-12) as x * rsqrt(max(|x|^2, 1e-24)): no division on this path
-        const float iq = qscale * rsqrtf(fmaxf(sq, 1e-24f)), ik = rsqrtf(fmaxf(sk, 1e-24f));
-        uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
-        split2(k[0] * ik, k[1] * ik, kh0, kl0);
-        split2(k[2] * ik, k[3] * ik, kh1, kl1);
-        split2(q[0] * iq, q[1] * iq, qh0, ql0);
-        split2(q[2] * iq, q[3] * iq, qh1, ql1);
-        const int rk_ = i, rq_ = 64 + i;
-        const uint32_t ok_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rk_ & 7)) << 4) + e8 * 2;
-        const uint32_t oq_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rq_ & 7)) << 4) + e8 * 2;
-        sts_v2(base + oKQH + rk_ * 128 + ok_, kh0, kh1);
-        sts_v2(base + oKQL + rk_ * 128 + ok_, kl0, kl1);
-        sts_v2(base + oKQH + rq_ * 128 + oq_, qh0, qh1);
-        sts_v2(base + oKQL + rq_ * 128 + oq_, ql0, ql1);
-        sts_v2(base + oV + (i * D + d) * 2, v.x, v.y);
+        const float tot = reduce_scatter<16>(part, lane);
+        const float rn = ((lane >> 1) < 8 ? qscale : 1.f) * rsqrtf(fmaxf(tot, 1e-24f));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = lw + 4 * (8 * bt + j);
+          const float iq = __shfl_sync(0xffffffffu, rn, 2 * j);
+          const float ik = __shfl_sync(0xffffffffu, rn, 16 + 2 * j);
+          uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
+          split2(k[j][0] * ik, k[j][1] * ik, kh0, kl0);
+          split2(k[j][2] * ik, k[j][3] * ik, kh1, kl1);
+          split2(q[j][0] * iq, q[j][1] * iq, qh0, ql0);
+          split2(q[j][2] * iq, q[j][3] * iq, qh1, ql1);
+          const int rk_ = i, rq_ = 64 + i;
+          const uint32_t ok_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rk_ & 7)) << 4) + e8 * 2;
+          const uint32_t oq_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rq_ & 7)) << 4) + e8 * 2;
+          sts_v2(base + oKQH + rk_ * 128 + ok_, kh0, kh1);
+          sts_v2(base + oKQL + rk_ * 128 + ok_, kl0, kl1);
+          sts_v2(base + oKQH + rq_ * 128 + oq_, qh0, qh1);
+          sts_v2(base + oKQL + rq_ * 128 + oq_, ql0, ql1);
+        }
       }
       named_barrier(2, 128);  // graw complete
       if (lw == 0) {  // gamma = inclusive cumulative sum of g over the chunk, in log2 units
@@ -1545,41 +1587,41 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         const __nv_bfloat16* zs = reinterpret_cast<const __nv_bfloat16*>(sb + oZ);
         T* outb = reinterpret_cast<T*>(a.out) + (t0 + c0) * a.out_stride_tok + (int64_t)vh * D + 4 * lane;
         const bool ovec = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)(a.out_stride_tok * 2)) & 7) == 0;
+        // 8 rows at a time (rows warp + 4m): their squared norms reduce-scattered over the warp
 #pragma unroll 1
-        for (int i0 = warp; i0 < c; i0 += 8) {
-          const int i1 = i0 + 4;
-          const bool has1 = i1 < c;
-          float x0[4], x1[4], y0[4], y1[4];
-          load4(ot + i0 * D + 4 * lane, true, x0);
-          load4(ot + i1 * D + 4 * lane, has1, x1);
+        for (int bt = 0; bt < 2; ++bt) {
+          if (warp + 32 * bt >= c) break;
+          float x[8][4], part[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int i = warp + 4 * (8 * bt + j);
+            load4(ot + i * D + 4 * lane, i < c, x[j]);
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ss = fmaf(x[j][e], x[j][e], ss);
+            part[j] = ss;
+          }
+          float rr = 1.f;
           if (wn) {
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) { s0 = fmaf(x0[e], x0[e], s0); s1 = fmaf(x1[e], x1[e], s1); }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-              s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-            }
-            const float r0 = rsqrtf(s0 / (float)D + a.norm_eps), r1 = rsqrtf(s1 / (float)D + a.norm_eps);
-            const uint2 z0 = *reinterpret_cast<const uint2*>(zs + i0 * D + 4 * lane);
-            const uint2 z1 = has1 ? *reinterpret_cast<const uint2*>(zs + i1 * D + 4 * lane) : z0;
-            const __nv_bfloat16* z0e = reinterpret_cast<const __nv_bfloat16*>(&z0);
-            const __nv_bfloat16* z1e = reinterpret_cast<const __nv_bfloat16*>(&z1);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              y0[e] = wv[e] * (x0[e] * r0) * silu_fast(__bfloat162float(z0e[e]));
-              y1[e] = wv[e] * (x1[e] * r1) * silu_fast(__bfloat162float(z1e[e]));
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) { y0[e] = x0[e]; y1[e] = x1[e]; }
+            const float tot = reduce_scatter<8>(part, lane);
+            rr = rsqrtf(tot / (float)D + a.norm_eps);
           }
 #pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            if (r == 1 && !has1) break;
-            const float* y = r == 0 ? y0 : y1;
-            T* out = outb + (int64_t)(r == 0 ? i0 : i1) * a.out_stride_tok;
+          for (int j = 0; j < 8; ++j) {
+            const int i = warp + 4 * (8 * bt + j);
+            if (i >= c) break;
+            float y[4];
+            if (wn) {
+              const float r = __shfl_sync(0xffffffffu, rr, 4 * j);
+              const uint2 zu = *reinterpret_cast<const uint2*>(zs + i * D + 4 * lane);
+              const __nv_bfloat16* ze = reinterpret_cast<const __nv_bfloat16*>(&zu);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) y[e] = wv[e] * (x[j][e] * r) * silu_fast(__bfloat162float(ze[e]));
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) y[e] = x[j][e];
+            }
+            T* out = outb + (int64_t)i * a.out_stride_tok;
             if (ovec) {
               T pk[4];
 #pragma unroll
