@@ -320,6 +320,20 @@ __global__ void offsets_kernel(const int64_t* ext, int B, int64_t* start) {
   }
 }
 
+// order[k] = the request with the k-th longest extend (ties by index): the chunk kernel takes its
+// CTAs longest request first, so that the longest chains do not start last (scheduling only)
+__global__ void order_kernel(const int64_t* ext, int B, int32_t* order) {
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int64_t e = ext[b];
+    int rank = 0;
+    for (int o = 0; o < B; ++o) {
+      const int64_t eo = ext[o];
+      rank += (eo > e) || (eo == e && o < b);
+    }
+    order[rank] = b;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) conv_extend_kernel(tf_gdn_args a, const int64_t* start,
                                                           T* conv_out) {
@@ -1155,7 +1169,7 @@ __device__ __forceinline__ void load4(const T* p, bool live, float (&f)[4]) {
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, const int64_t* start,
-                                                               const T* conv_out) {
+                                                               const T* conv_out, const int32_t* order) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023) & ~1023u;
@@ -1175,8 +1189,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
 
-  const int b = blockIdx.x / a.num_v_heads;
-  const int vh = blockIdx.x - b * a.num_v_heads;
+  const int b = order[blockIdx.x / a.num_v_heads];
+  const int vh = blockIdx.x % a.num_v_heads;
   const int kh = vh / (a.num_v_heads / a.num_k_heads);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int key_dim = a.num_k_heads * D;
@@ -1661,6 +1675,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
 
 struct ExtWs {
   int64_t* start;  // [B+1]
+  int32_t* order;  // [B] requests by decreasing extend length
   void* conv_out;  // [T, conv_dim] of T
 };
 
@@ -1669,7 +1684,9 @@ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 inline ExtWs carve_ext(void* base, const tf_gdn_args& a) {
   ExtWs w;
   w.start = (int64_t*)base;
-  w.conv_out = (char*)base + align256((size_t)(a.batch_size + 1) * 8);
+  const size_t o1 = align256((size_t)(a.batch_size + 1) * 8);
+  w.order = (int32_t*)((char*)base + o1);
+  w.conv_out = (char*)base + o1 + align256((size_t)a.batch_size * 4);
   return w;
 }
 
@@ -1678,6 +1695,7 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
   ExtWs w = carve_ext(ws, a);
   const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
   offsets_kernel<<<1, 32, 0, s>>>(a.extend_lens, a.batch_size, w.start);
+  order_kernel<<<1, 256, 0, s>>>(a.extend_lens, a.batch_size, w.order);
   const bool conv_vec = sizeof(T) == 2 && a.conv_kernel == 4 && conv_dim % 4 == 0 &&
                         a.qkv_stride_tok % 4 == 0 && (reinterpret_cast<uintptr_t>(a.qkv) & 7) == 0;
   if (conv_vec) {
@@ -1701,7 +1719,7 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
     if (e != cudaSuccess) return e;
     tc_chunk::chunk_tc_kernel<T><<<a.batch_size * a.num_v_heads, tc_chunk::kThreads, tsmem, s>>>(
-        a, w.start, (const T*)w.conv_out);
+        a, w.start, (const T*)w.conv_out, w.order);
     return cudaGetLastError();
   }
   if constexpr (DK == DV && (DK == 64 || DK == 128)) {  // a7: chunked form
@@ -1760,7 +1778,8 @@ cudaError_t launch_gdn_decode(const tf_gdn_args& a, cudaStream_t s) {
 size_t gdn_extend_workspace(const tf_gdn_args& a) {
   const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
   const size_t eb = a.dtype == TF_DTYPE_F32 ? 4 : 2;
-  return gdn::align256((size_t)(a.batch_size + 1) * 8) + (size_t)a.num_tokens * conv_dim * eb;
+  return gdn::align256((size_t)(a.batch_size + 1) * 8) + gdn::align256((size_t)a.batch_size * 4) +
+         (size_t)a.num_tokens * conv_dim * eb;
 }
 
 cudaError_t launch_gdn_extend(const tf_gdn_args& a, void* ws, size_t ws_bytes, cudaStream_t s) {
