@@ -103,15 +103,18 @@ class ClockSampler:
         self._stop = threading.Event()
         self._thread = None
 
+    def _nvml_sample(self, handle, nv):
+        try:
+            mx = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
+            sm = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
+            self.lines.append(f"{sm}, {mx}, 0, {bits:#x}")
+        except Exception:  # noqa: BLE001 - a failed read is just a missing sample
+            pass
+
     def _nvml_loop(self, handle, nv):
-        mx = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
         while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
-                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
-                self.lines.append(f"{sm}, {mx}, 0, {bits:#x}")
-            except Exception:  # noqa: BLE001 - a failed read is just a missing sample
-                pass
+            self._nvml_sample(handle, nv)
             time.sleep(0.002)
 
     def __enter__(self):
@@ -120,6 +123,7 @@ class ClockSampler:
             nv.nvmlInit()
             idx = torch.cuda._get_nvml_device_index(self.gpu)
             handle = nv.nvmlDeviceGetHandleByIndex(idx)
+            self._nvml = (handle, nv)
             self._thread = threading.Thread(target=self._nvml_loop, args=(handle, nv), daemon=True)
             self._thread.start()
             return self
@@ -144,6 +148,8 @@ class ClockSampler:
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=5)
+            if not self.lines:  # a region too short for the thread to be scheduled: one read now
+                self._nvml_sample(*self._nvml)
         if self.proc is not None:
             self.proc.terminate()
             try:

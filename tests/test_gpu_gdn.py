@@ -116,6 +116,37 @@ def test_state_after_256_decode_steps_within_1e3():
     np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
 
 
+def test_decode_many_items_with_a_skipped_request():
+    """More (request, k-head) items than the persistent decode grid holds (800 items; 2 CTAs per
+    SM), so CTAs walk several items with the next item's state prefetched across the boundary.
+    Request 150 (items 300-301, the middle items of their CTAs on a 148-SM part) has an index out
+    of range: it is recorded and skipped, and every other request is stepped as the oracle steps
+    it."""
+    from tokenfactory_b200 import ops
+    B, bad = 400, 150
+    req = np.random.default_rng(90).permutation(B + 8)[:B].tolist()
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=[1] * B, req=req,
+                slots=B + 8, seed=91)
+    inp = C.gdn_inputs(spec)
+    t = _tensors(inp, "bf16")
+    t["req_pool_indices"][bad] = B + 8 + 5
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = ops.gdn_decode(t["qkv"], t["b"], t["a"], t["conv_weight"], t["A_log"], t["dt_bias"],
+                         t["conv_state"], t["ssm_state"], t["req_pool_indices"], z=t["z"],
+                         norm_weight=t["norm_weight"], num_k_heads=2, head_k_dim=128,
+                         head_v_dim=128, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 2  # TF_KERR_REQ_RANGE
+    keep = [i for i in range(B) if i != bad]
+    sub = dict(inp)
+    for k in ("qkv", "b", "a", "z"):
+        sub[k] = inp[k][keep]
+    orc, cs, ss = _oracle(dict(spec, req=[req[i] for i in keep], ext=[1] * len(keep)), sub, True)
+    assert_close(values(out, "bf16")[keep], orc, "bf16", what="decode, 800 items")
+    np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+    np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=1e-4, atol=1e-5)
+
+
 @pytest.mark.parametrize("ext", [[1, 300, 7, 64], [65, 1, 1, 129]])
 def test_extend_random_27b_heads_vs_oracle(ext):
     spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext,

@@ -27,6 +27,33 @@ template <> __device__ __forceinline__ __half from_f<__half>(float x) { return _
 // Round a float to the precision of T and back (models a torch op whose result tensor is T).
 template <typename T> __device__ __forceinline__ float round_to(float x) { return to_f(from_f<T>(x)); }
 
+// Two floats rounded to a 16-bit T by one paired conversion (the same round-to-nearest-even as
+// two from_f), packed with `a` in the low half; unpack_lo / unpack_hi read them back as floats.
+// Conversions issue on a narrow pipe, so rows of 16-bit values are rounded and kept in pairs.
+template <typename T> __device__ __forceinline__ uint32_t pack2_rn(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2_rn<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2_rn<__half>(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <typename T> __device__ __forceinline__ float unpack_lo(uint32_t u);
+template <typename T> __device__ __forceinline__ float unpack_hi(uint32_t u);
+template <> __device__ __forceinline__ float unpack_lo<__nv_bfloat16>(uint32_t u) {
+  return __uint_as_float(u << 16);
+}
+template <> __device__ __forceinline__ float unpack_hi<__nv_bfloat16>(uint32_t u) {
+  return __uint_as_float(u & 0xffff0000u);
+}
+template <> __device__ __forceinline__ float unpack_lo<__half>(uint32_t u) {
+  return __half2float(__ushort_as_half((unsigned short)(u & 0xffffu)));
+}
+template <> __device__ __forceinline__ float unpack_hi<__half>(uint32_t u) {
+  return __half2float(__ushort_as_half((unsigned short)(u >> 16)));
+}
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
 

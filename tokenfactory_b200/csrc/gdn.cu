@@ -41,12 +41,17 @@ struct TokenScalars {
   float alpha, beta, inv_nq, inv_nk, kq;  // inv_nq includes the dk**-0.5 scale
 };
 
+struct NoHook {
+  __device__ __forceinline__ void operator()() const {}
+};
+
 // One recurrent step on the register-resident state.  q_s/k_s hold RAW conv outputs (the 1/||.||
-// factors are applied here), v_s the v row.  Writes o (unrounded, fp32) to o_s.
-template <int DK, int DV>
+// factors are applied here), v_s the v row.  Writes o (unrounded, fp32) to o_s.  after_read() runs
+// once every element of S has been consumed by the first pass (its loads have completed).
+template <int DK, int DV, typename Hook = NoHook>
 __device__ __forceinline__ void state_step(float4 (&S)[DK / 8], const float* q_s, const float* k_s,
                                            const float* v_s, const TokenScalars& ts, float* red_s,
-                                           float* delta_s, float* o_s) {
+                                           float* delta_s, float* o_s, Hook after_read = Hook()) {
   using Y = Lay<DK, DV>;
   const int tid = threadIdx.x;
   const int cg = tid % Y::kCG, rg = tid / Y::kCG;
@@ -62,6 +67,7 @@ __device__ __forceinline__ void state_step(float4 (&S)[DK / 8], const float* q_s
   }
   reinterpret_cast<float4*>(red_s + (rg * 2 + 0) * DV)[cg] = pa;
   reinterpret_cast<float4*>(red_s + (rg * 2 + 1) * DV)[cg] = pc;
+  after_read();
   __syncthreads();
   if (tid < DV) {
     float sa = 0.f, sc = 0.f;
@@ -94,6 +100,31 @@ __device__ __forceinline__ void load_state(float4 (&S)[DK / 8], const float* st)
 #pragma unroll
   for (int r = 0; r < Y::kRPT; ++r)
     S[r] = __ldcs(reinterpret_cast<const float4*>(st + (size_t)(rg * Y::kRPT + r) * DV) + cg);
+}
+
+// cp.async of the state elements this thread owns into the same positions of `buf` (one group);
+// take_state waits for this thread's own copies only, so neither needs a CTA barrier
+template <int DK, int DV>
+__device__ __forceinline__ void prefetch_state(float* buf, const float* st) {
+  using Y = Lay<DK, DV>;
+  const int cg = threadIdx.x % Y::kCG, rg = threadIdx.x / Y::kCG;
+  const uint32_t b0 = smem_u32(buf);
+#pragma unroll
+  for (int r = 0; r < Y::kRPT; ++r) {
+    const size_t off = (size_t)(rg * Y::kRPT + r) * DV + 4 * cg;
+    cp_async16(b0 + 4 * (uint32_t)off, st + off);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int DK, int DV>
+__device__ __forceinline__ void take_state(float4 (&S)[DK / 8], const float* buf) {
+  using Y = Lay<DK, DV>;
+  const int cg = threadIdx.x % Y::kCG, rg = threadIdx.x / Y::kCG;
+  asm volatile("cp.async.wait_all;" ::: "memory");
+#pragma unroll
+  for (int r = 0; r < Y::kRPT; ++r)
+    S[r] = reinterpret_cast<const float4*>(buf + (size_t)(rg * Y::kRPT + r) * DV)[cg];
 }
 
 template <int DK, int DV>
@@ -180,6 +211,39 @@ __device__ __forceinline__ void write_output(const tf_gdn_args& a, int64_t t, in
   }
 }
 
+// write_output with silu(z) and the norm weight of the v-head already in shared memory (zs, ws:
+// DV floats each; same products in the same order, so the same bits)
+template <typename T, int DV>
+__device__ __forceinline__ void write_output_staged(const tf_gdn_args& a, int64_t t, int vh,
+                                                    const float* o_s, const float* zs,
+                                                    const float* ws) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp != 0) return;
+  T* out = reinterpret_cast<T*>(a.out) + t * a.out_stride_tok + (int64_t)vh * DV;
+  constexpr int PER = (DV + 31) / 32;
+  float x[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int j = lane + 32 * k;
+    x[k] = j < DV ? round_to<T>(o_s[j]) : 0.f;
+    ss = fmaf(x[k], x[k], ss);
+  }
+  if (a.z == nullptr) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k)
+      if (lane + 32 * k < DV) out[lane + 32 * k] = from_f<T>(x[k]);
+    return;
+  }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / (float)DV + a.norm_eps);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int j = lane + 32 * k;
+    if (j < DV) out[j] = from_f<T>(ws[j] * (x[k] * rs) * zs[j]);
+  }
+}
+
 // depthwise causal conv of one channel at in-request position i, then SiLU, with the reference's
 // double rounding to T.  window(p) = p >= 0 ? x[p] : state[K-1+p].
 template <typename T>
@@ -198,20 +262,25 @@ __device__ __forceinline__ float conv_channel(const tf_gdn_args& a, const T* xro
 }
 
 // ---------------------------------------------------------------------------------------------
-// decode: one CTA per (request, k-head)
+// decode: a persistent grid walks the (request, k-head) items
 // ---------------------------------------------------------------------------------------------
+// One CTA per item would leave its SM's load stream empty from its last v-head's step until the
+// next CTA's first state arrives; instead each CTA takes items blockIdx.x, + gridDim.x, ... and
+// keeps exactly one state in flight at all times: while v-head j of an item is stepped from
+// registers, pre_s receives the next one (head j+1, or head 0 of the CTA's next item, during
+// that item's conv).
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(2 * DV) decode_kernel(tf_gdn_args a) {
-  using Y = Lay<DK, DV>;
-  const int b = blockIdx.x / a.num_k_heads;
-  const int kh = blockIdx.x - b * a.num_k_heads;
-  const int vpk = a.num_v_heads / a.num_k_heads;
+__global__ void __launch_bounds__(2 * DV, 2) decode_kernel(tf_gdn_args a) {
+  const int Hk = a.num_k_heads;
+  const int vpk = a.num_v_heads / Hk;
+  const int n_items = a.batch_size * Hk;
   const int tid = threadIdx.x;
-  const int key_dim = a.num_k_heads * DK;
+  const int key_dim = Hk * DK;
   const int K = a.conv_kernel;
 
   extern __shared__ float sm[];
-  float* q_s = sm;                       // [DK]
+  float* pre_s = sm;                     // [DK][DV] the state in flight
+  float* q_s = sm + DK * DV;             // [DK]
   float* k_s = q_s + DK;                 // [DK]
   float* v_s = k_s + DK;                 // [vpk][DV]
   float* red_s = v_s + vpk * DV;         // [8][2][DV]
@@ -219,57 +288,96 @@ __global__ void __launch_bounds__(2 * DV) decode_kernel(tf_gdn_args a) {
   float* o_s = delta_s + DV;             // [DV]
   float* sc_s = o_s + DV;                // [4]
   float* gb_s = sc_s + 4;                // [vpk][2]
+  float* zs_s = gb_s + 2 * vpk;          // [vpk][DV] silu(z)
+  float* ws_s = zs_s + vpk * DV;         // [vpk][DV] norm weight
 
-  const int64_t slot = a.req_pool_indices[b];
-  if (slot < 0 || slot >= a.num_slots) {
-    if (tid == 0) record_err(a.err, TF_KERR_REQ_RANGE);
-    return;
-  }
-  float* st_base = a.ssm_state + slot * a.ssm_stride_slot;
-  float4 S[DK / 8];
-  load_state<DK, DV>(S, st_base + (size_t)(kh * vpk) * DK * DV);  // in flight during the conv
-
-  // causal conv of this CTA's channels; the CTA owns these conv_state rows
-  const T* x = reinterpret_cast<const T*>(a.qkv) + (int64_t)b * a.qkv_stride_tok;
-  T* cst = reinterpret_cast<T*>(a.conv_state) + slot * a.conv_stride_slot;
-  const int nch = 2 * DK + vpk * DV;
-  for (int e = tid; e < nch; e += blockDim.x) {
-    int c;
-    if (e < DK) c = kh * DK + e;
-    else if (e < 2 * DK) c = key_dim + kh * DK + (e - DK);
-    else c = 2 * key_dim + kh * vpk * DV + (e - 2 * DK);
-    float win[8];
-    for (int j = 0; j < K - 1; ++j) win[j] = to_f(cst[(int64_t)c * (K - 1) + j]);
-    const float xv = to_f(x[c]);
-    const T* w = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * K;
-    float acc = 0.f;
-    for (int j = 0; j < K - 1; ++j) acc = fmaf(to_f(w[j]), win[j], acc);
-    acc = fmaf(to_f(w[K - 1]), xv, acc);
-    if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
-    const float y = round_to<T>(silu_f(round_to<T>(acc)));
-    for (int j = 0; j + 1 < K - 1; ++j) cst[(int64_t)c * (K - 1) + j] = from_f<T>(win[j + 1]);
-    if (K > 1) cst[(int64_t)c * (K - 1) + K - 2] = x[c];
-    sm[e] = y;  // q_s | k_s | v_s are contiguous
-  }
-  if (tid < vpk) {
-    float g, be;
-    gate_values<T>(a, b, kh * vpk + tid, &g, &be);
-    gb_s[2 * tid] = g;
-    gb_s[2 * tid + 1] = be;
-  }
-  __syncthreads();
-  qk_norms<DK>(q_s, k_s, sc_s);
-  __syncthreads();
+  // the pool slot of item `it`, or -1 when out of range (the item is then skipped and recorded)
+  auto slot_of = [&](int it) -> int64_t {
+    if (it >= n_items) return -1;
+    const int64_t s = a.req_pool_indices[it / Hk];
+    return s >= 0 && s < a.num_slots ? s : -1;
+  };
+  auto state_ptr = [&](int64_t slot, int vh) -> const float* {
+    return a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * DK * DV;
+  };
   const float scale = rsqrtf((float)DK);
-  for (int j = 0; j < vpk; ++j) {
-    const int vh = kh * vpk + j;
-    if (j > 0) load_state<DK, DV>(S, st_base + (size_t)vh * DK * DV);
-    const TokenScalars ts = make_scalars(sc_s, scale, gb_s[2 * j], gb_s[2 * j + 1]);
-    state_step<DK, DV>(S, q_s, k_s, v_s + j * DV, ts, red_s, delta_s, o_s);
-    store_state<DK, DV>(S, st_base + (size_t)vh * DK * DV);
-    write_output<T, DV>(a, b, vh, o_s);
-    __syncthreads();  // o_s / delta_s reuse
+  int it = blockIdx.x;
+  int64_t slot = slot_of(it);
+  if (slot >= 0) prefetch_state<DK, DV>(pre_s, state_ptr(slot, (it % Hk) * vpk));
+  for (; it < n_items; it += gridDim.x) {
+    const int b = it / Hk, kh = it - (it / Hk) * Hk;
+    const int nxt = it + gridDim.x;
+    const int64_t nslot = slot_of(nxt);
+    if (slot < 0) {  // nothing of this item was prefetched; start the next one's stream
+      if (tid == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+      if (nslot >= 0) prefetch_state<DK, DV>(pre_s, state_ptr(nslot, (nxt % Hk) * vpk));
+      slot = nslot;
+      continue;
+    }
+    __syncthreads();  // the previous item's readers of q_s .. ws_s are done
+
+    // causal conv of this item's channels; the item owns these conv_state rows
+    const T* x = reinterpret_cast<const T*>(a.qkv) + (int64_t)b * a.qkv_stride_tok;
+    T* cst = reinterpret_cast<T*>(a.conv_state) + slot * a.conv_stride_slot;
+    const int nch = 2 * DK + vpk * DV;
+    for (int e = tid; e < nch; e += blockDim.x) {
+      int c;
+      if (e < DK) c = kh * DK + e;
+      else if (e < 2 * DK) c = key_dim + kh * DK + (e - DK);
+      else c = 2 * key_dim + kh * vpk * DV + (e - 2 * DK);
+      float win[8];
+      for (int j = 0; j < K - 1; ++j) win[j] = to_f(cst[(int64_t)c * (K - 1) + j]);
+      const float xv = to_f(x[c]);
+      const T* w = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * K;
+      float acc = 0.f;
+      for (int j = 0; j < K - 1; ++j) acc = fmaf(to_f(w[j]), win[j], acc);
+      acc = fmaf(to_f(w[K - 1]), xv, acc);
+      if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
+      const float y = round_to<T>(silu_f(round_to<T>(acc)));
+      for (int j = 0; j + 1 < K - 1; ++j) cst[(int64_t)c * (K - 1) + j] = from_f<T>(win[j + 1]);
+      if (K > 1) cst[(int64_t)c * (K - 1) + K - 2] = x[c];
+      q_s[e] = y;  // q_s | k_s | v_s are contiguous
+    }
+    if (tid < vpk) {
+      float g, be;
+      gate_values<T>(a, b, kh * vpk + tid, &g, &be);
+      gb_s[2 * tid] = g;
+      gb_s[2 * tid + 1] = be;
+    }
+    if (a.z != nullptr) {  // the output gate's operands, off the per-head critical path
+      const T* zr = reinterpret_cast<const T*>(a.z) + (int64_t)b * a.z_stride_tok +
+                    (int64_t)kh * vpk * DV;
+      const bool shared_w = a.norm_weight_len == DV;
+      const T* wr = reinterpret_cast<const T*>(a.norm_weight) + (shared_w ? 0 : (int64_t)kh * vpk * DV);
+      for (int e = tid; e < vpk * DV; e += blockDim.x) {
+        zs_s[e] = silu_f(to_f(zr[e]));
+        ws_s[e] = to_f(wr[shared_w ? e % DV : e]);
+      }
+    }
+    __syncthreads();
+    qk_norms<DK>(q_s, k_s, sc_s);
+    __syncthreads();
+    // No barrier closes a v-head: red_s and delta_s of head j+1 are written only after the first
+    // barrier of its step, which every thread reaches after its last read of head j's, and warp 0
+    // reads o_s (write_output_staged) before it reaches that barrier.
+    for (int j = 0; j < vpk; ++j) {
+      const int vh = kh * vpk + j;
+      float4 S[DK / 8];
+      take_state<DK, DV>(S, pre_s);
+      // the next state is requested once this thread's reads of pre_s have been consumed
+      const float* next = j + 1 < vpk ? state_ptr(slot, vh + 1)
+                                      : (nslot >= 0 ? state_ptr(nslot, (nxt % Hk) * vpk) : nullptr);
+      auto refill = [&]() {
+        if (next != nullptr) prefetch_state<DK, DV>(pre_s, next);
+      };
+      const TokenScalars ts = make_scalars(sc_s, scale, gb_s[2 * j], gb_s[2 * j + 1]);
+      state_step<DK, DV>(S, q_s, k_s, v_s + j * DV, ts, red_s, delta_s, o_s, refill);
+      store_state<DK, DV>(S, a.ssm_state + slot * a.ssm_stride_slot + (size_t)vh * DK * DV);
+      write_output_staged<T, DV>(a, b, vh, o_s, zs_s + j * DV, ws_s + j * DV);
+    }
+    slot = nslot;
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight into shared memory at exit
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -545,14 +653,19 @@ __global__ void __launch_bounds__(kConvVecThreads, 4) conv4_vec_kernel(tf_gdn_ar
       }
     }
     const T* xv = reinterpret_cast<const T*>(&win[i + 3]);
-    T out[4];
+    float acc[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float acc = fmaf(w[e][0], h[0][e], fmaf(w[e][1], h[1][e],
-                       fmaf(w[e][2], h[2][e], fmaf(w[e][3], to_f(xv[e]), bias[e]))));
-      out[e] = from_f<T>(round_to<T>(silu_rt(round_to<T>(acc))));
+    for (int e = 0; e < 4; ++e)
+      acc[e] = fmaf(w[e][0], h[0][e], fmaf(w[e][1], h[1][e],
+                    fmaf(w[e][2], h[2][e], fmaf(w[e][3], to_f(xv[e]), bias[e]))));
+    // both roundings in pairs (one conversion per two channels)
+    uint32_t ow[2];
+#pragma unroll
+    for (int e2 = 0; e2 < 2; ++e2) {
+      const uint32_t r = pack2_rn<T>(acc[2 * e2], acc[2 * e2 + 1]);
+      ow[e2] = pack2_rn<T>(silu_rt(unpack_lo<T>(r)), silu_rt(unpack_hi<T>(r)));
     }
-    __stcs(reinterpret_cast<uint2*>(conv_out + t * conv_dim + c), *reinterpret_cast<const uint2*>(out));
+    __stcs(reinterpret_cast<uint2*>(conv_out + t * conv_dim + c), make_uint2(ow[0], ow[1]));
   }
 }
 
@@ -1003,7 +1116,7 @@ __global__ void __launch_bounds__(256, 1) chunk_extend_kernel(tf_gdn_args a, con
 
 template <int DK, int DV>
 constexpr size_t decode_smem(int vpk) {
-  return (size_t)(2 * DK + vpk * DV + 16 * DV + 2 * DV + 4 + 2 * vpk) * 4;
+  return (size_t)(DK * DV + 2 * DK + 3 * vpk * DV + 16 * DV + 2 * DV + 4 + 2 * vpk) * 4;
 }
 
 template <typename T, int DK, int DV>
@@ -1013,7 +1126,16 @@ cudaError_t launch_decode_t(const tf_gdn_args& a, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, DK, DV>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  decode_kernel<T, DK, DV><<<a.batch_size * a.num_k_heads, 2 * DV, smem, s>>>(a);
+  // persistent: as many CTAs as fit at once (2 per SM by the launch bounds, fewer when the
+  // shared memory of a large vpk does not allow it), never more than there are items
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<T, DK, DV>, 2 * DV, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t items = (int64_t)a.batch_size * a.num_k_heads;
+  const int64_t cap = (int64_t)device_sm_count() * per_sm;
+  const int grid = (int)(items < cap ? items : cap);
+  decode_kernel<T, DK, DV><<<grid, 2 * DV, smem, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -16,6 +16,7 @@ namespace prologue {
 
 constexpr int kThreads = 256;
 constexpr int kMaxD = 256;
+constexpr int kTPC = 4;  // tokens per CTA of the vector form
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) prologue_kernel(tf_attn_prologue_args a) {
@@ -121,84 +122,191 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(tf_attn_prologue_arg
 // access at D 256 in bf16), so the rotation partner d +- half sits in lane l ^ (half / E) at the
 // same position.  Needs rows aligned to E elements and half a multiple of E with half / E a power
 // of two below 32 (rotary_dim = D/4 at D 64/128/256).
+//
+// A CTA takes TPC consecutive tokens: one preamble (cos/sin of its tokens, their pool slots) and
+// one barrier for all of them, then its warps walk the TPC x (Hq + 2 Hkv) rows (row ri is head row
+// ri / TPC of token ri % TPC) with a ring of PF rows in flight per warp.  The norm weights sit in
+// registers, cos/sin are read as vectors, and the rotation partners of 16-bit rows cross lanes two
+// per shuffle: about a third of the shared/shuffle traffic of one token per CTA.
 template <int BYTES> struct VecT;
 template <> struct VecT<4> { using type = uint32_t; };
 template <> struct VecT<8> { using type = uint2; };
 template <> struct VecT<16> { using type = uint4; };
-struct alignas(32) Vec32 { uint4 lo, hi; };  // fp32 at D 256: takes the strided path (vec_ok)
-template <> struct VecT<32> { using type = Vec32; };
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads) prologue_vec_kernel(tf_attn_prologue_args a) {
+template <typename V>
+__device__ __forceinline__ V ld_stream(const void* p) {
+  if constexpr (sizeof(V) == 16) return __ldcs(reinterpret_cast<const uint4*>(p));
+  else if constexpr (sizeof(V) == 8) return __ldcs(reinterpret_cast<const uint2*>(p));
+  else return __ldcs(reinterpret_cast<const unsigned int*>(p));
+}
+
+// E consecutive cos and sin values of a token from shared memory (16-byte loads when E % 4 == 0;
+// the first index is a multiple of E)
+template <int E>
+__device__ __forceinline__ void load_cos_sin(const float* cp, const float* sp, float (&c)[E],
+                                             float (&sv)[E]) {
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < E / 4; ++k) {
+      const float4 c4 = reinterpret_cast<const float4*>(cp)[k];
+      const float4 s4 = reinterpret_cast<const float4*>(sp)[k];
+      c[4 * k] = c4.x; c[4 * k + 1] = c4.y; c[4 * k + 2] = c4.z; c[4 * k + 3] = c4.w;
+      sv[4 * k] = s4.x; sv[4 * k + 1] = s4.y; sv[4 * k + 2] = s4.z; sv[4 * k + 3] = s4.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) { c[e] = cp[e]; sv[e] = sp[e]; }
+  }
+}
+
+template <typename T, int D, int TPC>
+__global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prologue_args a) {
   constexpr int E = D / 32;
   constexpr int NW = kThreads / 32;
+  constexpr int PF = 4;
   using V = typename VecT<E * (int)sizeof(T)>::type;
-  __shared__ float cs[kMaxD / 2], sn[kMaxD / 2];
-  __shared__ int64_t s_loc;
-  const int64_t t = blockIdx.x;
+  __shared__ __align__(16) float cs[TPC][kMaxD / 2];
+  __shared__ __align__(16) float sn[TPC][kMaxD / 2];
+  __shared__ int64_t s_loc[TPC];
+  const int64_t t0 = (int64_t)blockIdx.x * TPC;
+  const int ntok = a.num_tokens - t0 < TPC ? (int)(a.num_tokens - t0) : TPC;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int Hq = a.num_q_heads, Hkv = a.num_kv_heads;
-  const int nrows = Hq + 2 * Hkv;
+  const int R = (Hq + 2 * Hkv) * TPC;
   const int d0 = lane * E;
-  auto src_of = [&](int r) -> const T* {
-    if (r < Hq) return reinterpret_cast<const T*>(a.q) + t * a.q_stride_tok + (int64_t)r * a.q_stride_head;
-    const bool isk = r < Hq + Hkv;
-    const int h = isk ? r - Hq : r - Hq - Hkv;
-    return reinterpret_cast<const T*>(isk ? a.k : a.v) + t * (isk ? a.k_stride_tok : a.v_stride_tok) +
-           (int64_t)h * (isk ? a.k_stride_head : a.v_stride_head);
+  auto load = [&](int ri) -> V {
+    const int tt = ri % TPC, r = ri / TPC;
+    if (ri >= R || tt >= ntok) return V();
+    const int64_t t = t0 + tt;
+    const T* src;
+    if (r < Hq) {
+      src = reinterpret_cast<const T*>(a.q) + t * a.q_stride_tok + (int64_t)r * a.q_stride_head;
+    } else {
+      const bool isk = r < Hq + Hkv;
+      const int h = isk ? r - Hq : r - Hq - Hkv;
+      src = reinterpret_cast<const T*>(isk ? a.k : a.v) + t * (isk ? a.k_stride_tok : a.v_stride_tok) +
+            (int64_t)h * (isk ? a.k_stride_head : a.v_stride_head);
+    }
+    return ld_stream<V>(src + d0);
   };
-  // this warp's first row is loading while the token's cos/sin and slot are prepared
-  V cur = warp < nrows ? *reinterpret_cast<const V*>(src_of(warp) + d0) : V();
+  // this warp's first rows are loading while the tokens' cos/sin and slots are prepared
+  V ring[PF];
+#pragma unroll
+  for (int u = 0; u < PF; ++u) ring[u] = load(warp + u * NW);
   const int half = a.rotary_dim / 2;
-  for (int j = tid; j < half; j += kThreads) {
+  for (int j = tid; j < TPC * half; j += kThreads) {
+    const int tt = j / half, jj = j - tt * half;
+    if (tt >= ntok) continue;
     int prow = 0;
     if (a.pos_rows == 3) {
       if (a.mrope_interleaved) {
-        const int m = j % 3;
-        if (m == 1 && j < 3 * a.mrope_section[1]) prow = 1;
-        else if (m == 2 && j < 3 * a.mrope_section[2]) prow = 2;
+        const int m = jj % 3;
+        if (m == 1 && jj < 3 * a.mrope_section[1]) prow = 1;
+        else if (m == 2 && jj < 3 * a.mrope_section[2]) prow = 2;
       } else {
-        prow = j < a.mrope_section[0] ? 0 : (j < a.mrope_section[0] + a.mrope_section[1] ? 1 : 2);
+        prow = jj < a.mrope_section[0] ? 0 : (jj < a.mrope_section[0] + a.mrope_section[1] ? 1 : 2);
       }
     }
-    const float f = (float)a.positions[prow * a.pos_stride + t] * a.inv_freq[j];
-    cs[j] = round_to<T>(cosf(f));
-    sn[j] = round_to<T>(sinf(f));
+    const float f = (float)a.positions[prow * a.pos_stride + t0 + tt] * a.inv_freq[jj];
+    float sf, cf;
+    sincosf(f, &sf, &cf);
+    cs[tt][jj] = round_to<T>(cf);
+    sn[tt][jj] = round_to<T>(sf);
   }
-  if (tid == 32) {
-    int64_t loc = a.out_cache_loc[t];
+  if (tid >= 32 && tid < 32 + TPC && tid - 32 < ntok) {
+    int64_t loc = a.out_cache_loc[t0 + tid - 32];
     if (loc < 0) loc += a.num_slots;  // torch index semantics
     if (loc < 0 || loc >= a.num_slots) {
       record_err(a.err, TF_KERR_SLOT_RANGE);
       loc = -1;
     }
-    s_loc = loc;
+    s_loc[tid - 32] = loc;
+  }
+  float wq[E], wk[E];
+  const bool wf32 = a.norm_weight_dtype == TF_DTYPE_F32;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    wq[e] = wf32 ? reinterpret_cast<const float*>(a.q_norm_weight)[d0 + e]
+                 : to_f(reinterpret_cast<const T*>(a.q_norm_weight)[d0 + e]);
+    wk[e] = wf32 ? reinterpret_cast<const float*>(a.k_norm_weight)[d0 + e]
+                 : to_f(reinterpret_cast<const T*>(a.k_norm_weight)[d0 + e]);
   }
   __syncthreads();
-  const int64_t loc = s_loc;
-  const bool wf32 = a.norm_weight_dtype == TF_DTYPE_F32;
   const int pmask = half / E;  // rotation partner: lane ^ pmask
   const bool rotates = d0 < 2 * half, lower = d0 < half;
-  for (int r = warp; r < nrows; r += NW) {
-    const V nxt = r + NW < nrows ? *reinterpret_cast<const V*>(src_of(r + NW) + d0) : V();
-    T* dst;
-    bool isv = false;
-    if (r < Hq) {
-      dst = reinterpret_cast<T*>(a.q_out) + t * a.q_out_stride_tok + (int64_t)r * a.q_out_stride_head;
-    } else {
-      const bool isk = r < Hq + Hkv;
-      const int h = isk ? r - Hq : r - Hq - Hkv;
-      dst = loc < 0 ? nullptr
-                    : reinterpret_cast<T*>(isk ? a.k_buffer : a.v_buffer) + loc * a.buf_stride_slot +
-                          (int64_t)h * a.buf_stride_head;
-      isv = !isk;
-    }
-    if (dst != nullptr) {
-      if (isv) {
-        *reinterpret_cast<V*>(dst + d0) = cur;  // v: copied as is
+  const int j0 = lower ? d0 : d0 - half;
+  for (int base = warp; base < R; base += PF * NW) {
+#pragma unroll
+    for (int u = 0; u < PF; ++u) {
+      const int ri = base + u * NW;
+      if (ri >= R) break;
+      const V cur = ring[u];
+      ring[u] = load(ri + PF * NW);
+      const int tt = ri % TPC, r = ri / TPC;
+      if (tt >= ntok) continue;
+      const int64_t t = t0 + tt;
+      T* dst;
+      bool isv = false;
+      if (r < Hq) {
+        dst = reinterpret_cast<T*>(a.q_out) + t * a.q_out_stride_tok + (int64_t)r * a.q_out_stride_head;
+      } else {
+        const int64_t loc = s_loc[tt];
+        const bool isk = r < Hq + Hkv;
+        const int h = isk ? r - Hq : r - Hq - Hkv;
+        if (loc < 0) continue;
+        dst = reinterpret_cast<T*>(isk ? a.k_buffer : a.v_buffer) + loc * a.buf_stride_slot +
+              (int64_t)h * a.buf_stride_head;
+        isv = !isk;
+      }
+      if (isv) {  // v: copied as is
+        *reinterpret_cast<V*>(dst + d0) = cur;
+        continue;
+      }
+      const bool isq = r < Hq;
+      V outv;
+      if constexpr (sizeof(T) == 2) {
+        // 16-bit rows stay in packed pairs: each rounding is one paired conversion
+        constexpr int W2 = E / 2;
+        const uint32_t* xw = reinterpret_cast<const uint32_t*>(&cur);
+        float x[E];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < W2; ++i) {
+          x[2 * i] = unpack_lo<T>(xw[i]);
+          x[2 * i + 1] = unpack_hi<T>(xw[i]);
+          ss = fmaf(x[2 * i], x[2 * i], ss);
+          ss = fmaf(x[2 * i + 1], x[2 * i + 1], ss);
+        }
+        ss = warp_sum(ss);
+        const float rs = rsqrtf(ss / (float)D + a.eps);
+        uint32_t yw[W2], pw[W2];
+#pragma unroll
+        for (int i = 0; i < W2; ++i) {
+          yw[i] = pack2_rn<T>((isq ? wq[2 * i] : wk[2 * i]) * (x[2 * i] * rs),
+                              (isq ? wq[2 * i + 1] : wk[2 * i + 1]) * (x[2 * i + 1] * rs));
+          pw[i] = __shfl_xor_sync(0xffffffffu, yw[i], pmask);  // the rotation partner's pair
+        }
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&outv);
+        if (rotates) {
+          float c[E], sv[E];
+          load_cos_sin<E>(&cs[tt][j0], &sn[tt][j0], c, sv);
+#pragma unroll
+          for (int i = 0; i < W2; ++i) {
+            const float p0 = unpack_lo<T>(pw[i]), p1 = unpack_hi<T>(pw[i]);
+            const uint32_t t1 = pack2_rn<T>(unpack_lo<T>(yw[i]) * c[2 * i],
+                                            unpack_hi<T>(yw[i]) * c[2 * i + 1]);
+            const uint32_t t2 = pack2_rn<T>((lower ? -p0 : p0) * sv[2 * i],
+                                            (lower ? -p1 : p1) * sv[2 * i + 1]);
+            ow[i] = pack2_rn<T>(unpack_lo<T>(t1) + unpack_lo<T>(t2),
+                                unpack_hi<T>(t1) + unpack_hi<T>(t2));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < W2; ++i) ow[i] = yw[i];
+        }
       } else {
         const T* xe = reinterpret_cast<const T*>(&cur);
-        float x[E];
+        float x[E], y[E], p[E];
         float ss = 0.f;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
@@ -207,26 +315,26 @@ __global__ void __launch_bounds__(kThreads) prologue_vec_kernel(tf_attn_prologue
         }
         ss = warp_sum(ss);
         const float rs = rsqrtf(ss / (float)D + a.eps);
-        const void* w = r < Hq ? a.q_norm_weight : a.k_norm_weight;
-        V outv;
-        T* oe = reinterpret_cast<T*>(&outv);
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const float wv = wf32 ? reinterpret_cast<const float*>(w)[d0 + e]
-                                : to_f(reinterpret_cast<const T*>(w)[d0 + e]);
-          const float y = round_to<T>(wv * (x[e] * rs));
-          const float p = __shfl_xor_sync(0xffffffffu, y, pmask);
-          float o = y;
-          if (rotates) {
-            const int j = (lower ? d0 : d0 - half) + e;
-            o = round_to<T>(round_to<T>(y * cs[j]) + round_to<T>((lower ? -p : p) * sn[j]));
-          }
-          oe[e] = from_f<T>(o);
+          y[e] = round_to<T>((isq ? wq[e] : wk[e]) * (x[e] * rs));
+          p[e] = __shfl_xor_sync(0xffffffffu, y[e], pmask);
         }
-        *reinterpret_cast<V*>(dst + d0) = outv;
+        T* oe = reinterpret_cast<T*>(&outv);
+        if (rotates) {
+          float c[E], sv[E];
+          load_cos_sin<E>(&cs[tt][j0], &sn[tt][j0], c, sv);
+#pragma unroll
+          for (int e = 0; e < E; ++e)
+            oe[e] = from_f<T>(round_to<T>(round_to<T>(y[e] * c[e]) +
+                                          round_to<T>((lower ? -p[e] : p[e]) * sv[e])));
+        } else {
+#pragma unroll
+          for (int e = 0; e < E; ++e) oe[e] = from_f<T>(y[e]);
+        }
       }
+      *reinterpret_cast<V*>(dst + d0) = outv;
     }
-    cur = nxt;
   }
 }
 
@@ -252,10 +360,13 @@ template <typename T>
 static cudaError_t launch_t(const tf_attn_prologue_args& a, cudaStream_t s) {
   const unsigned g = (unsigned)a.num_tokens;
   if (vec_ok<T>(a)) {
+    const unsigned gv = (unsigned)((a.num_tokens + kTPC - 1) / kTPC);
     switch (a.head_dim) {
-      case 64: prologue_vec_kernel<T, 64><<<g, kThreads, 0, s>>>(a); break;
-      case 128: prologue_vec_kernel<T, 128><<<g, kThreads, 0, s>>>(a); break;
-      default: prologue_vec_kernel<T, 256><<<g, kThreads, 0, s>>>(a); break;
+      case 64: prologue_vec_kernel<T, 64, kTPC><<<gv, kThreads, 0, s>>>(a); break;
+      case 128: prologue_vec_kernel<T, 128, kTPC><<<gv, kThreads, 0, s>>>(a); break;
+      default:  // 16-bit only: fp32 rows of 256 need 32 bytes per lane and take the strided form
+        if constexpr (sizeof(T) == 2) prologue_vec_kernel<T, 256, kTPC><<<gv, kThreads, 0, s>>>(a);
+        break;
     }
     return cudaGetLastError();
   }
