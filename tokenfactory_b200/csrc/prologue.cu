@@ -164,6 +164,8 @@ __global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prolo
   constexpr int E = D / 32;
   constexpr int NW = kThreads / 32;
   constexpr int PF = 4;
+  static_assert(NW % TPC == 0, "a warp serves one token");
+  constexpr int RSTEP = NW / TPC;  // head rows between a warp's consecutive rows
   using V = typename VecT<E * (int)sizeof(T)>::type;
   __shared__ __align__(16) float cs[TPC][kMaxD / 2];
   __shared__ __align__(16) float sn[TPC][kMaxD / 2];
@@ -172,31 +174,30 @@ __global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prolo
   const int ntok = a.num_tokens - t0 < TPC ? (int)(a.num_tokens - t0) : TPC;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int Hq = a.num_q_heads, Hkv = a.num_kv_heads;
-  const int R = (Hq + 2 * Hkv) * TPC;
+  const int nrows = Hq + 2 * Hkv;
   const int d0 = lane * E;
-  auto load = [&](int ri) -> V {
-    const int tt = ri % TPC, r = ri / TPC;
-    if (ri >= R || tt >= ntok) return V();
-    const int64_t t = t0 + tt;
-    const T* src;
-    if (r < Hq) {
-      src = reinterpret_cast<const T*>(a.q) + t * a.q_stride_tok + (int64_t)r * a.q_stride_head;
-    } else {
-      const bool isk = r < Hq + Hkv;
-      const int h = isk ? r - Hq : r - Hq - Hkv;
-      src = reinterpret_cast<const T*>(isk ? a.k : a.v) + t * (isk ? a.k_stride_tok : a.v_stride_tok) +
-            (int64_t)h * (isk ? a.k_stride_head : a.v_stride_head);
-    }
-    return ld_stream<V>(src + d0);
+  // warp w serves token tt = w % TPC, head rows r0, r0 + RSTEP, ... (q heads, then k, then v)
+  const int tt = warp % TPC, r0 = warp / TPC;
+  const bool live = tt < ntok;  // warp-uniform
+  const int64_t t = t0 + tt;
+  const T* q_src = reinterpret_cast<const T*>(a.q) + t * a.q_stride_tok + d0;
+  const T* k_src = reinterpret_cast<const T*>(a.k) + t * a.k_stride_tok + d0;
+  const T* v_src = reinterpret_cast<const T*>(a.v) + t * a.v_stride_tok + d0;
+  auto load = [&](int r) -> V {
+    if (!live || r >= nrows) return V();
+    const T* src = r < Hq ? q_src + (int64_t)r * a.q_stride_head
+                 : r < Hq + Hkv ? k_src + (int64_t)(r - Hq) * a.k_stride_head
+                                : v_src + (int64_t)(r - Hq - Hkv) * a.v_stride_head;
+    return ld_stream<V>(src);
   };
   // this warp's first rows are loading while the tokens' cos/sin and slots are prepared
   V ring[PF];
 #pragma unroll
-  for (int u = 0; u < PF; ++u) ring[u] = load(warp + u * NW);
+  for (int u = 0; u < PF; ++u) ring[u] = load(r0 + u * RSTEP);
   const int half = a.rotary_dim / 2;
   for (int j = tid; j < TPC * half; j += kThreads) {
-    const int tt = j / half, jj = j - tt * half;
-    if (tt >= ntok) continue;
+    const int jt = j / half, jj = j - jt * half;
+    if (jt >= ntok) continue;
     int prow = 0;
     if (a.pos_rows == 3) {
       if (a.mrope_interleaved) {
@@ -207,11 +208,11 @@ __global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prolo
         prow = jj < a.mrope_section[0] ? 0 : (jj < a.mrope_section[0] + a.mrope_section[1] ? 1 : 2);
       }
     }
-    const float f = (float)a.positions[prow * a.pos_stride + t0 + tt] * a.inv_freq[jj];
+    const float f = (float)a.positions[prow * a.pos_stride + t0 + jt] * a.inv_freq[jj];
     float sf, cf;
     sincosf(f, &sf, &cf);
-    cs[tt][jj] = round_to<T>(cf);
-    sn[tt][jj] = round_to<T>(sf);
+    cs[jt][jj] = round_to<T>(cf);
+    sn[jt][jj] = round_to<T>(sf);
   }
   if (tid >= 32 && tid < 32 + TPC && tid - 32 < ntok) {
     int64_t loc = a.out_cache_loc[t0 + tid - 32];
@@ -232,35 +233,35 @@ __global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prolo
                  : to_f(reinterpret_cast<const T*>(a.k_norm_weight)[d0 + e]);
   }
   __syncthreads();
+  if (!live) return;
+  const int64_t loc = s_loc[tt];
+  T* q_dst = reinterpret_cast<T*>(a.q_out) + t * a.q_out_stride_tok + d0;
+  T* k_dst = loc < 0 ? nullptr : reinterpret_cast<T*>(a.k_buffer) + loc * a.buf_stride_slot + d0;
+  T* v_dst = loc < 0 ? nullptr : reinterpret_cast<T*>(a.v_buffer) + loc * a.buf_stride_slot + d0;
   const int pmask = half / E;  // rotation partner: lane ^ pmask
   const bool rotates = d0 < 2 * half, lower = d0 < half;
   const int j0 = lower ? d0 : d0 - half;
-  for (int base = warp; base < R; base += PF * NW) {
+  // rotary_dim 64 at D 256 (the 0.25 partial rotation): the 32 bf16 pairs of the rotated dims sit
+  // in lanes 0-7; they are spread one pair per lane for the rotation and gathered back, so the
+  // rotation's roundings run on all 32 lanes instead of 8
+  const bool spread = sizeof(T) == 2 && E == 8 && half == 32;
+  for (int m0 = 0; r0 + m0 * RSTEP < nrows; m0 += PF) {
 #pragma unroll
     for (int u = 0; u < PF; ++u) {
-      const int ri = base + u * NW;
-      if (ri >= R) break;
+      const int r = r0 + (m0 + u) * RSTEP;
+      if (r >= nrows) break;
       const V cur = ring[u];
-      ring[u] = load(ri + PF * NW);
-      const int tt = ri % TPC, r = ri / TPC;
-      if (tt >= ntok) continue;
-      const int64_t t = t0 + tt;
+      ring[u] = load(r + PF * RSTEP);
       T* dst;
-      bool isv = false;
       if (r < Hq) {
-        dst = reinterpret_cast<T*>(a.q_out) + t * a.q_out_stride_tok + (int64_t)r * a.q_out_stride_head;
-      } else {
-        const int64_t loc = s_loc[tt];
-        const bool isk = r < Hq + Hkv;
-        const int h = isk ? r - Hq : r - Hq - Hkv;
-        if (loc < 0) continue;
-        dst = reinterpret_cast<T*>(isk ? a.k_buffer : a.v_buffer) + loc * a.buf_stride_slot +
-              (int64_t)h * a.buf_stride_head;
-        isv = !isk;
-      }
-      if (isv) {  // v: copied as is
-        *reinterpret_cast<V*>(dst + d0) = cur;
+        dst = q_dst + (int64_t)r * a.q_out_stride_head;
+      } else if (loc < 0) {
         continue;
+      } else if (r >= Hq + Hkv) {  // v: copied as is
+        *reinterpret_cast<V*>(v_dst + (int64_t)(r - Hq - Hkv) * a.buf_stride_head) = cur;
+        continue;
+      } else {
+        dst = k_dst + (int64_t)(r - Hq) * a.buf_stride_head;
       }
       const bool isq = r < Hq;
       V outv;
@@ -279,30 +280,59 @@ __global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prolo
         }
         ss = warp_sum(ss);
         const float rs = rsqrtf(ss / (float)D + a.eps);
-        uint32_t yw[W2], pw[W2];
+        uint32_t yw[W2];
 #pragma unroll
-        for (int i = 0; i < W2; ++i) {
+        for (int i = 0; i < W2; ++i)
           yw[i] = pack2_rn<T>((isq ? wq[2 * i] : wk[2 * i]) * (x[2 * i] * rs),
                               (isq ? wq[2 * i + 1] : wk[2 * i + 1]) * (x[2 * i + 1] * rs));
-          pw[i] = __shfl_xor_sync(0xffffffffu, yw[i], pmask);  // the rotation partner's pair
-        }
         uint32_t* ow = reinterpret_cast<uint32_t*>(&outv);
-        if (rotates) {
-          float c[E], sv[E];
-          load_cos_sin<E>(&cs[tt][j0], &sn[tt][j0], c, sv);
+        if (spread) {
+          if constexpr (W2 == 4) {
+            // lane l takes word l % 4 of lane l / 4: dims 2l, 2l + 1; the partner pair is lane l ^ 16
+            uint32_t g = 0;
 #pragma unroll
-          for (int i = 0; i < W2; ++i) {
-            const float p0 = unpack_lo<T>(pw[i]), p1 = unpack_hi<T>(pw[i]);
-            const uint32_t t1 = pack2_rn<T>(unpack_lo<T>(yw[i]) * c[2 * i],
-                                            unpack_hi<T>(yw[i]) * c[2 * i + 1]);
-            const uint32_t t2 = pack2_rn<T>((lower ? -p0 : p0) * sv[2 * i],
-                                            (lower ? -p1 : p1) * sv[2 * i + 1]);
-            ow[i] = pack2_rn<T>(unpack_lo<T>(t1) + unpack_lo<T>(t2),
-                                unpack_hi<T>(t1) + unpack_hi<T>(t2));
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t v = __shfl_sync(0xffffffffu, yw[k], lane >> 2);
+              if ((lane & 3) == k) g = v;
+            }
+            const uint32_t pg = __shfl_xor_sync(0xffffffffu, g, 16);
+            const bool lo_half = lane < 16;
+            const int jj = (2 * lane) & 31;
+            const float2 c2 = *reinterpret_cast<const float2*>(&cs[tt][jj]);
+            const float2 s2 = *reinterpret_cast<const float2*>(&sn[tt][jj]);
+            const float p0 = unpack_lo<T>(pg), p1 = unpack_hi<T>(pg);
+            const uint32_t t1 = pack2_rn<T>(unpack_lo<T>(g) * c2.x, unpack_hi<T>(g) * c2.y);
+            const uint32_t t2 = pack2_rn<T>((lo_half ? -p0 : p0) * s2.x, (lo_half ? -p1 : p1) * s2.y);
+            const uint32_t og = pack2_rn<T>(unpack_lo<T>(t1) + unpack_lo<T>(t2),
+                                            unpack_hi<T>(t1) + unpack_hi<T>(t2));
+            // lane s < 8 takes back word k from lane 4 s + k
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t v = __shfl_sync(0xffffffffu, og, (4 * lane + k) & 31);
+              ow[k] = lane < 8 ? v : yw[k];
+            }
           }
         } else {
+          uint32_t pw[W2];
 #pragma unroll
-          for (int i = 0; i < W2; ++i) ow[i] = yw[i];
+          for (int i = 0; i < W2; ++i) pw[i] = __shfl_xor_sync(0xffffffffu, yw[i], pmask);
+          if (rotates) {
+            float c[E], sv[E];
+            load_cos_sin<E>(&cs[tt][j0], &sn[tt][j0], c, sv);
+#pragma unroll
+            for (int i = 0; i < W2; ++i) {
+              const float p0 = unpack_lo<T>(pw[i]), p1 = unpack_hi<T>(pw[i]);
+              const uint32_t t1 = pack2_rn<T>(unpack_lo<T>(yw[i]) * c[2 * i],
+                                              unpack_hi<T>(yw[i]) * c[2 * i + 1]);
+              const uint32_t t2 = pack2_rn<T>((lower ? -p0 : p0) * sv[2 * i],
+                                              (lower ? -p1 : p1) * sv[2 * i + 1]);
+              ow[i] = pack2_rn<T>(unpack_lo<T>(t1) + unpack_lo<T>(t2),
+                                  unpack_hi<T>(t1) + unpack_hi<T>(t2));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < W2; ++i) ow[i] = yw[i];
+          }
         }
       } else {
         const T* xe = reinterpret_cast<const T*>(&cur);
@@ -333,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 3) prologue_vec_kernel(tf_attn_prolo
           for (int e = 0; e < E; ++e) oe[e] = from_f<T>(y[e]);
         }
       }
-      *reinterpret_cast<V*>(dst + d0) = outv;
+      *reinterpret_cast<V*>(dst) = outv;
     }
   }
 }
