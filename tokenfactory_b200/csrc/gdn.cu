@@ -1161,8 +1161,8 @@ constexpr int kThreads = 288;
 constexpr int kKQBlk = 128 * 128;             // one 64-dim block of the [K; Q] stack (128 rows)
 constexpr int oKQH = 0, oKQL = 2 * kKQBlk;    // hi / lo stacks, 32 KB each
 constexpr int oV = 4 * kKQBlk;                // T [64][128] v rows
-constexpr int oZ = oV + C * D * 2;            // bf16 [64][128] z rows
-constexpr int oOT = oZ + C * D * 2;           // T [64][128] output rows (O' transposed, rounded)
+constexpr int oZ = oV + C * D * 2;            // fp32 [64][128] silu(z) of the output gate
+constexpr int oOT = oZ + C * D * 4;           // T [64][128] output rows (O' transposed, rounded)
 constexpr int oMk = oOT + C * D * 2;          // fp32 [64 j][64 i]: Mk transposed
 constexpr int oMqH = oMk + C * C * 4;         // bf16 [64 rows][128 B] K-major (SWIZZLE_128B)
 constexpr int oMqL = oMqH + C * 128;
@@ -1457,7 +1457,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       }
       tc::fence_proxy_async_smem();  // the [K; Q] stack is read by the tensor core
       mbar_arrive(in_full);
-      // z rows once the previous chunk's output rows are written
+      // silu(z) rows once the previous chunk's output rows are written: the gate's exponentials
+      // and divisions run here, while the lanes wait for the chunk's first products, instead of
+      // on the lanes' output rows
       if (!waitb(chunk_free, ci & 1, abort)) { ok = false; }
       ok = bar_and(2, 128, ok);
       if (!ok) break;
@@ -1466,8 +1468,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         const int i = lw + 4 * m;
         float z[4];
         load4(rz + i * D + d, i < c && zb, z);
-        __nv_bfloat162 z01 = __floats2bfloat162_rn(z[0], z[1]), z23 = __floats2bfloat162_rn(z[2], z[3]);
-        sts_v2(base + oZ + (i * D + d) * 2, *reinterpret_cast<uint32_t*>(&z01), *reinterpret_cast<uint32_t*>(&z23));
+        sts_v4(base + oZ + (i * D + d) * 4, __float_as_uint(silu_fast(z[0])),
+               __float_as_uint(silu_fast(z[1])), __float_as_uint(silu_fast(z[2])),
+               __float_as_uint(silu_fast(z[3])));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(z_full);
@@ -1720,7 +1723,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       ok = bar_and(1, 128, waitb(z_full, ci & 1, abort));  // also: every O' row is in place
       if (!ok) break;
       {
-        const __nv_bfloat16* zs = reinterpret_cast<const __nv_bfloat16*>(sb + oZ);
+        const float* zs = reinterpret_cast<const float*>(sb + oZ);  // silu(z)
         T* outb = reinterpret_cast<T*>(a.out) + (t0 + c0) * a.out_stride_tok + (int64_t)vh * D + 4 * lane;
         const bool ovec = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)(a.out_stride_tok * 2)) & 7) == 0;
         // 8 rows at a time (rows warp + 4m): their squared norms reduce-scattered over the warp
@@ -1749,10 +1752,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
             float y[4];
             if (wn) {
               const float r = __shfl_sync(0xffffffffu, rr, 4 * j);
-              const uint2 zu = *reinterpret_cast<const uint2*>(zs + i * D + 4 * lane);
-              const __nv_bfloat16* ze = reinterpret_cast<const __nv_bfloat16*>(&zu);
+              const float4 zf = *reinterpret_cast<const float4*>(zs + i * D + 4 * lane);
+              const float ze[4] = {zf.x, zf.y, zf.z, zf.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) y[e] = wv[e] * (x[j][e] * r) * silu_fast(__bfloat162float(ze[e]));
+              for (int e = 0; e < 4; ++e) y[e] = wv[e] * (x[j][e] * r) * ze[e];
             } else {
 #pragma unroll
               for (int e = 0; e < 4; ++e) y[e] = x[j][e];
