@@ -1145,22 +1145,27 @@ cudaError_t launch_decode_t(const tf_gdn_args& a, cudaStream_t s) {
 //   X   = [K; Q] K^T        (M128 N64: rows 0-63 K K^T, rows 64-127 Q K^T)
 //   KS' = S' K^T,  QS' = S' Q^T     with S' = S^T [dv x dk] resident in TMEM across chunks
 //   U'  = solve of (I + Mk) against beta (V - e^g KS)^T, one dv row per thread, in registers
-//   O'  = e^g QS' + U' Mq^T,   S' = e^gC S' + U' Kd        (Kd = K o e^(gC - g))
-// Every product of fp32 values is computed as three bf16 MMAs, hi.hi + hi.lo + lo.hi with
-// x = hi + lo (hi = bf16(x), lo = bf16(x - hi)): about 2^-16 relative per product, which keeps the
-// state within 1e-5 of the fp32 recurrence over thousands of tokens.  TMEM (512 columns): S' fp32
-// 128, S' hi/lo as bf16 pairs 64 + 64, X 64, KS' 64, QS'/O' 64, U' hi/lo 32 + 32.
+//   O'  = e^g QS' + U' Mq^T,   S' = e^gC S' + U'' K      (U'' = U' o e^(gC - g))
+// K and Q enter the products as the raw bf16 conv outputs: a product of two bf16 values is exact
+// in the fp32 accumulator, so X takes one MMA per k-step, and the L2-norm factors 1/|k|, 1/|q| are
+// applied to the products (in Mk, Mq, the solve's right side, O' and U'').  Products with an fp32
+// operand (S', U', Mq) run as bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi)):
+// S'.K = S'hi.K + S'lo.K, U'.Mq^T = hi.hi + hi.lo + lo.hi, about 2^-16 relative per product, which
+// keeps the state within 1e-5 of the fp32 recurrence over thousands of tokens.  TMEM (512
+// columns): S' fp32 128, S' hi/lo as bf16 pairs 64 + 64, X (then U'' hi/lo) 64, KS' 64, QS'/O' 64,
+// U' hi/lo 32 + 32.
 // Roles: warps 0-3 own TMEM lanes (solve, mask building, rescales, output with the fused gated
-// RMSNorm), warps 4-7 load and split the chunk's q/k (normalised) into a SWIZZLE_128B [K; Q] stack,
-// v, z and the gates, warp 8 allocates TMEM and one of its threads issues the MMAs.
+// RMSNorm), warps 4-7 copy the chunk's raw q/k rows into a SWIZZLE_128B [K; Q] stack and compute
+// their norms and the per-token factors, v, silu(z) and the gates, warp 8 allocates TMEM and one
+// of its threads issues the MMAs.
 // ---------------------------------------------------------------------------------------------
 namespace tc_chunk {
 
 constexpr int C = 64, D = 128;
 constexpr int kThreads = 288;
 constexpr int kKQBlk = 128 * 128;             // one 64-dim block of the [K; Q] stack (128 rows)
-constexpr int oKQH = 0, oKQL = 2 * kKQBlk;    // hi / lo stacks, 32 KB each
-constexpr int oV = 4 * kKQBlk;                // T [64][128] v rows
+constexpr int oKQ = 0;                        // [K; Q] stack of the raw bf16 rows, 32 KB
+constexpr int oV = 2 * kKQBlk;                // T [64][128] v rows
 constexpr int oZ = oV + C * D * 2;            // fp32 [64][128] silu(z) of the output gate
 constexpr int oOT = oZ + C * D * 4;           // T [64][128] output rows (O' transposed, rounded)
 constexpr int oMk = oOT + C * D * 2;          // fp32 [64 j][64 i]: Mk transposed
@@ -1169,7 +1174,12 @@ constexpr int oMqL = oMqH + C * 128;
 constexpr int oG = oMqL + C * 128;            // gamma [64], log2 units
 constexpr int oGr = oG + C * 4;               // raw g [64]
 constexpr int oB = oGr + C * 4;               // beta [64]
-constexpr int oBar = oB + C * 4;              // in_full p1 l1 p2 tm_free z_full chunk_free fin
+constexpr int oInK = oB + C * 4;              // 1 / |k_i|
+constexpr int oInQ = oInK + C * 4;            // dk^-1/2 / |q_i|
+constexpr int oEk = oInQ + C * 4;             // e^gamma_i / |k_i|        (the solve's right side)
+constexpr int oEq = oEk + C * 4;              // e^gamma_i dk^-1/2 / |q_i| (O' = e^g QS')
+constexpr int oSk = oEq + C * 4;              // e^(gamma_C - gamma_i) / |k_i| (U'' for the state)
+constexpr int oBar = oSk + C * 4;             // in_full p1 l1 p2 tm_free z_full chunk_free fin
 constexpr int oWords = oBar + 64;             // tmem holder, abort
 constexpr int oRaw = (oWords + 16 + 1023) & ~1023;  // next chunk's raw q, k, v, z rows (T)
 constexpr int kRawPart = C * D * 2;           // one [64][128] part in a 16-bit T
@@ -1300,6 +1310,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   float* gam = reinterpret_cast<float*>(sb + oG);
   float* graw = reinterpret_cast<float*>(sb + oGr);
   float* bet = reinterpret_cast<float*>(sb + oB);
+  float* ink = reinterpret_cast<float*>(sb + oInK);
+  float* inq = reinterpret_cast<float*>(sb + oInQ);
+  float* ekf = reinterpret_cast<float*>(sb + oEk);
+  float* eqf = reinterpret_cast<float*>(sb + oEq);
+  float* skf = reinterpret_cast<float*>(sb + oSk);
   uint64_t* in_full = reinterpret_cast<uint64_t*>(sb + oBar);
   uint64_t* p1 = in_full + 1;
   uint64_t* l1 = in_full + 2;
@@ -1344,7 +1359,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   const uint32_t tmem = *tmem_holder;
 
   if (warp >= 4 && warp < 8) {
-    // ============ loaders: the chunk's q/k (normalised, split), v, z and gates ============
+    // ============ loaders: the chunk's raw q/k rows and norms, v, silu(z) and gates ============
     // The next chunk's raw rows are copied into a staging area with cp.async (every copy in
     // flight at once) while the current chunk computes; the split into the MMA layouts starts as
     // soon as the lane warps release the working buffers.
@@ -1406,42 +1421,34 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       // warp, one rsqrt per lane, then each row's factor broadcast back
 #pragma unroll 1
       for (int bt = 0; bt < 2; ++bt) {
-        float q[8][4], k[8][4], part[16];
+        float part[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int i = lw + 4 * (8 * bt + j);
           const bool live = i < c;
-          load4(rq + i * D + d, live, q[j]);
-          load4(rk + i * D + d, live, k[j]);
+          // the raw rows are the MMA operands: bf16 products are exact in the fp32 accumulators,
+          // and the 1/|q|, 1/|k| factors are applied to the products
+          const uint2 qr = live ? *reinterpret_cast<const uint2*>(rq + i * D + d) : make_uint2(0u, 0u);
+          const uint2 kr = live ? *reinterpret_cast<const uint2*>(rk + i * D + d) : make_uint2(0u, 0u);
           const uint2 v = live ? *reinterpret_cast<const uint2*>(rv + i * D + d) : make_uint2(0u, 0u);
           sts_v2(base + oV + (i * D + d) * 2, v.x, v.y);
-          float sq = 0.f, sk = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) { sq = fmaf(q[j][e], q[j][e], sq); sk = fmaf(k[j][e], k[j][e], sk); }
-          part[j] = sq;
-          part[8 + j] = sk;
-        }
-        // x / max(|x|, 1e-12) as x * rsqrt(max(|x|^2, 1e-24)): no division on this path
-        const float tot = reduce_scatter<16>(part, lane);
-        const float rn = ((lane >> 1) < 8 ? qscale : 1.f) * rsqrtf(fmaxf(tot, 1e-24f));
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = lw + 4 * (8 * bt + j);
-          const float iq = __shfl_sync(0xffffffffu, rn, 2 * j);
-          const float ik = __shfl_sync(0xffffffffu, rn, 16 + 2 * j);
-          uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
-          split2(k[j][0] * ik, k[j][1] * ik, kh0, kl0);
-          split2(k[j][2] * ik, k[j][3] * ik, kh1, kl1);
-          split2(q[j][0] * iq, q[j][1] * iq, qh0, ql0);
-          split2(q[j][2] * iq, q[j][3] * iq, qh1, ql1);
           const int rk_ = i, rq_ = 64 + i;
           const uint32_t ok_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rk_ & 7)) << 4) + e8 * 2;
           const uint32_t oq_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rq_ & 7)) << 4) + e8 * 2;
-          sts_v2(base + oKQH + rk_ * 128 + ok_, kh0, kh1);
-          sts_v2(base + oKQL + rk_ * 128 + ok_, kl0, kl1);
-          sts_v2(base + oKQH + rq_ * 128 + oq_, qh0, qh1);
-          sts_v2(base + oKQL + rq_ * 128 + oq_, ql0, ql1);
+          sts_v2(base + oKQ + rk_ * 128 + ok_, kr.x, kr.y);
+          sts_v2(base + oKQ + rq_ * 128 + oq_, qr.x, qr.y);
+          const float q0 = unpack_lo<T>(qr.x), q1 = unpack_hi<T>(qr.x), q2 = unpack_lo<T>(qr.y),
+                      q3 = unpack_hi<T>(qr.y);
+          const float k0 = unpack_lo<T>(kr.x), k1 = unpack_hi<T>(kr.x), k2 = unpack_lo<T>(kr.y),
+                      k3 = unpack_hi<T>(kr.y);
+          part[j] = fmaf(q3, q3, fmaf(q2, q2, fmaf(q1, q1, q0 * q0)));
+          part[8 + j] = fmaf(k3, k3, fmaf(k2, k2, fmaf(k1, k1, k0 * k0)));
         }
+        // x / max(|x|, 1e-12) as x * rsqrt(max(|x|^2, 1e-24)): no division on this path.  Lane
+        // 2j holds q row j's factor, lane 16 + 2j k row j's
+        const float tot = reduce_scatter<16>(part, lane);
+        const float rn = ((lane >> 1) < 8 ? qscale : 1.f) * rsqrtf(fmaxf(tot, 1e-24f));
+        if ((lane & 1) == 0) (lane < 16 ? inq : ink)[lw + 4 * (8 * bt + ((lane >> 1) & 7))] = rn;
       }
       named_barrier(2, 128);  // graw complete
       if (lw == 0) {  // gamma = inclusive cumulative sum of g over the chunk, in log2 units
@@ -1454,6 +1461,16 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         }
         gam[2 * lane] = incl - g1;
         gam[2 * lane + 1] = incl;
+        // the per-token factors of the products (every loader's norms are in place)
+        const float gC = __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = 2 * lane + h;
+          const float gi = h ? incl : incl - g1, eg = ex2(gi);
+          ekf[i] = eg * ink[i];
+          eqf[i] = eg * inq[i];
+          skf[i] = ex2(gC - gi) * ink[i];
+        }
       }
       tc::fence_proxy_async_smem();  // the [K; Q] stack is read by the tensor core
       mbar_arrive(in_full);
@@ -1485,23 +1502,22 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       constexpr uint32_t idYZ = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(128, 64, false, false);
       constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, true);
-      const uint32_t kqh = base + oKQH, kql = base + oKQL;
+      const uint32_t kq = base + oKQ;
       for (int ci = 0; ci < nchunks; ++ci) {
         if (!waitb(tm_free, ci & 1, abort) || !waitb(in_full, ci & 1, abort)) break;
         tc::fence_proxy_async_smem();
         tc::fence_after_sync();
-        // X = [K; Q] K^T, KS' = S' K^T, QS' = S' Q^T: each as hi.hi + hi.lo + lo.hi
+        // X = [K; Q] K^T of the raw rows (exact bf16 products: one MMA per k-step); KS' = S' K^T
+        // and QS' = S' Q^T as S'hi.K + S'lo.K
 #pragma unroll 1
-        for (int part = 0; part < 3; ++part) {
-          const uint32_t aS = part == 2 ? kql : kqh;   // A of X (the stack)
-          const uint32_t bS = part == 1 ? kql : kqh;   // B (K or Q rows)
-          const uint32_t aT = tmem + (part == 2 ? cSL : cSH);
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t aT = tmem + (part ? cSL : cSH);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * kKQBlk + (kk & 3) * 32;
             const bool acc = part > 0 || kk > 0;
-            const uint64_t bKQ = tc::sw128_desc(bS + off, 16, 1024);  // K rows, then Q rows
-            tc::mma_bf16(tmem + cX, tc::sw128_desc(aS + off, 16, 1024), bKQ, idX, acc);
+            const uint64_t bKQ = tc::sw128_desc(kq + off, 16, 1024);  // K rows, then Q rows
+            if (part == 0) tc::mma_bf16(tmem + cX, bKQ, bKQ, idX, kk > 0);
             mma_ts(tmem + cY, aT + kk * 8, bKQ, idYZ, acc);  // [KS' | QS'] over cY, cZ
           }
         }
@@ -1509,16 +1525,18 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         if (!waitb(l1, ci & 1, abort)) break;
         tc::fence_after_sync();
         tc::fence_proxy_async_smem();
-        // O' += U' Mq^T (N = 64 tokens) and S' += U' Kd (N = 128 dk, Kd MN-major over the K rows)
+        // O' += U' Mq^T (N = 64 tokens, hi.hi + hi.lo + lo.hi) and S' += U'' K (N = 128 dk, the
+        // raw K rows MN-major; U'' = U' e^(gamma_C - gamma) / |k| as hi + lo over cX)
 #pragma unroll 1
         for (int part = 0; part < 3; ++part) {
           const uint32_t aT = tmem + (part == 2 ? cUL : cUH);
           const uint32_t mq = base + (part == 1 ? oMqL : oMqH);
-          const uint32_t kd = part == 1 ? kql : kqh;
+          const uint32_t aK = tmem + cX + (part == 2 ? 32 : 0);
 #pragma unroll
           for (int kk = 0; kk < C / 16; ++kk) {
             mma_ts(tmem + cZ, aT + kk * 8, tc::sw128_desc(mq + kk * 32, 16, 1024), idO, true);
-            mma_ts(tmem + cS, aT + kk * 8, tc::sw128_desc(kd + kk * 2048, kKQBlk, 1024), idS, true);
+            if (part != 1)
+              mma_ts(tmem + cS, aK + kk * 8, tc::sw128_desc(kq + kk * 2048, kKQBlk, 1024), idS, true);
           }
         }
         tc::commit(p2);
@@ -1575,29 +1593,33 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         const int i = l & 63;
         const float gi = gam[i];
         const float4* g4 = reinterpret_cast<const float4*>(gam);
-        if (l < 64) {
-          const float bi = bet[i];
+        const float4* n4 = reinterpret_cast<const float4*>(ink);
+        if (l < 64) {  // Mk_ij = beta_i e^(g_i - g_j) k_i.k_j / (|k_i| |k_j|)
+          const float bi = bet[i] * ink[i];
 #pragma unroll
           for (int j4 = 0; j4 < 16; ++j4) {
-            const float4 g = g4[j4];
-            const float gj[4] = {g.x, g.y, g.z, g.w};
+            const float4 g = g4[j4], n = n4[j4];
+            const float gj[4] = {g.x, g.y, g.z, g.w}, nj[4] = {n.x, n.y, n.z, n.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int j = 4 * j4 + e;
-              MkT[j * C + i] = j < i ? bi * ex2(gi - gj[e]) * x[j] : 0.f;
+              MkT[j * C + i] = j < i ? bi * ex2(gi - gj[e]) * (x[j] * nj[e]) : 0.f;
             }
           }
-        } else {
+        } else {  // Mq_ij = e^(g_i - g_j) q_i.k_j dk^-1/2 / (|q_i| |k_j|)
+          const float qi = inq[i];
 #pragma unroll
           for (int c8 = 0; c8 < 8; ++c8) {
             const float4 ga = g4[2 * c8], gb = g4[2 * c8 + 1];
+            const float4 na = n4[2 * c8], nb = n4[2 * c8 + 1];
             const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+            const float nj[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
             uint32_t h[4], lo_[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int j0 = 8 * c8 + 2 * e, j1 = j0 + 1;
-              const float m0 = j0 <= i ? ex2(gi - gj[2 * e]) * x[j0] : 0.f;
-              const float m1 = j1 <= i ? ex2(gi - gj[2 * e + 1]) * x[j1] : 0.f;
+              const float m0 = j0 <= i ? qi * ex2(gi - gj[2 * e]) * (x[j0] * nj[2 * e]) : 0.f;
+              const float m1 = j1 <= i ? qi * ex2(gi - gj[2 * e + 1]) * (x[j1] * nj[2 * e + 1]) : 0.f;
               split2(m0, m1, h[e], lo_[e]);
             }
             const uint32_t off = i * 128 + ((uint32_t)(c8 ^ (i & 7)) << 4);
@@ -1620,7 +1642,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           tc::wait_ld();
           const T* vr = reinterpret_cast<const T*>(sb + oV);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * D + l]) - ex2(gam[i]) * u[i]);
+          for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * D + l]) - ekf[i] * u[i]);
 #pragma unroll
           for (int p = 0; p < 32; ++p) u2[p] = pack2(u[2 * p], u[2 * p + 1]);
         }
@@ -1644,8 +1666,20 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           st16u(lb + cUH + 16 * h, hi);
           st16u(lb + cUL + 16 * h, lo);
         }
+        // U'' = U' e^(gamma_C - gamma) / |k| (the state update's A; X is consumed)
+        const float2* s2 = reinterpret_cast<const float2*>(skf);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float2 sf = s2[16 * h + k];
+            split2(lo_of(u2[16 * h + k]) * sf.x, hi_of(u2[16 * h + k]) * sf.y, hi[k], lo[k]);
+          }
+          st16u(lb + cX + 16 * h, hi);
+          st16u(lb + cX + 32 + 16 * h, lo);
+        }
       }
-      // ---- O' = e^g QS' (the MMA adds U' Mq^T), S' *= e^gC, Kd = K o e^(gC - g) in place
+      // ---- O' = e^g QS' (the MMA adds U' Mq^T), S' *= e^gC
       {
         float zq[32];
 #pragma unroll
@@ -1653,7 +1687,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           tc::ld32(lb + cZ + 32 * h, zq);
           tc::wait_ld();
 #pragma unroll
-          for (int k = 0; k < 32; ++k) zq[k] *= ex2(gam[32 * h + k]);
+          for (int k = 0; k < 32; ++k) zq[k] *= eqf[32 * h + k];
           tc::st32(lb + cZ + 32 * h, zq);
         }
         const float gC = gam[C - 1], eC = ex2(gC);
@@ -1665,27 +1699,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           for (int k = 0; k < 32; ++k) zq[k] *= eC;
           tc::st32(lb + cS + 32 * cc, zq);
         }
-        const int i = l & 63, hb = l >> 6;
-        const float w = ex2(gC - gam[i]);
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          const uint32_t off = hb * kKQBlk + i * 128 + ((uint32_t)(c8 ^ (i & 7)) << 4);
-          const uint4 h4 = lds_v4(base + oKQH + off), l4 = lds_v4(base + oKQL + off);
-          const uint32_t hw[4] = {h4.x, h4.y, h4.z, h4.w}, lw4[4] = {l4.x, l4.y, l4.z, l4.w};
-          uint32_t nh[4], nl[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 hh = *reinterpret_cast<const __nv_bfloat162*>(&hw[e]);
-            const __nv_bfloat162 ll = *reinterpret_cast<const __nv_bfloat162*>(&lw4[e]);
-            split2((__low2float(hh) + __low2float(ll)) * w, (__high2float(hh) + __high2float(ll)) * w, nh[e], nl[e]);
-          }
-          sts_v4(base + oKQH + off, nh[0], nh[1], nh[2], nh[3]);
-          sts_v4(base + oKQL + off, nl[0], nl[1], nl[2], nl[3]);
-        }
       }
       tc::wait_st();
       tc::fence_before_sync();
-      tc::fence_proxy_async_smem();  // Mq and Kd are read by the tensor core
+      tc::fence_proxy_async_smem();  // Mq is read by the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(l1);
       ok = bar_and(1, 128, waitb(p2, ci & 1, abort));
