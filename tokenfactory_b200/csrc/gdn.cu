@@ -1361,34 +1361,29 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   if (warp >= 4 && warp < 8) {
     // ============ loaders: the chunk's raw q/k rows and norms, v, silu(z) and gates ============
     // The next chunk's raw rows are copied into a staging area with cp.async (every copy in
-    // flight at once) while the current chunk computes; the split into the MMA layouts starts as
+    // flight at once) while the current chunk computes; the copy into the MMA layouts starts as
     // soon as the lane warps release the working buffers.
     const int lt = tid - 128, lw = warp - 4;
     const float qscale = rsqrtf((float)D);
     const T* zb = a.z ? reinterpret_cast<const T*>(a.z) + (int64_t)vh * D : nullptr;
     const bool zvec = zb && ((reinterpret_cast<uintptr_t>(zb) | (uintptr_t)(a.z_stride_tok * 2)) & 15) == 0;
     float g_next = 0.f, b_next = 0.f;
-    auto prefetch = [&](int ci) {
+    // The raw rows of a chunk arrive as two cp.async groups: q, k, v (and the gates) are requested
+    // as soon as the split has consumed the previous chunk's, z once its silu rows are written;
+    // each wait below leaves only the newest group in flight.
+    auto prefetch_qkv = [&](int ci) {
       const int64_t c0 = (int64_t)ci * C;
       const int c = (int)(E - c0 < C ? E - c0 : C);
-      // 64 rows x 4 parts x 16 pieces of 16 bytes, 32 per loader thread
+      // 64 rows x 3 parts x 16 pieces of 16 bytes, 24 per loader thread
 #pragma unroll 4
-      for (int n = 0; n < 32; ++n) {
+      for (int n = 0; n < 24; ++n) {
         const int e = lt + 128 * n;
-        const int i = e >> 6, part = (e >> 4) & 3, pc = e & 15;
-        const uint32_t dst = base + oRaw + part * kRawPart + (i * D + pc * 8) * 2;
+        const int i = e / 48, part = (e % 48) >> 4, pc = e & 15;
         if (i < c) {
           const int64_t t = t0 + c0 + i;
-          if (part < 3) {
-            const int col = part == 0 ? kh * D : (part == 1 ? key_dim + kh * D : 2 * key_dim + vh * D);
-            cp_async16(dst, conv_out + t * conv_dim + col + pc * 8);
-          } else if (zvec) {
-            cp_async16(dst, zb + t * a.z_stride_tok + pc * 8);
-          } else if (zb) {
-            T* d = reinterpret_cast<T*>(sb + oRaw + part * kRawPart + (i * D + pc * 8) * 2);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) d[q] = zb[t * a.z_stride_tok + pc * 8 + q];
-          }
+          const int col = part == 0 ? kh * D : (part == 1 ? key_dim + kh * D : 2 * key_dim + vh * D);
+          cp_async16(base + oRaw + part * kRawPart + (i * D + pc * 8) * 2,
+                     conv_out + t * conv_dim + col + pc * 8);
         }
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
@@ -1398,12 +1393,33 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         if (lt < c) gate_values<T>(a, t0 + c0 + lt, vh, &g_next, &b_next);
       }
     };
-    prefetch(0);
+    auto prefetch_z = [&](int ci) {
+      const int64_t c0 = (int64_t)ci * C;
+      const int c = (int)(E - c0 < C ? E - c0 : C);
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {  // 64 rows x 16 pieces, 8 per loader thread
+        const int e = lt + 128 * n;
+        const int i = e >> 4, pc = e & 15;
+        if (i < c) {
+          const int64_t t = t0 + c0 + i;
+          if (zvec) {
+            cp_async16(base + oRaw + 3 * kRawPart + (i * D + pc * 8) * 2, zb + t * a.z_stride_tok + pc * 8);
+          } else if (zb) {
+            T* dz = reinterpret_cast<T*>(sb + oRaw + 3 * kRawPart + (i * D + pc * 8) * 2);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dz[q] = zb[t * a.z_stride_tok + pc * 8 + q];
+          }
+        }
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    prefetch_qkv(0);
+    prefetch_z(0);
     bool ok = true;
     for (int ci = 0; ci < nchunks && ok; ++ci) {
       const int64_t c0 = (int64_t)ci * C;
       const int c = (int)(E - c0 < C ? E - c0 : C);
-      asm volatile("cp.async.wait_all;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's q, k, v (z may fly on)
       // the stack, v rows and gates of the previous chunk are consumed once its last MMAs ran
       ok = bar_and(2, 128, ci == 0 || waitb(p2, (ci - 1) & 1, abort));  // and the staging landed
       if (!ok) break;
@@ -1474,10 +1490,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       }
       tc::fence_proxy_async_smem();  // the [K; Q] stack is read by the tensor core
       mbar_arrive(in_full);
+      if (ci + 1 < nchunks) prefetch_qkv(ci + 1);  // the raw q, k, v rows are consumed
       // silu(z) rows once the previous chunk's output rows are written: the gate's exponentials
       // and divisions run here, while the lanes wait for the chunk's first products, instead of
       // on the lanes' output rows
       if (!waitb(chunk_free, ci & 1, abort)) { ok = false; }
+      if (ci + 1 < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's z
+      else asm volatile("cp.async.wait_group 0;" ::: "memory");
       ok = bar_and(2, 128, ok);
       if (!ok) break;
 #pragma unroll 4
@@ -1491,8 +1510,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(z_full);
-      named_barrier(2, 128);  // the staging is consumed before it is refilled
-      if (ci + 1 < nchunks) prefetch(ci + 1);
+      named_barrier(2, 128);  // the z staging is consumed before it is refilled
+      if (ci + 1 < nchunks) prefetch_z(ci + 1);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == 8) {
