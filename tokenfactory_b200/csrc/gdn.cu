@@ -1179,7 +1179,7 @@ constexpr int oInQ = oInK + C * 4;            // dk^-1/2 / |q_i|
 constexpr int oEk = oInQ + C * 4;             // e^gamma_i / |k_i|        (the solve's right side)
 constexpr int oEq = oEk + C * 4;              // e^gamma_i dk^-1/2 / |q_i| (O' = e^g QS')
 constexpr int oSk = oEq + C * 4;              // e^(gamma_C - gamma_i) / |k_i| (U'' for the state)
-constexpr int oBar = oSk + C * 4;             // in_full p1 l1 p2 tm_free z_full chunk_free fin
+constexpr int oBar = oSk + C * 4;             // in_full p1 l1 p2 tm_free - chunk_free fin
 constexpr int oWords = oBar + 64;             // tmem holder, abort
 constexpr int oRaw = (oWords + 16 + 1023) & ~1023;  // next chunk's raw q, k, v, z rows (T)
 constexpr int kRawPart = C * D * 2;           // one [64][128] part in a 16-bit T
@@ -1319,9 +1319,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   uint64_t* p1 = in_full + 1;
   uint64_t* l1 = in_full + 2;
   uint64_t* p2 = in_full + 3;
-  uint64_t* tm_free = in_full + 4;     // S' hi / lo written and O' read out: phase 1 may run
-  uint64_t* z_full = in_full + 5;      // the chunk's z rows are in place
-  uint64_t* chunk_free = in_full + 6;  // the output rows are written: z may be replaced
+  uint64_t* tm_free = in_full + 4;     // S' hi / lo and the O' rows written: phase 1 may run
+  uint64_t* chunk_free = in_full + 6;  // the output rows are written: O' may replace them
   uint64_t* fin = in_full + 7;         // every MMA of the CTA has completed
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
@@ -1346,7 +1345,6 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     mbar_init(l1, 4);
     mbar_init(p2, 1);
     mbar_init(tm_free, 4);
-    mbar_init(z_full, 4);
     mbar_init(chunk_free, 4);
     mbar_init(fin, 1);
     *abort = 0;
@@ -1367,7 +1365,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     const float qscale = rsqrtf((float)D);
     const T* zb = a.z ? reinterpret_cast<const T*>(a.z) + (int64_t)vh * D : nullptr;
     const bool zvec = zb && ((reinterpret_cast<uintptr_t>(zb) | (uintptr_t)(a.z_stride_tok * 2)) & 15) == 0;
-    float g_next = 0.f, b_next = 0.f;
+    // gates: the next chunk's raw a, b are loaded with its rows and turned into g, beta when the
+    // chunk starts (the loads' latency overlaps this chunk), with the head's constants hoisted
+    T a_next = from_f<T>(0.f), b_next = from_f<T>(0.f);
+    bool gate_next = false;
+    const float neg_ea = -expf(to_f(reinterpret_cast<const T*>(a.A_log)[vh]));
+    const float dtb = to_f(reinterpret_cast<const T*>(a.dt_bias)[vh]);
     // The raw rows of a chunk arrive as two cp.async groups: q, k, v (and the gates) are requested
     // as soon as the split has consumed the previous chunk's, z once its silu rows are written;
     // each wait below leaves only the newest group in flight.
@@ -1388,9 +1391,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
       if (lt < C) {
-        g_next = 0.f;
-        b_next = 0.f;
-        if (lt < c) gate_values<T>(a, t0 + c0 + lt, vh, &g_next, &b_next);
+        gate_next = lt < c;
+        if (gate_next) {
+          const int64_t t = t0 + c0 + lt;
+          a_next = reinterpret_cast<const T*>(a.a)[t * a.a_stride_tok + vh];
+          b_next = reinterpret_cast<const T*>(a.b)[t * a.b_stride_tok + vh];
+        }
       }
     };
     auto prefetch_z = [&](int ci) {
@@ -1413,6 +1419,75 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    const T* wn = a.z ? reinterpret_cast<const T*>(a.norm_weight) + (a.norm_weight_len == D ? 0 : (int64_t)vh * D)
+                      : nullptr;
+    float wv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (wn) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wv[e] = to_f(wn[4 * lane + e]);
+    }
+    // output rows of chunk cj: o rounded to T (the lanes' O' rows), then the fused gated RMSNorm
+    // with this warp's rows lw + 4m; the lanes may replace the O' rows once chunk_free completes
+    auto out_rows = [&](int cj) -> bool {
+      const int64_t c0 = (int64_t)cj * C;
+      const int c = (int)(E - c0 < C ? E - c0 : C);
+      if (!bar_and(2, 128, waitb(tm_free, (cj + 1) & 1, abort))) return false;
+      const T* ot = reinterpret_cast<const T*>(sb + oOT);
+      {
+        const float* zs = reinterpret_cast<const float*>(sb + oZ);  // silu(z)
+        T* outb = reinterpret_cast<T*>(a.out) + (t0 + c0) * a.out_stride_tok + (int64_t)vh * D + 4 * lane;
+        const bool ovec = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)(a.out_stride_tok * 2)) & 7) == 0;
+        // 8 rows at a time (rows lw + 4m): their squared norms reduce-scattered over the warp
+#pragma unroll 1
+        for (int bt = 0; bt < 2; ++bt) {
+          if (lw + 32 * bt >= c) break;
+          float x[8][4], part[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int i = lw + 4 * (8 * bt + j);
+            load4(ot + i * D + 4 * lane, i < c, x[j]);
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ss = fmaf(x[j][e], x[j][e], ss);
+            part[j] = ss;
+          }
+          float rr = 1.f;
+          if (wn) {
+            const float tot = reduce_scatter<8>(part, lane);
+            rr = rsqrtf(tot / (float)D + a.norm_eps);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int i = lw + 4 * (8 * bt + j);
+            if (i >= c) break;
+            float y[4];
+            if (wn) {
+              const float r = __shfl_sync(0xffffffffu, rr, 4 * j);
+              const float4 zf = *reinterpret_cast<const float4*>(zs + i * D + 4 * lane);
+              const float ze[4] = {zf.x, zf.y, zf.z, zf.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) y[e] = wv[e] * (x[j][e] * r) * ze[e];
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) y[e] = x[j][e];
+            }
+            T* out = outb + (int64_t)i * a.out_stride_tok;
+            if (ovec) {
+              T pk[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) pk[e] = from_f<T>(y[e]);
+              *reinterpret_cast<uint2*>(out) = *reinterpret_cast<const uint2*>(pk);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) out[e] = from_f<T>(y[e]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(chunk_free);
+      return true;
+    };
     prefetch_qkv(0);
     prefetch_z(0);
     bool ok = true;
@@ -1424,8 +1499,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       ok = bar_and(2, 128, ci == 0 || waitb(p2, (ci - 1) & 1, abort));  // and the staging landed
       if (!ok) break;
       if (lt < C) {
-        graw[lt] = g_next;
-        bet[lt] = b_next;
+        // g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)  (linear_attention.py:178-181)
+        graw[lt] = gate_next ? neg_ea * softplus_f(to_f(a_next) + dtb) : 0.f;
+        bet[lt] = gate_next ? 1.0f / (1.0f + expf(-to_f(b_next))) : 0.f;
       }
       const T* rq = reinterpret_cast<const T*>(sb + oRaw);
       const T* rk = reinterpret_cast<const T*>(sb + oRaw + kRawPart);
@@ -1491,10 +1567,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       tc::fence_proxy_async_smem();  // the [K; Q] stack is read by the tensor core
       mbar_arrive(in_full);
       if (ci + 1 < nchunks) prefetch_qkv(ci + 1);  // the raw q, k, v rows are consumed
-      // silu(z) rows once the previous chunk's output rows are written: the gate's exponentials
-      // and divisions run here, while the lanes wait for the chunk's first products, instead of
-      // on the lanes' output rows
-      if (!waitb(chunk_free, ci & 1, abort)) { ok = false; }
+      // the previous chunk's output rows (its silu(z) rows are still in oZ), then this chunk's
+      // silu(z): the gate's exponentials and divisions and the output rows run here, beside the
+      // lanes' work on this chunk, instead of on the lanes' critical path
+      if (ci > 0 && !out_rows(ci - 1)) { ok = false; break; }
       if (ci + 1 < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's z
       else asm volatile("cp.async.wait_group 0;" ::: "memory");
       ok = bar_and(2, 128, ok);
@@ -1508,11 +1584,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
                __float_as_uint(silu_fast(z[1])), __float_as_uint(silu_fast(z[2])),
                __float_as_uint(silu_fast(z[3])));
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(z_full);
       named_barrier(2, 128);  // the z staging is consumed before it is refilled
       if (ci + 1 < nchunks) prefetch_z(ci + 1);
     }
+    if (ok) out_rows(nchunks - 1);
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == 8) {
     // ============ MMA issue (one thread) ============
@@ -1590,16 +1665,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         mbar_arrive(chunk_free);
       }
     }
-    const T* wn = a.z ? reinterpret_cast<const T*>(a.norm_weight) + (a.norm_weight_len == D ? 0 : (int64_t)vh * D)
-                      : nullptr;
-    float wv[4] = {0.f, 0.f, 0.f, 0.f};
-    if (wn) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) wv[e] = to_f(wn[4 * lane + e]);
-    }
     for (int ci = 0; ci < nchunks; ++ci) {
-      const int64_t c0 = (int64_t)ci * C;
-      const int c = (int)(E - c0 < C ? E - c0 : C);
       ok = bar_and(1, 128, ok && waitb(in_full, ci & 1, abort) && waitb(p1, ci & 1, abort));
       if (!ok) break;
       tc::fence_after_sync();
@@ -1724,11 +1790,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       tc::fence_proxy_async_smem();  // Mq is read by the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(l1);
-      ok = bar_and(1, 128, waitb(p2, ci & 1, abort));
+      // the previous chunk's output rows are written by the loaders before O' replaces them
+      ok = bar_and(1, 128, waitb(p2, ci & 1, abort) && waitb(chunk_free, ci & 1, abort));
       if (!ok) break;
       tc::fence_after_sync();
       // ---- O' rounded to T into the transposed output rows, S' hi / lo for the next chunk; then
-      //      the next chunk's products may start while the output rows are written
+      //      the next chunk's products start while the loaders write the output rows
       T* ot = reinterpret_cast<T*>(sb + oOT);
       {
         float o[32];
@@ -1755,62 +1822,6 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(tm_free);
-      // ---- output rows: gated RMSNorm per token, two rows per pass
-      ok = bar_and(1, 128, waitb(z_full, ci & 1, abort));  // also: every O' row is in place
-      if (!ok) break;
-      {
-        const float* zs = reinterpret_cast<const float*>(sb + oZ);  // silu(z)
-        T* outb = reinterpret_cast<T*>(a.out) + (t0 + c0) * a.out_stride_tok + (int64_t)vh * D + 4 * lane;
-        const bool ovec = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)(a.out_stride_tok * 2)) & 7) == 0;
-        // 8 rows at a time (rows warp + 4m): their squared norms reduce-scattered over the warp
-#pragma unroll 1
-        for (int bt = 0; bt < 2; ++bt) {
-          if (warp + 32 * bt >= c) break;
-          float x[8][4], part[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int i = warp + 4 * (8 * bt + j);
-            load4(ot + i * D + 4 * lane, i < c, x[j]);
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) ss = fmaf(x[j][e], x[j][e], ss);
-            part[j] = ss;
-          }
-          float rr = 1.f;
-          if (wn) {
-            const float tot = reduce_scatter<8>(part, lane);
-            rr = rsqrtf(tot / (float)D + a.norm_eps);
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int i = warp + 4 * (8 * bt + j);
-            if (i >= c) break;
-            float y[4];
-            if (wn) {
-              const float r = __shfl_sync(0xffffffffu, rr, 4 * j);
-              const float4 zf = *reinterpret_cast<const float4*>(zs + i * D + 4 * lane);
-              const float ze[4] = {zf.x, zf.y, zf.z, zf.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) y[e] = wv[e] * (x[j][e] * r) * ze[e];
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) y[e] = x[j][e];
-            }
-            T* out = outb + (int64_t)i * a.out_stride_tok;
-            if (ovec) {
-              T pk[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) pk[e] = from_f<T>(y[e]);
-              *reinterpret_cast<uint2*>(out) = *reinterpret_cast<const uint2*>(pk);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) out[e] = from_f<T>(y[e]);
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(chunk_free);
     }
     if (ok) {  // the state back to the pool
       ok = waitb(fin, 0, abort);
