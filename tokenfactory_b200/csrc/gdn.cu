@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "launch.h"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace tf {
 namespace gdn {
@@ -1163,30 +1164,32 @@ namespace tc_chunk {
 
 constexpr int C = 64, D = 128;
 constexpr int kThreads = 288;
-constexpr int kKQBlk = 128 * 128;             // one 64-dim block of the [K; Q] stack (128 rows)
-constexpr int oKQ = 0;                        // [K; Q] stack of the raw bf16 rows, 32 KB
-constexpr int oV = 2 * kKQBlk;                // T [64][128] v rows
-constexpr int oZ = oV + C * D * 2;            // fp32 [64][128] silu(z) of the output gate
+constexpr int kKQBlk = 128 * 128;             // one 64-dim block of a [K; Q] stack (128 rows)
+constexpr int kStack = 2 * kKQBlk;            // a [K; Q] stack of raw bf16 rows, 32 KB
+constexpr int kVBuf = C * D * 2;              // T [64][128] v rows
+// Chunks alternate between two sets of the buffers the loaders fill (stack, v rows, per-token
+// arrays), so that chunk c+1's rows are in place while chunk c still computes.
+constexpr int oKQ = 0;                        // stacks [2]
+constexpr int oV = 2 * kStack;                // v rows [2]
+constexpr int oZ = oV + 2 * kVBuf;            // fp32 [64][128] silu(z) of the output gate
 constexpr int oOT = oZ + C * D * 4;           // T [64][128] output rows (O' transposed, rounded)
 constexpr int oMk = oOT + C * D * 2;          // fp32 [64 j][64 i]: Mk transposed
 constexpr int oMqH = oMk + C * C * 4;         // bf16 [64 rows][128 B] K-major (SWIZZLE_128B)
 constexpr int oMqL = oMqH + C * 128;
-constexpr int oG = oMqL + C * 128;            // gamma [64], log2 units
-constexpr int oGr = oG + C * 4;               // raw g [64]
-constexpr int oB = oGr + C * 4;               // beta [64]
-constexpr int oInK = oB + C * 4;              // 1 / |k_i|
-constexpr int oInQ = oInK + C * 4;            // dk^-1/2 / |q_i|
-constexpr int oEk = oInQ + C * 4;             // e^gamma_i / |k_i|        (the solve's right side)
-constexpr int oEq = oEk + C * 4;              // e^gamma_i dk^-1/2 / |q_i| (O' = e^g QS')
-constexpr int oSk = oEq + C * 4;              // e^(gamma_C - gamma_i) / |k_i| (U'' for the state)
-constexpr int oBar = oSk + C * 4;             // in_full p1 l1 p2 tm_free - chunk_free fin
-constexpr int oWords = oBar + 64;             // tmem holder, abort
-constexpr int oRaw = (oWords + 16 + 1023) & ~1023;  // next chunk's raw q, k, v, z rows (T)
-constexpr int kRawPart = C * D * 2;           // one [64][128] part in a 16-bit T
-constexpr int kSmem = oRaw + 4 * kRawPart + 1024;
+// per-token arrays [2][7][64]: gamma (log2 units), beta, 1/|k|, dk^-1/2/|q|, e^gamma/|k| (the
+// solve's right side), e^gamma dk^-1/2/|q| (O' = e^g QS'), e^(gamma_C - gamma)/|k| (U'')
+constexpr int oArr = oMqL + C * 128;
+constexpr int kArr = 7 * C * 4;
+enum { aGam = 0, aBet, aInK, aInQ, aEk, aEq, aSk };
+constexpr int oGr = oArr + 2 * kArr;          // raw g [64] (loaders)
+constexpr int oBar = oGr + C * 4;             // in_full[2] p1 l1 p2[2] tm_free chunk_free fin rows_full[2]
+constexpr int oWords = oBar + 96;             // tmem holder, abort
+constexpr int oRawZ = (oWords + 16 + 1023) & ~1023;  // next chunk's raw z rows (T)
+constexpr int kSmem = oRawZ + C * D * 2 + 1024;
 static_assert(kSmem <= 232448, "shared memory per CTA");
 constexpr int cS = 0, cSH = 128, cSL = 192, cX = 256, cY = 320, cZ = 384, cUH = 448, cUL = 480;
-static_assert(oMqH % 1024 == 0 && oMqL % 1024 == 0, "SWIZZLE_128B tiles are 1024-byte aligned");
+static_assert(oMqH % 1024 == 0 && oMqL % 1024 == 0 && kStack % 1024 == 0,
+              "SWIZZLE_128B tiles are 1024-byte aligned");
 
 // 2^x (ex2.approx.ftz: relative error about 2^-22)
 __device__ __forceinline__ float ex2(float x) {
@@ -1301,27 +1304,28 @@ __device__ __forceinline__ void load4(const T* p, bool live, float (&f)[4]) {
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, const int64_t* start,
-                                                               const T* conv_out, const int32_t* order) {
+                                                               const T* conv_out, const int32_t* order,
+                                                               const __grid_constant__ CUtensorMap map_qk,
+                                                               const __grid_constant__ CUtensorMap map_v) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023) & ~1023u;
   unsigned char* sb = smem_raw + (base - raw_base);
   float* MkT = reinterpret_cast<float*>(sb + oMk);
-  float* gam = reinterpret_cast<float*>(sb + oG);
   float* graw = reinterpret_cast<float*>(sb + oGr);
-  float* bet = reinterpret_cast<float*>(sb + oB);
-  float* ink = reinterpret_cast<float*>(sb + oInK);
-  float* inq = reinterpret_cast<float*>(sb + oInQ);
-  float* ekf = reinterpret_cast<float*>(sb + oEk);
-  float* eqf = reinterpret_cast<float*>(sb + oEq);
-  float* skf = reinterpret_cast<float*>(sb + oSk);
-  uint64_t* in_full = reinterpret_cast<uint64_t*>(sb + oBar);
-  uint64_t* p1 = in_full + 1;
-  uint64_t* l1 = in_full + 2;
-  uint64_t* p2 = in_full + 3;
-  uint64_t* tm_free = in_full + 4;     // S' hi / lo and the O' rows written: phase 1 may run
-  uint64_t* chunk_free = in_full + 6;  // the output rows are written: O' may replace them
-  uint64_t* fin = in_full + 7;         // every MMA of the CTA has completed
+  auto arr = [&](int buf, int k) { return reinterpret_cast<float*>(sb + oArr + buf * kArr + k * C * 4); };
+  // A barrier used by chunks of one parity (in_full, p2) completes its phase for chunk c as its
+  // (c >> 1)-th: no waiter can find it two phases ahead, since the next use needs this one's
+  // consumers to have passed.
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + oBar);
+  uint64_t* in_full = bars;            // [2] a chunk's stack, v rows and arrays are in place
+  uint64_t* p1 = bars + 2;             // phase-1 products of the chunk are in TMEM
+  uint64_t* l1 = bars + 3;             // Mq, U', U'' and the rescales are written
+  uint64_t* p2 = bars + 4;             // [2] a chunk's phase-2 products have completed
+  uint64_t* tm_free = bars + 6;        // S' hi / lo and the O' rows written: phase 1 may run
+  uint64_t* chunk_free = bars + 7;     // the output rows are written: O' may replace them
+  uint64_t* fin = bars + 8;            // every MMA of the CTA has completed
+  uint64_t* rows_full = bars + 9;      // [2] a chunk's q, k, v rows have landed (TMA)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
 
@@ -1330,7 +1334,6 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   const int kh = vh / (a.num_v_heads / a.num_k_heads);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int key_dim = a.num_k_heads * D;
-  const int conv_dim = 2 * key_dim + a.num_v_heads * D;
   const int64_t slot = a.req_pool_indices[b];
   if (slot < 0 || slot >= a.num_slots) return;  // recorded by the conv kernel
   const int64_t t0 = start[b];
@@ -1341,9 +1344,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
 
   if (tid == 0) {
     mbar_init(in_full, 128);
+    mbar_init(in_full + 1, 128);
     mbar_init(p1, 1);
     mbar_init(l1, 4);
     mbar_init(p2, 1);
+    mbar_init(p2 + 1, 1);
+    mbar_init(rows_full, 1);
+    mbar_init(rows_full + 1, 1);
     mbar_init(tm_free, 4);
     mbar_init(chunk_free, 4);
     mbar_init(fin, 1);
@@ -1371,25 +1378,27 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     bool gate_next = false;
     const float neg_ea = -expf(to_f(reinterpret_cast<const T*>(a.A_log)[vh]));
     const float dtb = to_f(reinterpret_cast<const T*>(a.dt_bias)[vh]);
-    // The raw rows of a chunk arrive as two cp.async groups: q, k, v (and the gates) are requested
-    // as soon as the split has consumed the previous chunk's, z once its silu rows are written;
-    // each wait below leaves only the newest group in flight.
-    auto prefetch_qkv = [&](int ci) {
+    // A chunk's q, k, v rows arrive by TMA once chunk c-1's phase 2 has released the buffers of
+    // its parity: six 64-row x 64-column boxes, q and k SWIZZLE_128B straight into the [K; Q]
+    // stack (k rows 0-63, q rows 64-127 of each 64-dim block), v as two [64][64] halves; one
+    // thread issues them.  Rows past the batch are zero-filled by the TMA unit, rows of the next
+    // request are zeroed once they land.  The gates' raw a, b are loaded alongside; z is staged
+    // raw by cp.async once the previous silu rows are written.
+    auto prefetch_rows = [&](int ci) {
       const int64_t c0 = (int64_t)ci * C;
       const int c = (int)(E - c0 < C ? E - c0 : C);
-      // 64 rows x 3 parts x 16 pieces of 16 bytes, 24 per loader thread
-#pragma unroll 4
-      for (int n = 0; n < 24; ++n) {
-        const int e = lt + 128 * n;
-        const int i = e / 48, part = (e % 48) >> 4, pc = e & 15;
-        if (i < c) {
-          const int64_t t = t0 + c0 + i;
-          const int col = part == 0 ? kh * D : (part == 1 ? key_dim + kh * D : 2 * key_dim + vh * D);
-          cp_async16(base + oRaw + part * kRawPart + (i * D + pc * 8) * 2,
-                     conv_out + t * conv_dim + col + pc * 8);
+      if (lt == 0) {
+        const uint32_t stk = base + oKQ + (ci & 1) * kStack, vbuf = base + oV + (ci & 1) * kVBuf;
+        uint64_t* bar = rows_full + (ci & 1);
+        const int row = (int)(t0 + c0);
+        mbar_arrive_expect_tx(bar, 6 * C * 64 * 2);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tma::load_2d(stk + h * kKQBlk, &map_qk, key_dim + kh * D + 64 * h, row, bar);
+          tma::load_2d(stk + h * kKQBlk + 64 * 128, &map_qk, kh * D + 64 * h, row, bar);
+          tma::load_2d(vbuf + h * C * 128, &map_v, 2 * key_dim + vh * D + 64 * h, row, bar);
         }
       }
-      asm volatile("cp.async.commit_group;" ::: "memory");
       if (lt < C) {
         gate_next = lt < c;
         if (gate_next) {
@@ -1409,9 +1418,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         if (i < c) {
           const int64_t t = t0 + c0 + i;
           if (zvec) {
-            cp_async16(base + oRaw + 3 * kRawPart + (i * D + pc * 8) * 2, zb + t * a.z_stride_tok + pc * 8);
+            cp_async16(base + oRawZ + (i * D + pc * 8) * 2, zb + t * a.z_stride_tok + pc * 8);
           } else if (zb) {
-            T* dz = reinterpret_cast<T*>(sb + oRaw + 3 * kRawPart + (i * D + pc * 8) * 2);
+            T* dz = reinterpret_cast<T*>(sb + oRawZ + (i * D + pc * 8) * 2);
 #pragma unroll
             for (int q = 0; q < 8; ++q) dz[q] = zb[t * a.z_stride_tok + pc * 8 + q];
           }
@@ -1488,47 +1497,61 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       if (lane == 0) mbar_arrive(chunk_free);
       return true;
     };
-    prefetch_qkv(0);
+    prefetch_rows(0);
     prefetch_z(0);
     bool ok = true;
     for (int ci = 0; ci < nchunks && ok; ++ci) {
       const int64_t c0 = (int64_t)ci * C;
       const int c = (int)(E - c0 < C ? E - c0 : C);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's q, k, v (z may fly on)
-      // the stack, v rows and gates of the previous chunk are consumed once its last MMAs ran
-      ok = bar_and(2, 128, ci == 0 || waitb(p2, (ci - 1) & 1, abort));  // and the staging landed
+      const int bf = ci & 1;
+      float* gam = arr(bf, aGam);
+      float* bet = arr(bf, aBet);
+      float* ink = arr(bf, aInK);
+      float* inq = arr(bf, aInQ);
+      float* ekf = arr(bf, aEk);
+      float* eqf = arr(bf, aEq);
+      float* skf = arr(bf, aSk);
+      ok = bar_and(2, 128, waitb(rows_full + bf, (ci >> 1) & 1, abort));  // q, k, v have landed
       if (!ok) break;
+      if (c < C) {  // rows past the request's end (the next request's, or zero fill) become zeros
+        const uint32_t stk = oKQ + bf * kStack, vbuf = oV + bf * kVBuf;
+        for (int e = lt; e < (C - c) * 48; e += 128) {  // 48 pieces of 16 bytes per row
+          const int i = c + e / 48, pc = e % 48;
+          uint32_t off;
+          if (pc < 32) {  // k (pc < 16) or q row, 128-byte swizzled block rows: zero as a whole
+            const int r = pc < 16 ? i : 64 + i;
+            off = stk + ((pc >> 3) & 1) * kKQBlk + r * 128 + (pc & 7) * 16;
+          } else {
+            off = vbuf + ((pc >> 3) & 1) * C * 128 + i * 128 + (pc & 7) * 16;
+          }
+          *reinterpret_cast<uint4*>(sb + off) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        named_barrier(2, 128);
+      }
       if (lt < C) {
         // g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)  (linear_attention.py:178-181)
         graw[lt] = gate_next ? neg_ea * softplus_f(to_f(a_next) + dtb) : 0.f;
         bet[lt] = gate_next ? 1.0f / (1.0f + expf(-to_f(b_next))) : 0.f;
       }
-      const T* rq = reinterpret_cast<const T*>(sb + oRaw);
-      const T* rk = reinterpret_cast<const T*>(sb + oRaw + kRawPart);
-      const T* rv = reinterpret_cast<const T*>(sb + oRaw + 2 * kRawPart);
-      const T* rz = reinterpret_cast<const T*>(sb + oRaw + 3 * kRawPart);
+      const T* rz = reinterpret_cast<const T*>(sb + oRawZ);
+      const uint32_t stk = base + oKQ + bf * kStack;
       const int d = 4 * lane;               // this lane's 4 elements of a row
       const int blk = lane >> 4, ch = (lane & 15) >> 1, e8 = (lane & 1) * 4;
-      // 8 rows at a time: the 16 squared norms (8 q, 8 k) of the rows reduce-scattered over the
-      // warp, one rsqrt per lane, then each row's factor broadcast back
+      // the norms of the rows in the stack, 8 rows at a time: the 16 squared norms (8 q, 8 k)
+      // reduce-scattered over the warp, one rsqrt per lane.  The raw rows are the MMA operands:
+      // bf16 products are exact in the fp32 accumulators, and the 1/|q|, 1/|k| factors are
+      // applied to the products
 #pragma unroll 1
       for (int bt = 0; bt < 2; ++bt) {
         float part[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int i = lw + 4 * (8 * bt + j);
-          const bool live = i < c;
-          // the raw rows are the MMA operands: bf16 products are exact in the fp32 accumulators,
-          // and the 1/|q|, 1/|k| factors are applied to the products
-          const uint2 qr = live ? *reinterpret_cast<const uint2*>(rq + i * D + d) : make_uint2(0u, 0u);
-          const uint2 kr = live ? *reinterpret_cast<const uint2*>(rk + i * D + d) : make_uint2(0u, 0u);
-          const uint2 v = live ? *reinterpret_cast<const uint2*>(rv + i * D + d) : make_uint2(0u, 0u);
-          sts_v2(base + oV + (i * D + d) * 2, v.x, v.y);
           const int rk_ = i, rq_ = 64 + i;
           const uint32_t ok_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rk_ & 7)) << 4) + e8 * 2;
           const uint32_t oq_ = (uint32_t)blk * kKQBlk + ((uint32_t)(ch ^ (rq_ & 7)) << 4) + e8 * 2;
-          sts_v2(base + oKQ + rk_ * 128 + ok_, kr.x, kr.y);
-          sts_v2(base + oKQ + rq_ * 128 + oq_, qr.x, qr.y);
+          const uint2 kr = *reinterpret_cast<const uint2*>(sb + (stk - base) + rk_ * 128 + ok_);
+          const uint2 qr = *reinterpret_cast<const uint2*>(sb + (stk - base) + rq_ * 128 + oq_);
           const float q0 = unpack_lo<T>(qr.x), q1 = unpack_hi<T>(qr.x), q2 = unpack_lo<T>(qr.y),
                       q3 = unpack_hi<T>(qr.y);
           const float k0 = unpack_lo<T>(kr.x), k1 = unpack_hi<T>(kr.x), k2 = unpack_lo<T>(kr.y),
@@ -1565,14 +1588,20 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         }
       }
       tc::fence_proxy_async_smem();  // the [K; Q] stack is read by the tensor core
-      mbar_arrive(in_full);
-      if (ci + 1 < nchunks) prefetch_qkv(ci + 1);  // the raw q, k, v rows are consumed
+      mbar_arrive(in_full + bf);
+      // the next chunk's rows, into the buffers chunk ci-1 used, once its phase 2 has completed
+      if (ci + 1 < nchunks) {
+        if (!bar_and(2, 128, ci == 0 || waitb(p2 + (bf ^ 1), ((ci - 1) >> 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        prefetch_rows(ci + 1);
+      }
       // the previous chunk's output rows (its silu(z) rows are still in oZ), then this chunk's
       // silu(z): the gate's exponentials and divisions and the output rows run here, beside the
       // lanes' work on this chunk, instead of on the lanes' critical path
       if (ci > 0 && !out_rows(ci - 1)) { ok = false; break; }
-      if (ci + 1 < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's z
-      else asm volatile("cp.async.wait_group 0;" ::: "memory");
+      asm volatile("cp.async.wait_group 0;" ::: "memory");  // this chunk's z
       ok = bar_and(2, 128, ok);
       if (!ok) break;
 #pragma unroll 4
@@ -1596,9 +1625,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       constexpr uint32_t idYZ = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(128, 64, false, false);
       constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, true);
-      const uint32_t kq = base + oKQ;
       for (int ci = 0; ci < nchunks; ++ci) {
-        if (!waitb(tm_free, ci & 1, abort) || !waitb(in_full, ci & 1, abort)) break;
+        const int bf = ci & 1;
+        const uint32_t kq = base + oKQ + bf * kStack;
+        if (!waitb(tm_free, ci & 1, abort) || !waitb(in_full + bf, (ci >> 1) & 1, abort)) break;
         tc::fence_proxy_async_smem();
         tc::fence_after_sync();
         // X = [K; Q] K^T of the raw rows (exact bf16 products: one MMA per k-step); KS' = S' K^T
@@ -1633,7 +1663,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
               mma_ts(tmem + cS, aK + kk * 8, tc::sw128_desc(kq + kk * 2048, kKQBlk, 1024), idS, true);
           }
         }
-        tc::commit(p2);
+        tc::commit(p2 + bf);
       }
       // every MMA issued has completed before TMEM is read for the last time or released
       tc::commit(fin);
@@ -1666,7 +1696,15 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       }
     }
     for (int ci = 0; ci < nchunks; ++ci) {
-      ok = bar_and(1, 128, ok && waitb(in_full, ci & 1, abort) && waitb(p1, ci & 1, abort));
+      const int bf = ci & 1;
+      const float* gam = arr(bf, aGam);
+      const float* bet = arr(bf, aBet);
+      const float* ink = arr(bf, aInK);
+      const float* inq = arr(bf, aInQ);
+      const float* ekf = arr(bf, aEk);
+      const float* eqf = arr(bf, aEq);
+      const float* skf = arr(bf, aSk);
+      ok = bar_and(1, 128, ok && waitb(in_full + bf, (ci >> 1) & 1, abort) && waitb(p1, ci & 1, abort));
       if (!ok) break;
       tc::fence_after_sync();
       // ---- rows of X: Mk (l < 64, stored transposed) or Mq (l >= 64, bf16 hi / lo K-major rows)
@@ -1725,9 +1763,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           tc::ld32(lb + cY, *reinterpret_cast<float(*)[32]>(&u[0]));
           tc::ld32(lb + cY + 32, *reinterpret_cast<float(*)[32]>(&u[32]));
           tc::wait_ld();
-          const T* vr = reinterpret_cast<const T*>(sb + oV);
+          // v rows as two [64][64] halves: element (i, l) at (l / 64) * 4096 + i * 64 + l % 64
+          const T* vr = reinterpret_cast<const T*>(sb + oV + bf * kVBuf) + (l >> 6) * (C * 64) + (l & 63);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * D + l]) - ekf[i] * u[i]);
+          for (int i = 0; i < 64; ++i) u[i] = bet[i] * (to_f(vr[i * 64]) - ekf[i] * u[i]);
 #pragma unroll
           for (int p = 0; p < 32; ++p) u2[p] = pack2(u[2 * p], u[2 * p + 1]);
         }
@@ -1791,7 +1830,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       __syncwarp();
       if (lane == 0) mbar_arrive(l1);
       // the previous chunk's output rows are written by the loaders before O' replaces them
-      ok = bar_and(1, 128, waitb(p2, ci & 1, abort) && waitb(chunk_free, ci & 1, abort));
+      ok = bar_and(1, 128, waitb(p2 + bf, (ci >> 1) & 1, abort) && waitb(chunk_free, ci & 1, abort));
       if (!ok) break;
       tc::fence_after_sync();
       // ---- O' rounded to T into the transposed output rows, S' hi / lo for the next chunk; then
@@ -1890,8 +1929,16 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(tc_chunk::chunk_tc_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
     if (e != cudaSuccess) return e;
+    // the conv outputs [T, conv_dim] in 64 x 64 boxes: q, k SWIZZLE_128B (the MMA layout), v plain
+    CUtensorMap map_qk, map_v;
+    const uint64_t stride = (uint64_t)conv_dim * sizeof(T);
+    if (!tma::map_2d_u16(&map_qk, w.conv_out, (uint64_t)a.num_tokens, (uint64_t)conv_dim, stride,
+                         64, tc_chunk::C, true) ||
+        !tma::map_2d_u16(&map_v, w.conv_out, (uint64_t)a.num_tokens, (uint64_t)conv_dim, stride,
+                         64, tc_chunk::C, false))
+      return cudaErrorInvalidValue;
     tc_chunk::chunk_tc_kernel<T><<<a.batch_size * a.num_v_heads, tc_chunk::kThreads, tsmem, s>>>(
-        a, w.start, (const T*)w.conv_out, w.order);
+        a, w.start, (const T*)w.conv_out, w.order, map_qk, map_v);
     return cudaGetLastError();
   }
   if constexpr (DK == DV && (DK == 64 || DK == 128)) {  // a7: chunked form

@@ -1,0 +1,54 @@
+// 2-D tiled TMA loads (cp.async.bulk.tensor) of 16-bit row-major tensors in this GPU's own memory:
+// the device-side box load and the host-side tensor-map encoding.  No multicast.
+#pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tf {
+namespace tma {
+
+// one box at element coordinates (x = column, y = row) into shared memory at dst, completing
+// `bytes` of the barrier's expected transaction count; x * 2 bytes must be a multiple of 16
+__device__ __forceinline__ void load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                        uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [rows, cols] 16-bit elements with a row stride in bytes, read in boxes of box_rows x box_cols,
+// zero fill outside the tensor; swizzle128 lays a 128-byte box row out as SWIZZLE_128B
+inline bool map_2d_u16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                       uint64_t stride_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  auto enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tma
+}  // namespace tf
