@@ -1182,7 +1182,7 @@ constexpr int oArr = oMqL + C * 128;
 constexpr int kArr = 7 * C * 4;
 enum { aGam = 0, aBet, aInK, aInQ, aEk, aEq, aSk };
 constexpr int oGr = oArr + 2 * kArr;          // raw g [64] (loaders)
-constexpr int oBar = oGr + C * 4;             // in_full[2] p1 l1 p2[2] tm_free chunk_free fin rows_full[2]
+constexpr int oBar = oGr + C * 4;             // in_full[2] p1 l1 p2[2] tm_free chunk_free fin rows_full[2] p1x
 constexpr int oWords = oBar + 96;             // tmem holder, abort
 constexpr int oRawZ = (oWords + 16 + 1023) & ~1023;  // next chunk's raw z rows (T)
 constexpr int kSmem = oRawZ + C * D * 2 + 1024;
@@ -1326,6 +1326,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   uint64_t* chunk_free = bars + 7;     // the output rows are written: O' may replace them
   uint64_t* fin = bars + 8;            // every MMA of the CTA has completed
   uint64_t* rows_full = bars + 9;      // [2] a chunk's q, k, v rows have landed (TMA)
+  uint64_t* p1x = bars + 11;           // X of the chunk is in TMEM (the rest of phase 1 follows)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
 
@@ -1351,6 +1352,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     mbar_init(p2 + 1, 1);
     mbar_init(rows_full, 1);
     mbar_init(rows_full + 1, 1);
+    mbar_init(p1x, 1);
     mbar_init(tm_free, 4);
     mbar_init(chunk_free, 4);
     mbar_init(fin, 1);
@@ -1482,10 +1484,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
             }
             T* out = outb + (int64_t)i * a.out_stride_tok;
             if (ovec) {
-              T pk[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) pk[e] = from_f<T>(y[e]);
-              *reinterpret_cast<uint2*>(out) = *reinterpret_cast<const uint2*>(pk);
+              *reinterpret_cast<uint2*>(out) =
+                  make_uint2(pack2_rn<T>(y[0], y[1]), pack2_rn<T>(y[2], y[3]));
             } else {
 #pragma unroll
               for (int e = 0; e < 4; ++e) out[e] = from_f<T>(y[e]);
@@ -1631,18 +1631,23 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         if (!waitb(tm_free, ci & 1, abort) || !waitb(in_full + bf, (ci >> 1) & 1, abort)) break;
         tc::fence_proxy_async_smem();
         tc::fence_after_sync();
-        // X = [K; Q] K^T of the raw rows (exact bf16 products: one MMA per k-step); KS' = S' K^T
-        // and QS' = S' Q^T as S'hi.K + S'lo.K
+        // X = [K; Q] K^T of the raw rows (exact bf16 products: one MMA per k-step), committed on
+        // its own so that the masks start early; then KS' = S' K^T and QS' = S' Q^T as
+        // S'hi.K + S'lo.K
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t bKQ = tc::sw128_desc(kq + (kk >> 2) * kKQBlk + (kk & 3) * 32, 16, 1024);
+          tc::mma_bf16(tmem + cX, bKQ, bKQ, idX, kk > 0);
+        }
+        tc::commit(p1x);
 #pragma unroll 1
         for (int part = 0; part < 2; ++part) {
           const uint32_t aT = tmem + (part ? cSL : cSH);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * kKQBlk + (kk & 3) * 32;
-            const bool acc = part > 0 || kk > 0;
             const uint64_t bKQ = tc::sw128_desc(kq + off, 16, 1024);  // K rows, then Q rows
-            if (part == 0) tc::mma_bf16(tmem + cX, bKQ, bKQ, idX, kk > 0);
-            mma_ts(tmem + cY, aT + kk * 8, bKQ, idYZ, acc);  // [KS' | QS'] over cY, cZ
+            mma_ts(tmem + cY, aT + kk * 8, bKQ, idYZ, part > 0 || kk > 0);  // [KS' | QS'] over cY, cZ
           }
         }
         tc::commit(p1);
@@ -1674,18 +1679,22 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     const int l = tid;
     const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
     bool ok = true;
-    {  // S' = S^T into TMEM, with its bf16 hi / lo split
+    {  // S' = S^T into TMEM, with its bf16 hi / lo split; 64 loads in flight per thread
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        float sv[32];
+      for (int c2 = 0; c2 < 2; ++c2) {
+        float sv[64];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) sv[k] = __ldcs(st_g + (size_t)(cc * 32 + k) * D + l);
-        tc::st32(lb + cS + cc * 32, sv);
-        uint32_t hi[16], lo[16];
+        for (int k = 0; k < 64; ++k) sv[k] = __ldcs(st_g + (size_t)(c2 * 64 + k) * D + l);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) split2(sv[2 * k], sv[2 * k + 1], hi[k], lo[k]);
-        st16u(lb + cSH + cc * 16, hi);
-        st16u(lb + cSL + cc * 16, lo);
+        for (int h = 0; h < 2; ++h) {
+          const int cc = 2 * c2 + h;
+          tc::st32(lb + cS + cc * 32, *reinterpret_cast<float(*)[32]>(&sv[32 * h]));
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) split2(sv[32 * h + 2 * k], sv[32 * h + 2 * k + 1], hi[k], lo[k]);
+          st16u(lb + cSH + cc * 16, hi);
+          st16u(lb + cSL + cc * 16, lo);
+        }
       }
       tc::wait_st();
       tc::fence_before_sync();
@@ -1704,7 +1713,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       const float* ekf = arr(bf, aEk);
       const float* eqf = arr(bf, aEq);
       const float* skf = arr(bf, aSk);
-      ok = bar_and(1, 128, ok && waitb(in_full + bf, (ci >> 1) & 1, abort) && waitb(p1, ci & 1, abort));
+      ok = bar_and(1, 128, ok && waitb(in_full + bf, (ci >> 1) & 1, abort) && waitb(p1x, ci & 1, abort));
       if (!ok) break;
       tc::fence_after_sync();
       // ---- rows of X: Mk (l < 64, stored transposed) or Mq (l >= 64, bf16 hi / lo K-major rows)
@@ -1751,7 +1760,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           }
         }
       }
-      named_barrier(1, 128);
+      ok = bar_and(1, 128, waitb(p1, ci & 1, abort));  // KS', QS' (and the masks are written)
+      if (!ok) break;
+      tc::fence_after_sync();
       // ---- U' row l: (I + Mk) u = beta (v - e^g KS), right-looking: once u_j is final, every
       //      later row takes its term at once (independent FMAs; column j of Mk is contiguous)
       {
