@@ -39,25 +39,30 @@ def bf16_step(x: np.ndarray) -> np.ndarray:
     return np.exp2(e - 7)
 
 
-def assert_close_bf16(got: np.ndarray, ref: np.ndarray, max_abs=2e-2, mean_abs=2e-3, what=""):
+def assert_close_bf16(got: np.ndarray, ref: np.ndarray, max_abs=2e-2, mean_abs=2e-3, what="",
+                      steps=1):
     """The hot path's bf16 tolerance: max-abs 2e-2, mean-abs 2e-3.
 
     For |ref| >= 4 one bf16 step (2^-5 and up) is itself above 2e-2, so an element there passes
     when it is within one step of the reference value; everywhere else the absolute bound holds.
+    steps=2 is for outputs the reference rounds twice to bf16 (the gated RMSNorm of an output
+    that was itself rounded, rms_norm_gated.py after linear_attention.py:298): an fp32-level
+    difference that flips the first rounding moves the normalised value by one step of its own
+    before the second rounding, so such an element may sit two steps from the reference.
     """
     assert got.shape == ref.shape, (got.shape, ref.shape)
     assert np.isfinite(got).all(), f"{what}: non-finite output"
     r = ref.astype(np.float64)
     d = np.abs(got.astype(np.float64) - r)
-    bound = np.maximum(max_abs, bf16_step(r))
+    bound = np.maximum(max_abs, steps * bf16_step(r))
     worst = int(np.argmax(d - bound))
     assert (d <= bound).all(), (f"{what}: |diff| {d.ravel()[worst]:.3g} > {bound.ravel()[worst]:.3g}"
                                 f" at ref {r.ravel()[worst]:.4g} (max-abs {d.max():.3g})")
     assert d.mean() <= mean_abs, f"{what}: mean-abs {d.mean():.3g} > {mean_abs}"
 
 
-def assert_close(got, ref, dtype: str, what="", f32_rtol=1e-4, f32_atol=1e-5):
+def assert_close(got, ref, dtype: str, what="", f32_rtol=1e-4, f32_atol=1e-5, bf16_steps=1):
     if dtype == "f32":
         np.testing.assert_allclose(got, ref, rtol=f32_rtol, atol=f32_atol, err_msg=what)
     else:
-        assert_close_bf16(got, ref, what=what)
+        assert_close_bf16(got, ref, what=what, steps=bf16_steps)

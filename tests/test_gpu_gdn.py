@@ -147,6 +147,40 @@ def test_decode_many_items_with_a_skipped_request():
     np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=1e-4, atol=1e-5)
 
 
+def test_extend_long_request_27b_heads_vs_oracle():
+    """A 1000-token request (16 chunks: the tensor-core chunk kernel alternates its two sets of
+    chunk buffers and barriers many times) between short ones, against the oracle.  The gated
+    outputs are rounded twice by the reference: two bf16 steps allowed (tests/helpers.py)."""
+    ext = [3, 1000, 130]
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext, req=[2, 0, 3],
+                slots=5, seed=1133)
+    inp = C.gdn_inputs(spec)
+    t = _tensors(inp, "bf16")
+    out = values(_run(spec, t, True), "bf16")
+    orc, cs, ss = _oracle(spec, inp, True)
+    assert_close(out, orc, "bf16", what="extend with a 1000-token request", bf16_steps=2)
+    np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+    np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
+
+
+def test_extend_more_ctas_than_sms_vs_oracle():
+    """30 requests x 6 v-heads = 180 chunk-kernel CTAs (more than the SMs), lengths 1-200 in the
+    longest-first order, so SMs run a second CTA after the first released TMEM.  Of 2.3M gated
+    outputs, a dozen sit two bf16 steps from the reference (its double rounding), the raw outputs
+    within 3e-4."""
+    ext = np.random.default_rng(1180).integers(1, 201, 30).tolist()
+    req = np.random.default_rng(1181).permutation(34)[:30].tolist()
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext, req=req, slots=34,
+                seed=1182)
+    inp = C.gdn_inputs(spec)
+    t = _tensors(inp, "bf16")
+    out = values(_run(spec, t, True), "bf16")
+    orc, cs, ss = _oracle(spec, inp, True)
+    assert_close(out, orc, "bf16", what="extend, 180 CTAs", bf16_steps=2)
+    np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+    np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
+
+
 @pytest.mark.parametrize("ext", [[1, 300, 7, 64], [65, 1, 1, 129]])
 def test_extend_random_27b_heads_vs_oracle(ext):
     spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext,
