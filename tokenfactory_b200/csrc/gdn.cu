@@ -321,38 +321,104 @@ __global__ void __launch_bounds__(2 * DV, 2) decode_kernel(tf_gdn_args a) {
     const T* x = reinterpret_cast<const T*>(a.qkv) + (int64_t)b * a.qkv_stride_tok;
     T* cst = reinterpret_cast<T*>(a.conv_state) + slot * a.conv_stride_slot;
     const int nch = 2 * DK + vpk * DV;
-    for (int e = tid; e < nch; e += blockDim.x) {
-      int c;
-      if (e < DK) c = kh * DK + e;
-      else if (e < 2 * DK) c = key_dim + kh * DK + (e - DK);
-      else c = 2 * key_dim + kh * vpk * DV + (e - 2 * DK);
-      float win[8];
-      for (int j = 0; j < K - 1; ++j) win[j] = to_f(cst[(int64_t)c * (K - 1) + j]);
-      const float xv = to_f(x[c]);
-      const T* w = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * K;
-      float acc = 0.f;
-      for (int j = 0; j < K - 1; ++j) acc = fmaf(to_f(w[j]), win[j], acc);
-      acc = fmaf(to_f(w[K - 1]), xv, acc);
-      if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
-      const float y = round_to<T>(silu_f(round_to<T>(acc)));
-      for (int j = 0; j + 1 < K - 1; ++j) cst[(int64_t)c * (K - 1) + j] = from_f<T>(win[j + 1]);
-      if (K > 1) cst[(int64_t)c * (K - 1) + K - 2] = x[c];
-      q_s[e] = y;  // q_s | k_s | v_s are contiguous
-    }
-    if (tid < vpk) {
-      float g, be;
-      gate_values<T>(a, b, kh * vpk + tid, &g, &be);
-      gb_s[2 * tid] = g;
-      gb_s[2 * tid + 1] = be;
-    }
-    if (a.z != nullptr) {  // the output gate's operands, off the per-head critical path
-      const T* zr = reinterpret_cast<const T*>(a.z) + (int64_t)b * a.z_stride_tok +
-                    (int64_t)kh * vpk * DV;
-      const bool shared_w = a.norm_weight_len == DV;
-      const T* wr = reinterpret_cast<const T*>(a.norm_weight) + (shared_w ? 0 : (int64_t)kh * vpk * DV);
-      for (int e = tid; e < vpk * DV; e += blockDim.x) {
-        zs_s[e] = silu_f(to_f(zr[e]));
-        ws_s[e] = to_f(wr[shared_w ? e % DV : e]);
+    auto channel = [&](int e) {
+      return e < DK ? kh * DK + e
+                    : (e < 2 * DK ? key_dim + kh * DK + (e - DK) : 2 * key_dim + kh * vpk * DV + (e - 2 * DK));
+    };
+    const T* zr = a.z ? reinterpret_cast<const T*>(a.z) + (int64_t)b * a.z_stride_tok + (int64_t)kh * vpk * DV
+                      : nullptr;
+    const bool shared_w = a.norm_weight_len == DV;
+    const T* wr = a.z ? reinterpret_cast<const T*>(a.norm_weight) + (shared_w ? 0 : (int64_t)kh * vpk * DV)
+                      : nullptr;
+    const int bdim = blockDim.x;
+    if (sizeof(T) == 2 && K == 4 && nch <= 3 * bdim && vpk * DV <= 2 * bdim &&
+        (reinterpret_cast<uintptr_t>(a.conv_weight) & 7) == 0) {
+      // 16-bit activations (a channel's 4 weights are one 8-byte load): every load of the item
+      // first (conv windows, weights and inputs of up to 3 channels per thread, z and the norm
+      // weights, the gates), then the arithmetic: one memory round trip
+      // instead of one per pass.  Same products and roundings as the loop below.
+      T st[3][3], xv[3], zv[2], wv2[2];
+      uint2 w4[3];
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        const int e = tid + u * bdim;
+        if (e < nch) {
+          const int c = channel(e);
+          const T* sp = cst + (int64_t)c * 3;
+          st[u][0] = sp[0];
+          st[u][1] = sp[1];
+          st[u][2] = sp[2];
+          xv[u] = x[c];
+          w4[u] = *reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * 4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int e = tid + u * bdim;
+        if (zr != nullptr && e < vpk * DV) {
+          zv[u] = zr[e];
+          wv2[u] = wr[shared_w ? e % DV : e];
+        }
+      }
+      if (tid < vpk) {
+        float g, be;
+        gate_values<T>(a, b, kh * vpk + tid, &g, &be);
+        gb_s[2 * tid] = g;
+        gb_s[2 * tid + 1] = be;
+      }
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        const int e = tid + u * bdim;
+        if (e < nch) {
+          const T* wt = reinterpret_cast<const T*>(&w4[u]);
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < 3; ++j) acc = fmaf(to_f(wt[j]), to_f(st[u][j]), acc);
+          acc = fmaf(to_f(wt[3]), to_f(xv[u]), acc);
+          const int c = channel(e);
+          if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
+          T* sp = cst + (int64_t)c * 3;
+          sp[0] = st[u][1];
+          sp[1] = st[u][2];
+          sp[2] = xv[u];
+          q_s[e] = round_to<T>(silu_f(round_to<T>(acc)));  // q_s | k_s | v_s are contiguous
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int e = tid + u * bdim;
+        if (zr != nullptr && e < vpk * DV) {
+          zs_s[e] = silu_f(to_f(zv[u]));
+          ws_s[e] = to_f(wv2[u]);
+        }
+      }
+    } else {
+      for (int e = tid; e < nch; e += bdim) {
+        const int c = channel(e);
+        float win[8];
+        for (int j = 0; j < K - 1; ++j) win[j] = to_f(cst[(int64_t)c * (K - 1) + j]);
+        const float xvf = to_f(x[c]);
+        const T* w = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * K;
+        float acc = 0.f;
+        for (int j = 0; j < K - 1; ++j) acc = fmaf(to_f(w[j]), win[j], acc);
+        acc = fmaf(to_f(w[K - 1]), xvf, acc);
+        if (a.conv_bias) acc += to_f(reinterpret_cast<const T*>(a.conv_bias)[c]);
+        const float y = round_to<T>(silu_f(round_to<T>(acc)));
+        for (int j = 0; j + 1 < K - 1; ++j) cst[(int64_t)c * (K - 1) + j] = from_f<T>(win[j + 1]);
+        if (K > 1) cst[(int64_t)c * (K - 1) + K - 2] = x[c];
+        q_s[e] = y;  // q_s | k_s | v_s are contiguous
+      }
+      if (tid < vpk) {
+        float g, be;
+        gate_values<T>(a, b, kh * vpk + tid, &g, &be);
+        gb_s[2 * tid] = g;
+        gb_s[2 * tid + 1] = be;
+      }
+      if (zr != nullptr) {  // the output gate's operands, off the per-head critical path
+        for (int e = tid; e < vpk * DV; e += bdim) {
+          zs_s[e] = silu_f(to_f(zr[e]));
+          ws_s[e] = to_f(wr[shared_w ? e % DV : e]);
+        }
       }
     }
     __syncthreads();
