@@ -642,13 +642,13 @@ __global__ void __launch_bounds__(kConvThreads) conv4_tiled_kernel(tf_gdn_args a
 // arithmetic, so 19 independent loads are in flight per thread.  Same FMA order and roundings
 // as conv4_tiled_kernel; SiLU with a hardware exponential and an approximate division (the result
 // is rounded to the 16-bit type, where the two differ in rare last-place cases).
-constexpr int kConvVecTok = 16;
+constexpr int kConvVecTok = 8;
 constexpr int kConvVecThreads = 128;
 
 __device__ __forceinline__ float silu_rt(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <typename T>
-__global__ void __launch_bounds__(kConvVecThreads, 4) conv4_vec_kernel(tf_gdn_args a,
+__global__ void __launch_bounds__(kConvVecThreads, 6) conv4_vec_kernel(tf_gdn_args a,
                                                                        const int64_t* start,
                                                                        T* conv_out) {
   static_assert(sizeof(T) == 2, "16-bit activations");
