@@ -1,5 +1,5 @@
 // 2-D tiled TMA loads (cp.async.bulk.tensor) of 16-bit row-major tensors in this GPU's own memory:
-// the device-side box load and the host-side tensor-map encoding.  No multicast.
+// the device-side box load (into this CTA's own shared memory only) and the host-side tensor-map encoding.
 #pragma once
 #include <cuda.h>
 #include <cudaTypedefs.h>
