@@ -118,6 +118,26 @@ def test_decode_random_shapes_vs_oracle(shape):
     assert_close(out, want, "bf16", what=f"decode {shape}")
 
 
+def test_decode_request_without_keys_gives_nan_rows():
+    """A request with no keys (seq_len 0) among others: its output rows are NaN, as the
+    reference's softmax over an empty row, and the other rows match the batch where it has keys
+    (the split points move, so within the bf16 tolerance)."""
+    spec = _random_decode(321, 6, 32, 4, 256, 200, 5000, slots=1)
+    spec["slots"] = sum(spec["seq"]) + 3
+    inp = C.attn_inputs(spec)
+    B = len(spec["seq"])
+    ref = values(_run(inp, spec, gate_mode="sigmoid"), "bf16").reshape(B, -1)
+    sl = inp["seq_lens"].copy()
+    sl[2] = 0
+    seq = list(spec["seq"])
+    seq[2] = 0
+    out = values(_run(dict(inp, seq_lens=sl), dict(spec, seq=seq), gate_mode="sigmoid"),
+                 "bf16").reshape(B, -1)
+    assert np.isnan(out[2]).all()
+    keep = [i for i in range(B) if i != 2]
+    assert_close(out[keep], ref[keep], "bf16", what="decode beside an empty request")
+
+
 def test_decode_repeat_is_deterministic():
     spec = _random_decode(7, 9, 32, 4, 256, 10, 4000, slots=1)
     spec["slots"] = sum(spec["seq"]) + 1

@@ -480,67 +480,111 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
-// combine: units cut by CTA range boundaries
+// combine: the units cut by CTA range boundaries.  Combine CTA c takes the unit holding the first
+// tile of decode CTA c and merges it when c is that unit's first boundary (so each cut unit is
+// merged once, by one of at most nctas CTAs, with the schedule searched in shared memory); every
+// CTA also writes the NaN rows of the requests without keys b = c, c + gridDim.x, ...
 // ---------------------------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws ws,
                                                       int nctas_launched) {
-  extern __shared__ float csm[];  // w[np][kHeads] then int sl[np]
+  // w[nctas][kHeads], ml[nctas][kHeads][2], then int sl[nctas], ts[B+1]
+  extern __shared__ float csm[];
   const int B = a.batch_size, Hkv = a.num_kv_heads;
   const int G = a.num_q_heads / Hkv;
-  const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
-  const int64_t total = (int64_t)ws.tile_start[B] * Hkv;
-  const int nctas = (int64_t)nctas_launched < total ? nctas_launched : (int)total;
-  const int nt = ws.tile_start[b + 1] - ws.tile_start[b];
+  const int tid = threadIdx.x;
+  float* w = csm;
+  float* ml = w + nctas_launched * kHeads;
+  int* sl = reinterpret_cast<int*>(ml + nctas_launched * kHeads * 2);
+  int* ts = sl + nctas_launched;
+  for (int i = tid; i <= B; i += blockDim.x) ts[i] = ws.tile_start[i];
+  __syncthreads();
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
   const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
-  if (nt == 0) {  // no keys: softmax over an empty row is NaN in the reference as well
-    for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-      const int hd = e / D, d = e - hd * D;
-      out[(int64_t)b * a.out_stride_tok + (int64_t)(h * G + hd) * a.out_stride_head + d] =
-          __float2bfloat16_rn(NAN);
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    if (ts[b + 1] != ts[b]) continue;
+    // no keys: softmax over an empty row is NaN in the reference as well
+    for (int e = tid; e < Hkv * G * D; e += blockDim.x) {
+      const int hq = e / D, d = e - hq * D;
+      out[(int64_t)b * a.out_stride_tok + (int64_t)hq * a.out_stride_head + d] = __float2bfloat16_rn(NAN);
     }
-    return;
   }
-  const int64_t su = (int64_t)ws.tile_start[b] * Hkv + (int64_t)h * nt, eu = su + nt;
+  const int64_t total = (int64_t)ts[B] * Hkv;
+  const int nctas = (int64_t)nctas_launched < total ? nctas_launched : (int)total;
+  const int c = blockIdx.x;
+  if (c == 0 || c >= nctas) return;
+  const int64_t g = cta_range(c, total, nctas);
+  const int b = first_req_after(ts, B, Hkv, g);
+  const int nt = ts[b + 1] - ts[b];
+  const int h = (int)((g - (int64_t)ts[b] * Hkv) / nt);
+  const int64_t su = (int64_t)ts[b] * Hkv + (int64_t)h * nt, eu = su + nt;
   const int c0 = (int)(((su + 1) * nctas - 1) / total);
   const int c1 = (int)((eu * nctas - 1) / total);
-  if (c0 == c1) return;  // finished inside one CTA
+  if (c0 == c1 || c != c0 + 1) return;  // finished inside one CTA, or merged at its first boundary
   const int np = c1 - c0 + 1;
-  float* w = csm;
-  int* sl = reinterpret_cast<int*>(csm + np * kHeads);
-  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+  for (int i = tid; i < np; i += blockDim.x) {
     const int cc = c0 + i;
     const int64_t rc = cta_range(cc, total, nctas);
     sl[i] = 2 * cc + ((su > rc ? su : rc) == rc ? 0 : 1);
   }
   __syncthreads();
-  if (threadIdx.x < G) {
-    const int hd = threadIdx.x;
+  for (int e = tid; e < np * G; e += blockDim.x) {  // every piece's (max, sum) at once
+    const int i = e / G, hd = e - (e / G) * G;
+    ml[(i * kHeads + hd) * 2] = ws.part_ml[(sl[i] * kHeads + hd) * 2];
+    ml[(i * kHeads + hd) * 2 + 1] = ws.part_ml[(sl[i] * kHeads + hd) * 2 + 1];
+  }
+  __syncthreads();
+  if (tid < G) {
+    const int hd = tid;
     float M = -INFINITY;
-    for (int i = 0; i < np; ++i) M = fmaxf(M, ws.part_ml[(sl[i] * kHeads + hd) * 2]);
+    for (int i = 0; i < np; ++i) M = fmaxf(M, ml[(i * kHeads + hd) * 2]);
     float L = 0.f;
     for (int i = 0; i < np; ++i) {
-      const float m = ws.part_ml[(sl[i] * kHeads + hd) * 2];
+      const float m = ml[(i * kHeads + hd) * 2];
       const float f = m == -INFINITY ? 0.f : exp2f(m - M);
       w[i * kHeads + hd] = f;
-      L += ws.part_ml[(sl[i] * kHeads + hd) * 2 + 1] * f;
+      L += ml[(i * kHeads + hd) * 2 + 1] * f;
     }
     const float inv = 1.0f / L;
     for (int i = 0; i < np; ++i) w[i * kHeads + hd] *= inv;
   }
+  // this thread's outputs e = tid + 256 k: gate values and each piece's partial sums requested
+  // together (a piece at a time), then the same ordered sums as one loop per output
+  constexpr int kPer = kHeads * D / 256;
+  const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr;
+  __nv_bfloat16 gv[kPer];
+  float o[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int e = tid + k * 256;
+    o[k] = 0.f;
+    if (gated && e < G * D) {
+      const int hd = e / D, d = e - hd * D;
+      gv[k] = gate[(int64_t)b * a.gate_stride_tok + (int64_t)(h * G + hd) * a.gate_stride_head + d];
+    }
+  }
   __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+  for (int i = 0; i < np; ++i) {
+    float po[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int e = tid + k * 256;
+      if (e < G * D) po[k] = ws.part_o[((int64_t)sl[i] * kHeads + e / D) * D + (e - (e / D) * D)];
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int e = tid + k * 256;
+      if (e < G * D) o[k] = fmaf(w[i * kHeads + e / D], po[k], o[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int e = tid + k * 256;
+    if (e >= G * D) break;
     const int hd = e / D, d = e - hd * D;
-    float o = 0.f;
-    for (int i = 0; i < np; ++i)
-      o = fmaf(w[i * kHeads + hd], ws.part_o[((int64_t)sl[i] * kHeads + hd) * D + d], o);
     const int hq = h * G + hd;
-    float r = round_to<__nv_bfloat16>(o);
-    if (a.gate_mode != TF_GATE_NONE && gate != nullptr)
-      r = apply_gate<__nv_bfloat16>(
-          r, to_f(gate[(int64_t)b * a.gate_stride_tok + (int64_t)hq * a.gate_stride_head + d]),
-          a.gate_mode);
+    float r = round_to<__nv_bfloat16>(o[k]);
+    if (gated) r = apply_gate<__nv_bfloat16>(r, to_f(gv[k]), a.gate_mode);
     out[(int64_t)b * a.out_stride_tok + (int64_t)hq * a.out_stride_head + d] = __float2bfloat16_rn(r);
   }
 }
@@ -553,11 +597,13 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, c
   if (e != cudaSuccess) return e;
   plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, a.r2t_cols, ws.tile_start);
   decode_kernel<D><<<nctas, kThreads, Cfg<D>::kSmem, s>>>(a, ws, nctas);
-  // a unit spans at most every CTA: weights [nctas][kHeads] + slot ids [nctas]
-  const size_t csmem = (size_t)nctas * (kHeads * 4 + 4);
+  // a unit spans at most every CTA: weights [nctas][kHeads], (max, sum) [nctas][kHeads][2] and
+  // slot ids [nctas], then the schedule tile_start[B+1]
+  const size_t csmem = (size_t)nctas * (3 * kHeads * 4 + 4) + (size_t)(a.batch_size + 1) * 4;
+  if (csmem > 227 * 1024) return cudaErrorInvalidValue;
   e = cudaFuncSetAttribute(combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
   if (e != cudaSuccess) return e;
-  combine_kernel<D><<<a.batch_size * a.num_kv_heads, 256, csmem, s>>>(a, ws, nctas);
+  combine_kernel<D><<<nctas, 256, csmem, s>>>(a, ws, nctas);
   return cudaGetLastError();
 }
 
