@@ -151,10 +151,11 @@ constexpr int kAcc = 4;                         // TMEM accumulators of 128 colu
 constexpr int kSmem = kStages * kStageBytes + 256 + 1024;
 
 struct Bars {
-  uint64_t full[kStages], empty[kStages], pfull[kAcc], pfree[kAcc];
+  uint64_t full[kStages], empty[kStages], pfull[kAcc], pfree[kAcc], fin;
   uint32_t tmem;
   int abort;
 };
+static_assert(sizeof(Bars) <= 256, "barriers overflow their shared-memory slot");
 
 __device__ __forceinline__ bool wait_b(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t addr = smem_u32(bar);
@@ -219,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
       mbar_init(&bars->pfull[b], 1);
       mbar_init(&bars->pfree[b], 8);
     }
+    mbar_init(&bars->fin, 1);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -231,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
   if (warp == kLoadWarp) {
     // ============ loads: two TMA boxes (q rows, w rows; zero fill past M, N and K) per stage ============
     if (lane == 0) {
+      int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % kStages;
         if (kb >= kStages && !wait_b(&bars->empty[s], ((kb / kStages) - 1) & 1, abort)) break;
@@ -238,7 +241,11 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
         mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
         tma_load_box(st, &map_q, kb * kBK, (int)m0, &bars->full[s]);
         tma_load_box(st + kTile, &map_w, kb * kBK, n0, &bars->full[s]);
+        issued = kb + 1;
       }
+      // after an abort, boxes still in flight land (bounded wait) before the CTA ends
+      for (int kb = issued - kStages > 0 ? issued - kStages : 0; kb < issued; ++kb)
+        mbar_wait(&bars->full[kb % kStages], (kb / kStages) & 1);
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -267,6 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
         tc::commit(&bars->empty[s]);
         tc::commit(&bars->pfull[b]);
       }
+      // every MMA issued has completed before TMEM is released, also after an abort (bounded)
+      tc::commit(&bars->fin);
+      mbar_wait(&bars->fin, 0);
     }
     __syncwarp();
   } else {

@@ -1452,9 +1452,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     // thread issues them.  Rows past the batch are zero-filled by the TMA unit, rows of the next
     // request are zeroed once they land.  The gates' raw a, b are loaded alongside; z is staged
     // raw by cp.async once the previous silu rows are written.
+    int tma_pending = -1;  // the chunk whose rows were requested and not yet waited for
     auto prefetch_rows = [&](int ci) {
       const int64_t c0 = (int64_t)ci * C;
       const int c = (int)(E - c0 < C ? E - c0 : C);
+      tma_pending = ci;
       if (lt == 0) {
         const uint32_t stk = base + oKQ + (ci & 1) * kStack, vbuf = base + oV + (ci & 1) * kVBuf;
         uint64_t* bar = rows_full + (ci & 1);
@@ -1579,6 +1581,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       float* skf = arr(bf, aSk);
       ok = bar_and(2, 128, waitb(rows_full + bf, (ci >> 1) & 1, abort));  // q, k, v have landed
       if (!ok) break;
+      tma_pending = -1;
       if (c < C) {  // rows past the request's end (the next request's, or zero fill) become zeros
         const uint32_t stk = oKQ + bf * kStack, vbuf = oV + bf * kVBuf;
         for (int e = lt; e < (C - c) * 48; e += 128) {  // 48 pieces of 16 bytes per row
@@ -1684,6 +1687,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     }
     if (ok) out_rows(nchunks - 1);
     asm volatile("cp.async.wait_all;" ::: "memory");
+    // after an abort, rows still in flight land before the CTA (and its shared memory) ends
+    if (lt == 0 && tma_pending >= 0) mbar_wait(rows_full + (tma_pending & 1), (tma_pending >> 1) & 1);
   } else if (warp == 8) {
     // ============ MMA issue (one thread) ============
     if (lane == 0) {
@@ -1736,8 +1741,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         }
         tc::commit(p2 + bf);
       }
-      // every MMA issued has completed before TMEM is read for the last time or released
+      // every MMA issued has completed before TMEM is read for the last time or released; the
+      // issuing thread also waits for it (bounded), so that after an abort no MMA is in flight
+      // when TMEM is released
       tc::commit(fin);
+      mbar_wait(fin, 0);
     }
     __syncwarp();
   } else {

@@ -306,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every MMA issued above has completed before TMEM is read for the last time or released
       tc::commit(fin);
-      if (!wait_bar(fin, 0, abort)) *abort = 1;
+      // waited for also after an abort (bounded): no MMA may be in flight when TMEM is released
+      if (!mbar_wait(fin, 0)) *abort = 1;
     }
     __syncwarp();
   } else {
@@ -512,6 +513,16 @@ __device__ __forceinline__ bool wait_c(uint64_t* bar, uint32_t parity, volatile 
 // Same with the default (CTA-scope) acquire, for the many threads that poll barriers completed by
 // tcgen05.commit or by this CTA's own cp.async: what they read next is TMEM or this CTA's shared
 // memory behind tcgen05 / proxy fences, so no cluster-scope acquire is needed on their hot path.
+// Bounded wait that does not stop for the abort flag: the issuing thread drains the pair's MMAs
+// before either CTA releases TMEM, also after an abort.
+__device__ __forceinline__ bool drain_c(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (try_wait_cluster(addr, parity)) return true;
+    if ((it & 63u) == 63u && global_ns() - t0 > kSpinLimitNs) return false;
+  }
+}
 __device__ __forceinline__ bool wait_l(uint64_t* bar, uint32_t parity, volatile int* abort,
                                        uint32_t peer_abort, unsigned backoff_ns = 0) {
   const uint32_t addr = smem_u32(bar);
@@ -823,7 +834,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         remote_arrive(peer_addr(smem_u32(&full[slot]), 0));
         if (++slot == C::kSlots) { slot = 0; phase ^= 1u; }
       }
-      wait_l(fin, 0, abort, peer_abort);  // rank 0's MMAs done with this CTA's TMEM and smem
+      // rank 0's MMAs done with this CTA's TMEM and smem; waited for also after an abort (bounded)
+      mbar_wait(fin, 0);
     }
     __syncwarp();
   } else if (warp == kFwdWarp) {
@@ -892,7 +904,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       }
       if (!ok) commit_both(q_dead);  // aborted before the last S: release the waiters anyway
       commit_both(fin);  // completes once every MMA issued above has completed
-      wait_c(fin, 0, abort, peer_abort);
+      // waited for also after an abort (bounded): no MMA may be in flight when TMEM is released
+      drain_c(fin, 0);
     }
     __syncwarp();
   } else if (warp < kSmWarps) {
