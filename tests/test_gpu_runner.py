@@ -168,3 +168,54 @@ def test_captured_decode_step_matches_eager():
         assert torch.equal(go, eo) and torch.equal(gy, ey)
         for k in pools:
             assert torch.equal(graph_pools[k], eager_pools[k]), k
+
+
+def test_pipelined_decode_step_matches_eager():
+    """PipelinedStep: every submit's host output equals the eager step on the same inputs, with
+    the steps' in-place pool updates applied in submission order."""
+    from tokenfactory_b200 import ops
+    from tokenfactory_b200.runner import PipelinedStep
+    g = torch.Generator(device="cuda").manual_seed(12)
+    B, S, Hq, Hkv, D, maxL = 20, 12000, 8, 2, 128, 500
+    bf = torch.bfloat16
+    pools = dict(kb=torch.randn((S, Hkv, D), generator=g, device="cuda", dtype=bf),
+                 vb=torch.randn((S, Hkv, D), generator=g, device="cuda", dtype=bf))
+    # distinct slots, as the allocator hands them out: two tokens of one step never share a slot
+    r2t = (torch.randperm(S - 1, generator=g, device="cuda")[:B * maxL] + 1).view(B, maxL)
+
+    def inputs():
+        d = dict(q=torch.randn((B, Hq, D), generator=g, device="cuda", dtype=bf),
+                 gate=torch.randn((B, Hq, D), generator=g, device="cuda", dtype=bf),
+                 k=torch.randn((B, Hkv, D), generator=g, device="cuda", dtype=bf),
+                 v=torch.randn((B, Hkv, D), generator=g, device="cuda", dtype=bf),
+                 # a few slots of each step lie in the windows later steps read
+                 loc=r2t[torch.arange(B, device="cuda"), torch.randint(0, 50, (B,), generator=g,
+                                                                        device="cuda")],
+                 rpi=torch.randperm(B, generator=g, device="cuda"),
+                 lens=torch.randint(1, maxL + 1, (B,), generator=g, device="cuda"))
+        return {k: v.cpu().pin_memory() for k, v in d.items()}
+
+    def step(P, q, gate, k, v, loc, rpi, lens):
+        ops.kv_store(P["kb"], P["vb"], loc, k, v)
+        o = ops.paged_decode(q, P["kb"], P["vb"], r2t, rpi, lens, D ** -0.5, maxL, gate=gate,
+                             gate_mode="sigmoid")
+        return o, o.float().sum(dim=-1)
+
+    pipe_pools = {k: v.clone() for k, v in pools.items()}
+    pipe = PipelinedStep(lambda **kw: step(pipe_pools, **kw), inputs())
+    eager_pools = {k: v.clone() for k, v in pipe_pools.items()}  # state after the warm-up runs
+    steps = [inputs() for _ in range(6)]
+    pending = []
+    for i, inp in enumerate(steps):
+        pending.append((pipe.submit(**inp), step(eager_pools, **{k: v.cuda() for k, v in inp.items()})))
+        if len(pending) == 2:  # a buffer set's host outputs are read before it is submitted again
+            res, (eo, es) = pending.pop(0)
+            po, ps = res.wait()
+            assert torch.equal(po, eo.cpu()) and torch.equal(ps, es.cpu())
+    res, (eo, es) = pending.pop(0)
+    po, ps = res.wait()
+    assert torch.equal(po, eo.cpu()) and torch.equal(ps, es.cpu())
+    pipe.join()
+    torch.cuda.synchronize()
+    for k in pools:
+        assert torch.equal(pipe_pools[k], eager_pools[k]), k

@@ -13,6 +13,8 @@ softmax + multinomial and one ``.item()`` per request (``_sample``, :574-581).  
 * ``sample``: every row in one tf_sample_tokens launch and one device->host copy;
 * ``ModelRunnerHotPath``: mixin overriding ``_prepare_forward_batch`` and ``_sample`` with the
   reference's signatures; ``install()`` patches ``engine.model_runner.ModelRunner``.
+* ``CapturedStep`` / ``PipelinedStep``: a step replayed as a CUDA graph with new inputs; the
+  pipelined form overlaps each step's host<->device copies with its neighbours' kernels.
 """
 
 import importlib
@@ -241,3 +243,97 @@ class CapturedStep:
             dst.copy_(v, non_blocking=True)
         self.graph.replay()
         return self.outputs
+
+
+class PipelinedResult:
+    """The host outputs of one PipelinedStep.submit: valid once `wait()` returns, until the
+    same buffer set is submitted again (`depth` submits later)."""
+
+    def __init__(self, host: Tuple[torch.Tensor, ...], copied_out: torch.cuda.Event,
+                 copied_in: torch.cuda.Event):
+        self.host = host
+        self.copied_out = copied_out
+        self.inputs_consumed = copied_in  # the host inputs may be overwritten once this completes
+
+    def wait(self):
+        self.copied_out.synchronize()
+        return self.host[0] if len(self.host) == 1 else self.host
+
+
+class _Slot:
+    def __init__(self, cap: CapturedStep):
+        self.cap = cap
+        outs = cap.outputs if isinstance(cap.outputs, tuple) else (cap.outputs,)
+        self.outs = outs
+        self.host = tuple(torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs)
+        self.copied_in = torch.cuda.Event()
+        self.computed = torch.cuda.Event()
+        self.copied_out = torch.cuda.Event()
+        self.used = False
+
+
+class PipelinedStep:
+    """A captured step streamed over `depth` buffer sets so that host<->device copies overlap
+    the kernels of the neighbouring steps.
+
+    Each buffer set holds device copies of the inputs, a CUDA graph of ``fn`` captured over them
+    (a CapturedStep) and pinned host copies of its outputs.  ``submit(**host_inputs)`` (pinned
+    host tensors of the example shapes):
+
+    * copy-in stream: waits until the set's previous step has finished its kernels, then copies
+      the inputs in;
+    * the caller's current stream: waits for those copies (and for the set's previous outputs to
+      have left the device), replays the set's graph;
+    * copy-out stream: waits for the graph, copies the outputs to the set's pinned host tensors.
+
+    So step i+1's inputs travel while step i computes, and step i's outputs while step i+1
+    computes.  The graphs replay in submission order on one stream, so state that ``fn`` updates
+    in place (KV pool, recurrent state) sees the steps in order, as with CapturedStep.
+    ``fence()`` orders later copies after work already issued on the current stream; ``join()``
+    makes the current stream wait for every copy issued so far."""
+
+    def __init__(self, fn, example_inputs: Dict[str, torch.Tensor], depth: int = 2,
+                 warmup: int = 2):
+        if depth < 2:
+            raise ValueError("depth must be at least 2")
+        self.slots = [_Slot(CapturedStep(fn, example_inputs, warmup=warmup)) for _ in range(depth)]
+        self.copy_in = torch.cuda.Stream()
+        self.copy_out = torch.cuda.Stream()
+        self.n = 0
+
+    def fence(self):
+        cur = torch.cuda.current_stream()
+        self.copy_in.wait_stream(cur)
+        self.copy_out.wait_stream(cur)
+
+    def join(self):
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self.copy_in)
+        cur.wait_stream(self.copy_out)
+
+    def submit(self, **host_inputs) -> PipelinedResult:
+        slot = self.slots[self.n % len(self.slots)]
+        self.n += 1
+        compute = torch.cuda.current_stream()
+        static = slot.cap.static
+        for k, v in host_inputs.items():
+            if v.shape != static[k].shape:
+                raise ValueError(f"{k}: shape {tuple(v.shape)} != captured {tuple(static[k].shape)}")
+        if slot.used:
+            self.copy_in.wait_event(slot.computed)  # the previous step read these inputs
+        with torch.cuda.stream(self.copy_in):
+            for k, v in host_inputs.items():
+                static[k].copy_(v, non_blocking=True)
+            slot.copied_in.record(self.copy_in)
+        compute.wait_event(slot.copied_in)
+        if slot.used:
+            compute.wait_event(slot.copied_out)  # the previous outputs have left the device
+        slot.cap.graph.replay()
+        slot.computed.record(compute)
+        self.copy_out.wait_event(slot.computed)
+        with torch.cuda.stream(self.copy_out):
+            for h, d in zip(slot.host, slot.outs):
+                h.copy_(d, non_blocking=True)
+            slot.copied_out.record(self.copy_out)
+        slot.used = True
+        return PipelinedResult(slot.host, slot.copied_out, slot.copied_in)
