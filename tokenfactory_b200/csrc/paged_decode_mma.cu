@@ -248,6 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<D>;
   constexpr int NB = C::kBlocks;
   extern __shared__ __align__(128) unsigned char smem[];
+  // The combine kernel may be launched once every CTA of this grid has started (all are resident:
+  // one per SM); its CTAs take an SM only when a CTA here has exited, and wait for this grid's
+  // completion before they read its partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem);             // [8][kQStride]
   float* o_s = reinterpret_cast<float*>(smem + C::kQBytes);                  // [8 warps][8][kOStride]
   float* m_s = o_s + kWarps * kHeads * C::kOStride;                          // [8][8]
@@ -527,6 +531,9 @@ __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws w
     const int64_t rc = cta_range(cc, total, nctas);
     sl[i] = 2 * cc + ((su > rc ? su : rc) == rc ? 0 : 1);
   }
+  // everything above reads only the plan; the decode grid's partials are complete and visible
+  // after this wait (a no-op when the launch has no programmatic dependency)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   for (int e = tid; e < np * G; e += blockDim.x) {  // every piece's (max, sum) at once
     const int i = e / G, hd = e - (e / G) * G;
@@ -603,7 +610,20 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, c
   if (csmem > 227 * 1024) return cudaErrorInvalidValue;
   e = cudaFuncSetAttribute(combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
   if (e != cudaSuccess) return e;
-  combine_kernel<D><<<nctas, 256, csmem, s>>>(a, ws, nctas);
+  // programmatic dependent launch: the combine's CTAs are scheduled as the decode's CTAs exit and
+  // do their schedule search while the last decode CTAs still run
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)nctas);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = csmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, combine_kernel<D>, a, ws, nctas);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
