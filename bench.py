@@ -556,12 +556,18 @@ C4 = dict(B=16, Pmax=4096, Emin=512, Emax=2048, Hq=32, Hkv=4, D=256, Hk=16, Hv=4
           dv=128, K=4, slots=1_200_000)
 
 
-def _peak_tflops():
+def _peak_tflops(timed_region_s: float = 0.0):
+    """bf16 dense peak: the burst figure for a kernel timed in a short region, the sustained one
+    (the GPU settles at its power cap within about a second of dense tensor work) when the timed
+    region of back-to-back launches lasts longer than that."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured"
-    return 1590.0, "fallback"
+            peaks = json.load(f)
+        if timed_region_s > 1.0 and "bf16_tflops_sustained" in peaks:
+            return float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
+        return float(peaks["bf16_tflops"]), "measured (burst)"
+    return (1400.0, "fallback (sustained)") if timed_region_s > 1.0 else (1590.0, "fallback (burst)")
 
 
 def bench_extend(args, rank, world, dev):
@@ -681,7 +687,7 @@ def bench_extend(args, rank, world, dev):
     Pf, Ef = P.double(), E.double()
     flops = float((4 * C4["Hq"] * D * (Ef * Pf + Ef * (Ef + 1) / 2)).sum())  # whole job
     gdn_flops_tok = C4["Hv"] * (6 * dk * dv + 3 * 64 * dv) + C4["Hk"] * 4 * 64 * dk
-    peak, peak_kind = _peak_tflops()
+    peak, peak_kind = _peak_tflops(attn_s * args.steps)
     tflops = flops / attn_s / 1e12
     per_gpu = tflops / world
     return {
@@ -777,9 +783,9 @@ def bench_fp8(args, rank, world, dev):
                         "tflops_gemm": flops / gemm / 1e12, "tflops_linear": flops / full / 1e12,
                         "weight_gb_per_s_gemm": N * K / gemm / 1e9,
                         "torch_scaled_mm_loop_ms": ref_s * 1e3}
-    bf16_peak, peak_kind = _peak_tflops()
-    fp8_peak = 2 * bf16_peak
     pre = res["prefill"]
+    bf16_peak, peak_kind = _peak_tflops(pre["ms_gemm"] / 1e3 * args.steps)
+    fp8_peak = 2 * bf16_peak
     return {
         "metric": "block-FP8 linear TFLOP/s (27B MLP up projection 5120 -> 17408, 128x128 block scales)",
         "value": pre["tflops_gemm"] * world, "unit": "TFLOP/s", "n_gpus": world,
