@@ -105,3 +105,10 @@ def test_no_cpu_fallback():
         runner.prepare_forward_batch([req], [[-1] * 16] * 4, r2t, [0] * 4)
     with pytest.raises(ValueError, match="CUDA"):
         ops.sample_tokens(torch.zeros(2, 8), torch.zeros(2))
+
+
+def test_pipelined_step_needs_two_buffer_sets():
+    """A single buffer set could not overlap one step's copies with another step's kernels."""
+    from tokenfactory_b200.runner import PipelinedStep
+    with pytest.raises(ValueError, match="depth"):
+        PipelinedStep(lambda **kw: None, {}, depth=1)
