@@ -95,6 +95,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the decode grid may be launched now: its CTAs wait for this grid before reading the plan
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) carry = 0;
   __syncthreads();
   for (int b0 = 0; b0 < B; b0 += 1024) {
@@ -248,9 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<D>;
   constexpr int NB = C::kBlocks;
   extern __shared__ __align__(128) unsigned char smem[];
-  // The combine kernel may be launched once every CTA of this grid has started (all are resident:
-  // one per SM); its CTAs take an SM only when a CTA here has exited, and wait for this grid's
-  // completion before they read its partials.
+  // This grid is a programmatic dependent of the plan kernel: the plan (and, through stream order,
+  // every earlier launch such as the KV store) is complete and visible after this wait.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The combine kernel may be launched once every CTA of this grid has passed the wait above (all
+  // are resident: one per SM), so it may read the plan at once; its CTAs take an SM only when a
+  // CTA here has exited, and wait for this grid's completion before they read its partials.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem);             // [8][kQStride]
   float* o_s = reinterpret_cast<float*>(smem + C::kQBytes);                  // [8 warps][8][kOStride]
@@ -603,7 +608,19 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, c
                                        (int)Cfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, a.r2t_cols, ws.tile_start);
-  decode_kernel<D><<<nctas, kThreads, Cfg<D>::kSmem, s>>>(a, ws, nctas);
+  // the decode CTAs are scheduled while the plan runs and wait for it before their first read
+  cudaLaunchAttribute dep[1];
+  dep[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  dep[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t dcfg = {};
+  dcfg.gridDim = dim3((unsigned)nctas);
+  dcfg.blockDim = dim3(kThreads);
+  dcfg.dynamicSmemBytes = Cfg<D>::kSmem;
+  dcfg.stream = s;
+  dcfg.attrs = dep;
+  dcfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&dcfg, decode_kernel<D>, a, ws, nctas);
+  if (e != cudaSuccess) return e;
   // a unit spans at most every CTA: weights [nctas][kHeads], (max, sum) [nctas][kHeads][2] and
   // slot ids [nctas], then the schedule tile_start[B+1]
   const size_t csmem = (size_t)nctas * (3 * kHeads * 4 + 4) + (size_t)(a.batch_size + 1) * 4;
