@@ -179,18 +179,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def _profile_traffic(name: str):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name> (or None)."""
-    p = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(p):
-        return None
-    for line in open(p):
-        if line.strip().startswith("dram_bytes_per_launch_full_size:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
-    return None
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each leg's dominant kernel, from an
+# ncu capture of exactly that leg's default workload on one GPU (the commands and the figures are
+# in profiles/).  A run with other sizes or more GPUs reports null: its traffic was not measured.
+NCU_TRAFFIC_N1 = {"decode": 2_297_680_000, "gdn_decode": 1_593_400_000, "extend": 1_199_900_000}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -379,13 +371,17 @@ def bench_decode(args, rank, world, dev):
 
     rt = _step_runtime(B, dev, stream)
 
-    traffic = _profile_traffic("paged_decode_config2.md")
+    default_size = (B, C2["slots"]) == (128, 1_200_000)
+    traffic = NCU_TRAFFIC_N1["decode"] if world == 1 and default_size else None
     res = {
         "metric": METRIC, "value": B * args.steps / elapsed, "unit": "tok/s",
+        "value_per_gpu": B * args.steps / elapsed / world,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "config2 paged GQA decode (one full-attention layer step)",
+                   "value": "whole-job tokens/s over all GPUs (each rank decodes every request "
+                            "for its heads); value_per_gpu = value / n_gpus",
                    "batch": B, "q_heads": C2["Hq"], "kv_heads": C2["Hkv"], "head_dim": D,
                    "seq_len": f"U[{C2['Lmin']},{C2['Lmax']}]", "sum_seq_len": int(inp["lens"].sum()),
                    "pool_slots": C2["slots"], "page_size": 1, "gate": "sigmoid",
@@ -543,7 +539,7 @@ def bench_gdn_decode(args, rank, world, dev):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_kind": peak_kind,
                      "kernel": "tf_gdn_decode", "bytes_per_launch": nbytes,
-                     "traffic": _profile_traffic("gdn_decode_config3.md")},
+                     "traffic": NCU_TRAFFIC_N1["gdn_decode"] if world == 1 else None},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
@@ -684,6 +680,10 @@ def bench_extend(args, rank, world, dev):
         snap_s = timed(snap_step, args.steps)
         snap_torch_s = timed(snap_step_torch, max(1, args.steps // 4))
     pro_bytes = 2 * T * (hq + 2 * hkv) * D * 2 + 2 * T * 8
+    # GDN extend algorithmic bytes (this rank's heads): qkv in, z in, out, the recurrent states
+    # read and written once, conv states read and written, a and b
+    gdn_bytes = (T * conv_dim * 2 + 2 * T * hv * dv * 2 + B * hv * dk * dv * 4 * 2 +
+                 B * conv_dim * (K - 1) * 2 * 2 + 2 * T * hv * 2)
     Pf, Ef = P.double(), E.double()
     flops = float((4 * C4["Hq"] * D * (Ef * Pf + Ef * (Ef + 1) / 2)).sum())  # whole job
     gdn_flops_tok = C4["Hv"] * (6 * dk * dv + 3 * 64 * dv) + C4["Hk"] * 4 * 64 * dk
@@ -705,9 +705,18 @@ def bench_extend(args, rank, world, dev):
         "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                      "frac": per_gpu / peak, "peak_kind": peak_kind,
                      "kernel": "tf_paged_extend_attn (tcgen05)", "flops_per_launch": flops / world,
-                     "traffic": _profile_traffic("paged_extend_config4.md")},
+                     "traffic": NCU_TRAFFIC_N1["extend"] if world == 1 and B == C4["B"] and
+                     S == C4["slots"] else None},
         "gdn_extend": {"tok_per_s": T / gdn_s, "ms_per_step": gdn_s * 1e3,
                        "tflops_min_count": T * gdn_flops_tok / gdn_s / 1e12,
+                       "tflops_frac_of_peak": T * gdn_flops_tok / world / gdn_s / 1e12 / peak,
+                       "roofline": {"bound": "hbm", "achieved": gdn_bytes / gdn_s / 1e9,
+                                    "peak": _peaks()[0], "unit": "GB/s",
+                                    "frac": gdn_bytes / gdn_s / 1e9 / _peaks()[0],
+                                    "peak_kind": _peaks()[1], "bytes_per_launch": gdn_bytes,
+                                    "why": "the minimal FLOP count takes T*6.42 MFLOP / peak, "
+                                           "less time than streaming qkv, z, out and the states "
+                                           "once; HBM binds"},
                        "kernel": "tf_gdn_extend (varlen conv + chunked WY delta rule, C=64, tcgen05 with bf16x3 split products, fp32 state)"},
         "prologue": {"gb_per_s": pro_bytes / pro_s / 1e9, "ms_per_step": pro_s * 1e3,
                      "frac_of_hbm_peak": pro_bytes / pro_s / 1e9 / _peaks()[0], "peak_kind": _peaks()[1],
@@ -884,6 +893,8 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": "config2 paged GQA decode (one full-attention layer step)",
+                   "value": "whole-job tokens/s over all GPUs (each rank decodes every request "
+                            "for its heads); value_per_gpu = value / n_gpus",
                    "batch": C2["B"], "q_heads": C2["Hq"], "kv_heads": C2["Hkv"],
                    "head_dim": C2["D"], "seq_len": f"U[{C2['Lmin']},{C2['Lmax']}]",
                    "parallelism": "cpu"},
@@ -911,6 +922,8 @@ def main():
                     help="config 4: KV pool slots")
     ap.add_argument("--no-e2e", action="store_true",
                     help="profiling only: device-timed leg alone, short output")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="config 2 without the config 3 / config 4 legs that the default line carries")
     args = ap.parse_args()
     C2["B"], C2["slots"] = args.batch, args.pool_slots
     args.warmup = max(3, args.warmup)
@@ -929,6 +942,19 @@ def main():
     dev = torch.device("cuda", torch.cuda.current_device())
     res = {2: bench_decode, 3: bench_gdn_decode, 4: bench_extend,
            6: bench_fp8}[args.config](args, rank, world, dev)
+    if args.config == 2 and not args.no_e2e and not args.decode_only:
+        # the rest of the metric in the same line: config 3 (GDN decode) and config 4 (extend
+        # attention TFLOP/s, GDN extend), each timed on its own with CUDA events and clocks
+        torch.cuda.empty_cache()
+        g = bench_gdn_decode(args, rank, world, dev)
+        res["gdn_decode"] = {k: g[k] for k in ("metric", "value", "unit", "ms_per_step", "config",
+                                               "roofline", "clocks")}
+        torch.cuda.empty_cache()
+        e = bench_extend(args, rank, world, dev)
+        res["extend"] = {k: e[k] for k in ("value", "unit", "ms_per_step", "config", "roofline",
+                                           "gdn_extend", "prologue", "state_snapshot", "clocks")}
+        res["extend"]["metric"] = "extend attn TFLOP/s (config 4, whole job)"
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and args.config == 2 and not args.no_e2e and \
             args.cpu_baseline_seconds > 0:
         threads = os.cpu_count() or 1

@@ -177,7 +177,9 @@ typedef struct tf_paged_attn_args {
 } tf_paged_attn_args;
 
 /* a2: pure decode batch (every extend_len == 1; qwen3_8/full_attention.py:215-242).  Split-KV with
- * a balanced schedule over all SMs; `workspace` holds the schedule and the split partials. */
+ * a balanced schedule over all SMs; `workspace` holds the schedule and the split partials.  Batches
+ * of more than 32768 requests (and dtypes / head dims the tensor-core kernel does not cover) take a
+ * CUDA-core kernel that needs no workspace (the size function returns 0 for them). */
 TF_API size_t tf_paged_decode_workspace_size(const tf_paged_attn_args* args);
 TF_API tf_status tf_paged_decode_attn(const tf_paged_attn_args* args, void* workspace,
                                size_t workspace_bytes, void* stream);
@@ -186,12 +188,13 @@ TF_API tf_status tf_paged_decode_attn(const tf_paged_attn_args* args, void* work
  * cannot allocate device memory (a host runtime binding this ABI through a plain FFI with no CUDA
  * allocator, or a process whose device memory is all reserved by its own pool).  Same kernels and
  * results as tf_paged_decode_attn; the scratch is a fixed 4 MiB device array inside the library
- * that every GPU loading the library holds until exit.  Batches whose scratch would exceed it are
- * rejected with TF_ERR_WORKSPACE (for head_dim 256 on 148 SMs, 2.4 MiB of partials plus
- * 4 bytes per request: about 400K requests).  The first call on a device resolves the array's
- * device address (make it before any stream capture).  Calls share the array and it keeps the
- * last call's contents, so calls whose kernels overlap on one GPU race and must be serialised.
- * Allocates nothing (no cudaMalloc, cudaFree or allocating library call). */
+ * that every GPU loading the library holds until exit.  Batches of more than 32768 requests are
+ * rejected with TF_ERR_WORKSPACE before anything is launched (at head_dim 256 on 148 SMs such a
+ * batch needs 2.6 MiB of the array).  The first call on a device resolves the array's device
+ * address and must come before any stream capture; a capture that would need it is refused with
+ * TF_ERR_CUDA.  While capturing, the stream must belong to the current device.  Calls share the
+ * array and it keeps the last call's contents, so calls whose kernels overlap on one GPU race and
+ * must be serialised.  Allocates nothing (no cudaMalloc, cudaFree or allocating library call). */
 TF_API tf_status tf_paged_decode_attn_noalloc(const tf_paged_attn_args* args, void* stream);
 
 /* a3: extend / mixed batch over a radix-cached prefix (qwen3_8/full_attention.py:179-213 for one

@@ -118,6 +118,39 @@ def test_decode_random_shapes_vs_oracle(shape):
     assert_close(out, want, "bf16", what=f"decode {shape}")
 
 
+def test_decode_batch_beyond_the_tensor_core_schedule():
+    """A decode batch of 60,000 requests is above the tensor-core kernel's schedule bound (its
+    combine keeps one int32 per request in shared memory): the workspace size is 0 and the call
+    runs the CUDA-core kernel, checked against a vectorised fp32 torch evaluation of the
+    reference's batched decode (qwen3_8/full_attention.py:215-242)."""
+    from tokenfactory_b200 import _capi, ops
+    B, hq, hkv, d, lmax = 60_000, 8, 1, 64, 4
+    g = torch.Generator(device="cuda").manual_seed(60)
+    lens = torch.randint(1, lmax + 1, (B,), generator=g, device="cuda")
+    slots = B * lmax + 1
+    r2t = (torch.randperm(slots - 1, generator=g, device="cuda") + 1)[:B * lmax].view(B, lmax)
+    r2t = torch.where(torch.arange(lmax, device="cuda")[None] < lens[:, None], r2t, -1)
+    kb = torch.randn((slots, hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    vb = torch.randn((slots, hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn((B, hq, d), generator=g, device="cuda").to(torch.bfloat16)
+    rpi = torch.arange(B, device="cuda")
+    args, keep = ops._paged_args(q, kb, vb, r2t, rpi, lens, None, d ** -0.5, None, "none",
+                                 q, lmax, 1, "clamp", None)
+    import ctypes
+    assert _capi.load().tf_paged_decode_workspace_size(ctypes.byref(args)) == 0
+    del keep
+    out = ops.paged_decode(q, kb, vb, r2t, rpi, lens, d ** -0.5, lmax)
+    idx = r2t.clamp(min=0)
+    k = kb[idx][:, :, 0].float()                      # [B, L, D] (one kv head)
+    v = vb[idx][:, :, 0].float()
+    s = torch.einsum("bhd,bld->bhl", q.float(), k) * d ** -0.5
+    s = s.masked_fill(torch.arange(lmax, device="cuda")[None, None] >= lens[:, None, None],
+                      float("-inf"))
+    want = torch.einsum("bhl,bld->bhd", torch.softmax(s, -1), v)
+    torch.cuda.synchronize()
+    assert_close(values(out, "bf16"), want.cpu().numpy(), "bf16", what="decode B=60000")
+
+
 def test_decode_request_without_keys_gives_nan_rows():
     """A request with no keys (seq_len 0) among others: its output rows are NaN, as the
     reference's softmax over an empty row, and the other rows match the batch where it has keys
@@ -243,3 +276,40 @@ def test_extend_random_shapes_vs_oracle(shape):
     want = OA.output_gate(BF.round_f32(orc).reshape(t, -1), inp["gate"].reshape(t, -1),
                           "sigmoid", "bf16")
     assert_close(out, want, "bf16", what=f"extend {shape}")
+
+
+@pytest.mark.parametrize("growing", [False, True])
+def test_extend_at_config4_lengths_vs_oracle(growing):
+    """Config 4's longest requests: a prefix of 4096 with an extend of 2048 (up to 6144 keys and
+    16 query tiles of 128 rows at G = 8) next to (3000, 1500), on the SM-pair tcgen05 kernel at
+    head_dim 256, against the oracle at the plain bf16 bound.  growing=True scales each key row by
+    1 + position / 600 so that a query row's running max keeps rising along the 48 key tiles:
+    the kernel's lazy O rescale (taken when the row max grows by more than 2^8) then fires many
+    times per row.  That case runs without the output gate: its softmax is so peaked that the
+    attention output sits near single V values of up to ~4, where the reference's second
+    rounding (after the gate) can land an element that crossed 4 before gating two bf16 steps
+    away; the ungated output has one rounding and meets the plain bound."""
+    hq, hkv, d = 8, 1, 256
+    reqs = [(4096, 2048), (3000, 1500)]
+    seq = [p + e for p, e in reqs]
+    ext = [e for _, e in reqs]
+    B = len(reqs)
+    spec = dict(dtype="bf16", hq=hq, hkv=hkv, d=d, seq=seq, ext=ext, req=[1, 0],
+                slots=sum(seq) + 11, rows=B + 1, cols=max(seq) + 5, seed=4096 + int(growing))
+    inp = C.attn_inputs(spec)
+    if growing:
+        pos = np.zeros(spec["slots"], np.float32)
+        for b, r in enumerate(spec["req"]):
+            sl = inp["req_to_token"][r, :seq[b]]
+            pos[sl[sl >= 0]] = np.arange(seq[b])[sl >= 0]
+        kf = BF.as_f32(inp["k_buf"], "bf16") * (1.0 + pos / 600.0)[:, None, None]
+        inp["k_buf"] = BF.from_f32(kf.astype(np.float32))
+    mode = "none" if growing else "sigmoid"
+    out = values(_run(inp, spec, gate_mode=mode), "bf16").reshape(sum(ext), -1)
+    orc = OA.slot_based_attention(inp["q"], inp["k_buf"], inp["v_buf"], inp["req_to_token"],
+                                  inp["req_pool_indices"], inp["seq_lens"], inp["extend_lens"],
+                                  d ** -0.5, "bf16")
+    t = orc.shape[0]
+    want = orc.reshape(t, -1) if growing else OA.output_gate(
+        BF.round_f32(orc).reshape(t, -1), inp["gate"].reshape(t, -1), "sigmoid", "bf16")
+    assert_close(out, want, "bf16", what=f"extend config-4 lengths growing={growing}")

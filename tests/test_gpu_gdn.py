@@ -194,6 +194,44 @@ def test_extend_random_27b_heads_vs_oracle(ext):
     np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
 
 
+def test_extend_config4_lengths_from_cached_state():
+    """Config 4's longest GDN extend: a 2048-token request and a 1500-token one at the 27B head
+    shapes (dk = dv = 128, GVA 3:1) from non-zero cached conv and recurrent states, on the
+    tcgen05 chunk kernel.  The raw (un-normed) outputs are held to the plain bf16 bound
+    (max-abs 2e-2, mean-abs 2e-3); the gated outputs, which the reference rounds twice, to two
+    bf16 steps; the final states to the extend bound."""
+    ext = [2048, 1500]
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext, req=[2, 0], slots=3,
+                seed=2048)
+    inp = C.gdn_inputs(spec)
+    assert np.abs(inp["ssm_state"]).max() > 0 and np.abs(BF.to_f32(inp["conv_state"])).max() > 0
+    t_raw, t_gated = _tensors(inp, "bf16"), _tensors(inp, "bf16")
+    raw = values(_run(spec, t_raw, False), "bf16")
+    gated = values(_run(spec, t_gated, True), "bf16")
+    orc_raw, cs, ss = _oracle(spec, inp, False)
+    orc_gated, _, _ = _oracle(spec, inp, True)
+    assert_close(raw, orc_raw, "bf16", what="extend 2048 + 1500, raw outputs")
+    assert_close(gated, orc_gated, "bf16", what="extend 2048 + 1500, gated", bf16_steps=2)
+    for t in (t_raw, t_gated):
+        np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
+        np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
+
+
+def test_extend_180_ctas_raw_outputs_at_the_plain_bound():
+    """The un-normed outputs of the 180-CTA batch (test_extend_more_ctas_than_sms_vs_oracle) at
+    the plain bf16 bound, beside the gated ones there."""
+    ext = np.random.default_rng(1180).integers(1, 201, 30).tolist()
+    req = np.random.default_rng(1181).permutation(34)[:30].tolist()
+    spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext, req=req, slots=34,
+                seed=1182)
+    inp = C.gdn_inputs(spec)
+    t = _tensors(inp, "bf16")
+    out = values(_run(spec, t, False), "bf16")
+    orc, cs, ss = _oracle(spec, inp, False)
+    assert_close(out, orc, "bf16", what="extend, 180 CTAs, raw outputs")
+    np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
+
+
 def test_gated_rmsnorm_standalone():
     from tokenfactory_b200 import ops
     rng = np.random.default_rng(3)

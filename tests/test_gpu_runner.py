@@ -202,8 +202,13 @@ def test_pipelined_decode_step_matches_eager():
         return o, o.float().sum(dim=-1)
 
     pipe_pools = {k: v.clone() for k, v in pools.items()}
-    pipe = PipelinedStep(lambda **kw: step(pipe_pools, **kw), inputs())
-    eager_pools = {k: v.clone() for k, v in pipe_pools.items()}  # state after the warm-up runs
+    eager_pools = {k: v.clone() for k, v in pipe_pools.items()}
+    # the pools are in-place state: construction's warm-up runs must leave them as they were
+    pipe = PipelinedStep(lambda **kw: step(pipe_pools, **kw), inputs(),
+                         state=list(pipe_pools.values()))
+    torch.cuda.synchronize()
+    for k in pools:
+        assert torch.equal(pipe_pools[k], eager_pools[k]), f"{k} changed by construction"
     steps = [inputs() for _ in range(6)]
     pending = []
     for i, inp in enumerate(steps):

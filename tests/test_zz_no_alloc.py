@@ -7,7 +7,8 @@ it takes the same inputs and outputs but keeps its scratch in a fixed array insi
 it needs no workspace.  This test calls it through the C ABI twice in a row, on two different
 batches (the second call finds the first call's leftovers in the shared scratch), and checks each
 result against the workspace entry point within the hot path's bf16 tolerance.  It also checks
-that a batch too large for the fixed scratch is refused with a clear error instead of running.
+that a batch too large for the fixed scratch is refused with a clear error instead of running, and
+that a call captured into a CUDA graph (after a first call outside capture) replays correctly.
 """
 
 import ctypes
@@ -59,12 +60,36 @@ def test_noalloc_decode_matches_workspace_entry_point_on_two_calls():
                      what=f"noalloc call {seed}")
 
 
+def test_noalloc_call_replays_inside_a_cuda_graph():
+    """After one call outside capture has resolved the scratch's device address, a call captured
+    into a CUDA graph replays with the same result as the workspace entry point."""
+    from tokenfactory_b200 import ops
+    spec, t = _batch(3, 17, 32, 4, 256, 4000)
+    want = ops.paged_decode(t["q"], t["k_buf"], t["v_buf"], t["req_to_token"],
+                            t["req_pool_indices"], t["seq_lens"], 256 ** -0.5, max(spec["seq"]),
+                            gate=t["gate"], gate_mode="sigmoid")
+    got = torch.full_like(want, float("nan"))
+    _noalloc(spec, t, got)  # outside capture: resolves the scratch address on this device
+    torch.cuda.synchronize()
+    got.fill_(float("nan"))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _noalloc(spec, t, got)
+    for _ in range(2):
+        got.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert_close(values(got, "bf16"), values(want, "bf16"), "bf16", what="noalloc replay")
+    del graph
+
+
 def test_noalloc_refuses_a_batch_beyond_its_fixed_scratch():
-    """The fixed scratch holds 4 MiB; a batch needing more is rejected before any launch."""
+    """The fixed scratch serves batches of up to 32768 requests; a batch of 60,000 is rejected
+    before any launch (the arguments below point at a tiny pool and are never read)."""
     from tokenfactory_b200 import _capi
     dummy = torch.zeros(64, dtype=torch.int64, device="cuda")
     pool = torch.zeros((4, 1, 256), dtype=torch.bfloat16, device="cuda")
-    big = 2_000_000
+    big = 60_000
     a = _capi.PagedAttnArgs(
         q=pool.data_ptr(), q_stride_tok=8 * 256, q_stride_head=256,
         k_buffer=pool.data_ptr(), v_buffer=pool.data_ptr(), kv_stride_slot=256,

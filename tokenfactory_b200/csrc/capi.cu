@@ -264,6 +264,12 @@ tf_status tf_paged_decode_attn_noalloc(const tf_paged_attn_args* a, void* stream
   tf_status st = check_paged(a, true);
   if (st != TF_OK || a->batch_size == 0) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // one stated bound for every dtype and head_dim, checked before anything is launched
+  if (a->batch_size > kDecodeMmaMaxBatch)
+    return fail(TF_ERR_WORKSPACE,
+                "tf_paged_decode_attn_noalloc: the built-in scratch serves batches of up to %d "
+                "requests, this one has %d; use tf_paged_decode_attn with a caller workspace",
+                kDecodeMmaMaxBatch, a->batch_size);
   DeviceGuard g(s);
   if (!g.ok()) return fail(TF_ERR_CUDA, "cannot select the stream's device");
   if (!paged_decode_mma_supported(*a)) {  // the CUDA-core path needs no scratch at all
@@ -275,11 +281,16 @@ tf_status tf_paged_decode_attn_noalloc(const tf_paged_attn_args* a, void* stream
   const size_t need = paged_decode_mma_workspace(*a, nsm);
   if (need > kNoAllocScratchBytes)
     return fail(TF_ERR_WORKSPACE,
-                "tf_paged_decode_attn_noalloc: this batch needs %zu bytes of scratch but the "
-                "built-in scratch holds %zu (batch_size %d, head_dim %d, %d SMs); use "
-                "tf_paged_decode_attn with a caller workspace",
-                need, kNoAllocScratchBytes, a->batch_size, a->head_dim, nsm);
-  return cuda_status(launch_paged_decode_mma_noalloc(*a, nsm, s), "tf_paged_decode_attn_noalloc");
+                "tf_paged_decode_attn_noalloc: the built-in scratch holds %zu bytes; this batch "
+                "(batch_size %d, head_dim %d, %d SMs) needs %zu; use tf_paged_decode_attn with a "
+                "caller workspace",
+                kNoAllocScratchBytes, a->batch_size, a->head_dim, nsm, need);
+  const cudaError_t e = launch_paged_decode_mma_noalloc(*a, nsm, s);
+  if (e == cudaErrorStreamCaptureUnsupported)
+    return fail(TF_ERR_CUDA,
+                "tf_paged_decode_attn_noalloc: the first call on a device must be made outside "
+                "stream capture (it resolves the device address of the built-in scratch)");
+  return cuda_status(e, "tf_paged_decode_attn_noalloc");
 }
 
 size_t tf_paged_extend_workspace_size(const tf_paged_attn_args* a) {

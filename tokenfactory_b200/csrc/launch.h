@@ -21,12 +21,17 @@ cudaError_t launch_paged_attn_simt(const tf_paged_attn_args& a, cudaStream_t s);
 bool paged_extend_tc_supported(const tf_paged_attn_args& a);
 cudaError_t launch_paged_extend_tc(const tf_paged_attn_args& a, cudaStream_t s);
 
-// paged_decode_mma.cu: bf16 / fp16 decode on tensor cores, balanced split-KV
+// paged_decode_mma.cu: bf16 / fp16 decode on tensor cores, balanced split-KV.  Its combine kernel
+// keeps the schedule (batch_size + 1 int32) in shared memory, so batches above kDecodeMmaMaxBatch
+// take the CUDA-core kernel instead (checked before any launch).
+constexpr int kDecodeMmaMaxBatch = 32768;
 bool paged_decode_mma_supported(const tf_paged_attn_args& a);
 size_t paged_decode_mma_workspace(const tf_paged_attn_args& a, int num_sms);
 cudaError_t launch_paged_decode_mma(const tf_paged_attn_args& a, void* ws, size_t ws_bytes,
                                     int num_sms, cudaStream_t s);
-// same kernels with the scratch in a fixed device array of kNoAllocScratchBytes (no allocation)
+// same kernels with the scratch in a fixed device array of kNoAllocScratchBytes (no allocation);
+// cudaErrorStreamCaptureUnsupported when the stream is capturing and the array's address on the
+// current device has not been resolved by an earlier call outside capture
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
 cudaError_t launch_paged_decode_mma_noalloc(const tf_paged_attn_args& a, int num_sms,
                                             cudaStream_t s);

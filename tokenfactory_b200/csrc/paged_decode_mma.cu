@@ -88,7 +88,7 @@ inline size_t ws_bytes(int B, int nctas, int D) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// plan: tile_start[b] = sum_{b'<b} ceil(seq_lens[b'] / 32)
+// plan: tile_start[b] = sum_{b'<b} ceil(seq_lens[b'] / kTileTok)
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int B,
                                                     int64_t max_len, int32_t* tile_start) {
@@ -604,8 +604,15 @@ __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws w
 template <int D>
 static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, cudaStream_t s) {
   Ws ws = carve(wsp, a.batch_size, nctas, D);
+  // a unit spans at most every CTA: the combine holds weights [nctas][kHeads], (max, sum)
+  // [nctas][kHeads][2] and slot ids [nctas], then the schedule tile_start[B+1]; checked before
+  // the first launch so that a batch it cannot hold leaves nothing enqueued
+  const size_t csmem = (size_t)nctas * (3 * kHeads * 4 + 4) + (size_t)(a.batch_size + 1) * 4;
+  if (csmem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<D>::kSmem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
   if (e != cudaSuccess) return e;
   plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, a.r2t_cols, ws.tile_start);
   // the decode CTAs are scheduled while the plan runs and wait for it before their first read
@@ -620,12 +627,6 @@ static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, c
   dcfg.attrs = dep;
   dcfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&dcfg, decode_kernel<D>, a, ws, nctas);
-  if (e != cudaSuccess) return e;
-  // a unit spans at most every CTA: weights [nctas][kHeads], (max, sum) [nctas][kHeads][2] and
-  // slot ids [nctas], then the schedule tile_start[B+1]
-  const size_t csmem = (size_t)nctas * (3 * kHeads * 4 + 4) + (size_t)(a.batch_size + 1) * 4;
-  if (csmem > 227 * 1024) return cudaErrorInvalidValue;
-  e = cudaFuncSetAttribute(combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
   if (e != cudaSuccess) return e;
   // programmatic dependent launch: the combine's CTAs are scheduled as the decode's CTAs exit and
   // do their schedule search while the last decode CTAs still run
@@ -651,6 +652,7 @@ bool paged_decode_mma_supported(const tf_paged_attn_args& a) {
   if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return false;
   const int G = a.num_q_heads / a.num_kv_heads;
   if (G < 1 || G > dec::kHeads) return false;
+  if (a.batch_size > kDecodeMmaMaxBatch) return false;
   auto al = [](const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
   if (!al(a.k_buffer, 16) || !al(a.v_buffer, 16)) return false;
   if ((a.kv_stride_slot * 2) % 16 != 0 || (a.kv_stride_head * 2) % 16 != 0) return false;
@@ -691,17 +693,24 @@ std::mutex g_scratch_mu;
 void* g_scratch_ptr[kScratchMaxDevices] = {};
 }  // namespace
 
-// Device address of g_decode_scratch on the current device.  In host code the array's name is a
+// Device address of g_decode_scratch on the stream's device.  In host code the array's name is a
 // host-side stand-in, never a device address, so it is resolved once per device (with that device
-// current) by cudaGetSymbolAddress; this first call per device should come before any stream
-// capture.
-static cudaError_t decode_scratch_ptr(void** out) {
+// current) by cudaGetSymbolAddress.  Outside capture the C ABI has made the stream's device
+// current.  While `s` is being captured the stream's device cannot be queried without breaking the
+// capture, so the capturing thread's current device is taken (a captured stream must belong to it)
+// and the address must already be known: the first call on a device has to come before any
+// capture, and a capture that would need the lookup is refused instead of resolving it mid-capture.
+static cudaError_t decode_scratch_ptr(cudaStream_t s, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kScratchMaxDevices) return cudaErrorInvalidDevice;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(s, &cap);
+  if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (g_scratch_ptr[dev] == nullptr) {
+    if (cap != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_decode_scratch);
     if (e != cudaSuccess) return e;
@@ -714,7 +723,7 @@ static cudaError_t decode_scratch_ptr(void** out) {
 cudaError_t launch_paged_decode_mma_noalloc(const tf_paged_attn_args& a, int num_sms,
                                             cudaStream_t s) {
   void* ws = nullptr;
-  cudaError_t e = decode_scratch_ptr(&ws);
+  cudaError_t e = decode_scratch_ptr(s, &ws);
   if (e != cudaSuccess) return e;
   // the status word keeps the previous call's error code: start every call from zero
   e = cudaMemsetAsync(ws, 0, 256, s);

@@ -217,10 +217,16 @@ class CapturedStep:
     device values; the decode's split plan is computed on the device from seq_lens, so a
     ``max_seq_len`` bound can be fixed at capture).  Inputs are copied into static buffers of the
     captured shapes (host tensors from pinned memory copy asynchronously), the graph is
-    replayed, and the static outputs are returned (overwritten by the next call)."""
+    replayed, and the static outputs are returned (overwritten by the next call).
+
+    Construction runs ``fn`` eagerly ``warmup`` times on the example inputs before capturing it
+    (lazy initialisation must not happen inside the capture).  Those runs update whatever ``fn``
+    updates in place - KV-pool rows, recurrent GDN states - exactly like real steps.  List such
+    tensors in ``state`` to have them saved before the warm-up and restored after it (one
+    temporary copy of each); otherwise the warm-up steps stay applied to them."""
 
     def __init__(self, fn, example_inputs: Dict[str, torch.Tensor], warmup: int = 2,
-                 pool=None):
+                 pool=None, state: Sequence[torch.Tensor] = ()):
         self.static = {k: torch.empty_like(v, device=v.device if v.is_cuda else "cuda")
                        for k, v in example_inputs.items()}
         for k, v in example_inputs.items():
@@ -228,9 +234,13 @@ class CapturedStep:
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
+            saved = [t.clone() for t in state] if warmup > 0 else []
             for _ in range(warmup):
                 fn(**self.static)
+            for t, c in zip(state, saved):
+                t.copy_(c)
         torch.cuda.current_stream().wait_stream(side)
+        del saved
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, pool=pool):
             self.outputs = fn(**self.static)
@@ -290,13 +300,18 @@ class PipelinedStep:
     computes.  The graphs replay in submission order on one stream, so state that ``fn`` updates
     in place (KV pool, recurrent state) sees the steps in order, as with CapturedStep.
     ``fence()`` orders later copies after work already issued on the current stream; ``join()``
-    makes the current stream wait for every copy issued so far."""
+    makes the current stream wait for every copy issued so far.
+
+    Construction runs ``fn`` eagerly ``warmup`` times (for the first buffer set only; the other
+    sets are captured without running it), with the same effect on in-place state as
+    CapturedStep: pass the tensors ``fn`` updates in place as ``state`` to have them restored."""
 
     def __init__(self, fn, example_inputs: Dict[str, torch.Tensor], depth: int = 2,
-                 warmup: int = 2):
+                 warmup: int = 2, state: Sequence[torch.Tensor] = ()):
         if depth < 2:
             raise ValueError("depth must be at least 2")
-        self.slots = [_Slot(CapturedStep(fn, example_inputs, warmup=warmup)) for _ in range(depth)]
+        self.slots = [_Slot(CapturedStep(fn, example_inputs, warmup=warmup if i == 0 else 0,
+                                         state=state)) for i in range(depth)]
         self.copy_in = torch.cuda.Stream()
         self.copy_out = torch.cuda.Stream()
         self.n = 0
