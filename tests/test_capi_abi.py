@@ -135,3 +135,25 @@ def test_state_slots_copy_checks_without_a_gpu():
     for empty in ({"num_ops": 0}, {"num_layers": 0}, {"conv_state": None, "ssm_state": None}):
         a = _capi.StateCopyArgs(**{**base, **empty})
         assert lib.tf_state_slots_copy(ctypes.byref(a), None) == _capi.TF_OK
+
+
+def test_torch_extension_loads_over_the_library_and_refuses_cpu_tensors():
+    """tokenfactory_b200._C (the PyTorch front end) imports without a GPU, is linked to the same
+    libtfattn.so, binds one function per ops entry point, and rejects CPU tensors before any
+    launch (no CPU fallback)."""
+    import torch
+    from tokenfactory_b200 import _C, _capi, ops
+    assert _C.ABI_VERSION == _capi.ABI_VERSION
+    for name in ("kv_store", "attn_prologue", "paged_decode", "paged_extend", "gdn_decode",
+                 "gdn_extend", "gated_rmsnorm", "state_slots_copy", "req_to_token_sync",
+                 "sample_tokens", "fp8_quantize", "fp8_block_gemm"):
+        assert callable(getattr(_C, name)), name
+        assert callable(getattr(ops, name)), name
+    maps = open(f"/proc/{os.getpid()}/maps").read()
+    assert os.path.realpath(_capi.LIB_PATH) in maps and os.path.realpath(_C.__file__) in maps
+    q = torch.zeros((2, 8, 64), dtype=torch.bfloat16)
+    i = torch.zeros(2, dtype=torch.int64)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.paged_decode(q, q, q, i.view(1, 2), i, i, 0.125, 1)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.kv_store(q, q, i, q, q)

@@ -5,7 +5,9 @@
 Every csrc/*.cu is compiled to an object under tokenfactory_b200/_build/ (in parallel, only when the
 source or a header is newer than the object), then linked with the static CUDA runtime into
 tokenfactory_b200/libtfattn.so.  A linker version script exports only the tf_* symbols declared in
-include/tfattn.h, so the library's private copy of the runtime never clashes with torch's.
+include/tfattn.h, so the library's private copy of the runtime never clashes with torch's.  Then
+csrc/torch_ext.cpp, the PyTorch front end over that C ABI, is compiled into
+tokenfactory_b200/_C.<python ext suffix>.so.
 """
 
 import argparse
@@ -58,7 +60,53 @@ def _compile(nvcc: str, src: str, verbose_ptxas: bool) -> str:
     return obj
 
 
+def _ext_path() -> str:
+    import sysconfig
+    return os.path.join(PKG, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_torch_ext() -> str:
+    """The PyTorch front end (tokenfactory_b200._C, csrc/torch_ext.cpp): a host C++ module over
+    libtfattn.so's C ABI, compiled with the host compiler against torch's headers and libraries,
+    linked to libtfattn.so through an $ORIGIN run path.  Returns the module's path."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    src = os.path.join(CSRC, "torch_ext.cpp")
+    out = _ext_path()
+    newest = max(os.path.getmtime(src), os.path.getmtime(LIB), _headers_mtime())
+    if os.path.exists(out) and os.path.getmtime(out) >= newest:
+        return out
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_C",
+           "-DTORCH_API_INCLUDE_EXTENSION_H", "-I", INCLUDE,
+           "-I", sysconfig.get_paths()["include"]]
+    for inc in ce.include_paths(device_type="cuda"):
+        cmd += ["-isystem", inc]
+    cmd += [src, "-o", out + ".tmp"]
+    for lib_dir in ce.library_paths(device_type="cuda"):
+        cmd += ["-L", lib_dir]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+            "-L", PKG, "-l:libtfattn.so", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch extension build failed:\n{r.stderr[-4000:]}")
+    os.replace(out + ".tmp", out)
+    return out
+
+
 def build(verbose_ptxas: bool = False, jobs: int = 0) -> str:
+    """Compile and link libtfattn.so, then the torch front end over it; returns the library path."""
+    lib = build_lib(verbose_ptxas, jobs)
+    build_torch_ext()
+    return lib
+
+
+def build_lib(verbose_ptxas: bool = False, jobs: int = 0) -> str:
     """Compile and link; returns the path of libtfattn.so."""
     nvcc = _nvcc()
     os.makedirs(BUILD, exist_ok=True)
