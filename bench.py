@@ -815,6 +815,195 @@ def bench_fp8(args, rank, world, dev):
 
 
 # ---------------------------------------------------------------------------------------------
+# config 5: 27B-shape hybrid decoder end to end
+# ---------------------------------------------------------------------------------------------
+C5 = dict(requests=256, prompt=1024, gen=256, layers=64, prefill_chunk=16)
+
+
+class _HotPathTimer:
+    """CUDA events around every hot-path call of the drop-in layers (the fused prologue and the
+    paged attention of full layers: a1-a4; the GDN conv + recurrence + gated norm of linear
+    layers: a5-a9), so that the projections, the MLP and the all-reduce stay outside.  Wraps
+    ops.attn_prologue, hybrid_attention._attend and hybrid_attention.linear_attention_core."""
+
+    def __init__(self):
+        from tokenfactory_b200 import hybrid_attention as H, ops
+        self.H, self.ops = H, ops
+        self.pairs = []
+        self.saved = (ops.attn_prologue, H._attend, H.linear_attention_core)
+
+    def _wrap(self, fn):
+        def timed(*a, **k):
+            s = torch.cuda.current_stream()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            r = fn(*a, **k)
+            e1.record(s)
+            self.pairs.append((e0, e1))
+            return r
+        return timed
+
+    def __enter__(self):
+        self.ops.attn_prologue = self._wrap(self.saved[0])
+        self.H._attend = self._wrap(self.saved[1])
+        self.H.linear_attention_core = self._wrap(self.saved[2])
+        return self
+
+    def __exit__(self, *exc):
+        self.ops.attn_prologue, self.H._attend, self.H.linear_attention_core = self.saved
+
+    def take_ms(self) -> float:
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in self.pairs)
+        self.pairs = []
+        return ms
+
+
+def bench_e2e(args, rank, world, dev):
+    """a random-init bf16 27B-shape hybrid decoder (hidden 5120, 64 layers,
+    every 4th full attention with the heads of config 2, GDN layers with those of config 3, MLP
+    17408, vocab 248320, MTP off) under head-sharded TP over `world` GPUs, on 256 concurrent
+    requests of 1024 uniform-random prompt tokens that each generate 256 greedy tokens: the
+    prompts prefill in chunks of 16 requests (16K tokens per forward), then all requests decode
+    together for 256 steps, each step's tokens sampled on the device (ops.sample_tokens) and fed
+    back without a host sync.  The hot-path calls are bracketed by CUDA events (_HotPathTimer):
+    the row-parallel all-reduces (NCCL) and the projections stay outside that figure."""
+    from tokenfactory_b200 import ForwardBatch, ops
+    from tokenfactory_b200.hybrid_model import HybridCachePool, HybridConfig, HybridForCausalLM
+
+    R, P, G, nl = args.c5_requests, args.c5_prompt, args.c5_gen, args.c5_layers
+    chunk = min(C5["prefill_chunk"], R)
+    cfg = HybridConfig(hidden_size=5120, intermediate_size=17408, num_hidden_layers=nl,
+                       vocab_size=248320, num_attention_heads=C2["Hq"],
+                       num_key_value_heads=C2["Hkv"], head_dim=C2["D"],
+                       linear_num_key_heads=C3["Hk"], linear_num_value_heads=C3["Hv"],
+                       linear_key_head_dim=C3["dk"], linear_value_head_dim=C3["dv"],
+                       output_gate_mode="sigmoid", tp_size=world, tp_rank=rank)
+    t_init = time.perf_counter()
+    torch.manual_seed(5 + rank)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = HybridForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(prev)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            if n.endswith("norm.weight") or n.endswith("layernorm.weight"):
+                p.fill_(1.0)
+            elif n.endswith("A_log"):
+                p.uniform_(0.0, 1.5)
+            elif n.endswith("dt_bias"):
+                p.normal_(0.0, 0.5)
+            elif "conv1d" in n:
+                p.normal_(0.0, 0.5)
+            else:
+                p.normal_(0.0, 0.02)
+    slots = R * (P + G) + 1
+    pool = HybridCachePool(cfg, slots, R, 0, dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator().manual_seed(55)
+    perm = torch.randperm(slots - 1, generator=gen)[: R * (P + G)] + 1
+    r2t = perm.view(R, P + G).to(dev)
+    prompts = torch.randint(0, cfg.vocab_size, (R, P), generator=gen).to(dev)
+    temps = torch.zeros(R, dtype=torch.float32, device=dev)
+    weights_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
+    init_s = time.perf_counter() - t_init
+
+    def prefill(c):
+        rows = torch.arange(c * chunk, (c + 1) * chunk, device=dev)
+        ext = [P] * chunk
+        fb = ForwardBatch(batch_size=chunk, req_pool_indices=rows,
+                          seq_lens=torch.full((chunk,), P, device=dev),
+                          prefix_lens=torch.zeros(chunk, dtype=torch.long, device=dev),
+                          extend_lens=ext, out_cache_loc=r2t[rows, :P].reshape(-1),
+                          req_to_token=r2t, is_prefill=True, max_seq_len=P, max_extend_len=P,
+                          extend_lens_tensor=torch.full((chunk,), P, device=dev),
+                          req_pool_indices_list=list(range(c * chunk, (c + 1) * chunk)))
+        pos = torch.arange(P, device=dev).repeat(chunk)
+        return model(prompts[c * chunk:(c + 1) * chunk].reshape(-1), pos, pool, fb)
+
+    rows_all = torch.arange(R, device=dev)
+    ones = torch.ones(R, dtype=torch.long, device=dev)
+
+    def decode(step, ids):
+        L = P + step + 1
+        fb = ForwardBatch(batch_size=R, req_pool_indices=rows_all,
+                          seq_lens=torch.full((R,), L, device=dev),
+                          prefix_lens=torch.full((R,), L - 1, device=dev), extend_lens=[1] * R,
+                          out_cache_loc=r2t[:, L - 1], req_to_token=r2t, is_prefill=False,
+                          max_seq_len=L, max_extend_len=1, extend_lens_tensor=ones,
+                          req_pool_indices_list=list(range(R)))
+        return model(ids, torch.full((R,), L - 1, device=dev), pool, fb)
+
+    def run(timer):
+        pool.conv_state.zero_()
+        pool.ssm_state.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        stream = torch.cuda.current_stream()
+        ev[0].record(stream)
+        first = []
+        for c in range(R // chunk):
+            first.append(ops.sample_tokens(prefill(c), temps[:chunk]))
+        ev[1].record(stream)
+        pre_attn = timer.take_ms() if timer else 0.0
+        ids = torch.cat(first)
+        for step in range(G - 1):  # the prefill produced each request's first token
+            ids = ops.sample_tokens(decode(step, ids), temps)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        dec_attn = timer.take_ms() if timer else 0.0
+        return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), pre_attn, dec_attn
+
+    # warm-up: one prefill chunk and a few decode steps (kernel set-up, cuBLAS heuristics)
+    pool.ssm_state.zero_()
+    out = prefill(0)
+    ids = torch.zeros(R, dtype=torch.long, device=dev)
+    for step in range(min(3, G - 1)):
+        decode(step, ids)
+    torch.cuda.synchronize()
+    _barrier(world)
+    with ClockSampler(torch.cuda.current_device()) as clk, _HotPathTimer() as timer:
+        timer.take_ms()
+        pre_ms, dec_ms, pre_attn, dec_attn = run(timer)
+    _barrier(world)
+    pre_ms = _max_over_ranks(pre_ms, world)
+    dec_ms = _max_over_ranks(dec_ms, world)
+    pre_attn = _max_over_ranks(pre_attn, world)
+    dec_attn = _max_over_ranks(dec_attn, world)
+    total_s = (pre_ms + dec_ms) / 1e3
+    toks = R * (P + G)
+    del out
+    return {
+        "metric": "27B-shape hybrid end to end: tokens/s and attention hot-path time (config 5)",
+        "value": toks / total_s, "unit": "tok/s (prompt + generated, whole job)",
+        "n_gpus": world, "steps": 1, "warmup": 1, "ms_per_step": (pre_ms + dec_ms),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights ~N(0, 0.02), uniform-random prompt ids)",
+        "config": {"workload": "config5 27B-shape hybrid decoder, continuous batch of "
+                               f"{R} requests x ({P} prompt + {G} generated) tokens",
+                   "hidden": 5120, "layers": nl, "full_attention_layers": nl // 4,
+                   "q_heads": C2["Hq"], "kv_heads": C2["Hkv"], "head_dim": C2["D"],
+                   "gdn_heads": f"{C3['Hk']}/{C3['Hv']} dk=dv=128", "mlp": 17408,
+                   "vocab": 248320, "parallelism": f"tp{world}", "prefill_chunk_requests": chunk,
+                   "weights_gb_per_rank": weights_gb, "init_s": init_s},
+        "prefill": {"ms": pre_ms, "tok_per_s": R * P / (pre_ms / 1e3),
+                    "attention_hot_path_ms": pre_attn,
+                    "attention_share": pre_attn / pre_ms if pre_ms else None},
+        "decode": {"ms": dec_ms, "steps": G - 1, "ms_per_step": dec_ms / max(1, G - 1),
+                   "tok_per_s": R * (G - 1) / (dec_ms / 1e3), "attention_hot_path_ms": dec_attn,
+                   "attention_share": dec_attn / dec_ms if dec_ms else None},
+        "attention_hot_path_ms": pre_attn + dec_attn,
+        "how": "CUDA events on the launching stream around the whole run and around every "
+               "hot-path call (prologue + paged attention of the 16 full layers, GDN conv + "
+               "recurrence + gated norm of the 48 linear layers); max over ranks; the "
+               "row-parallel all-reduces (NCCL) and projections are outside the hot-path figure",
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU baseline: the oracle (restatement of the reference's torch algorithm) on this host
 # ---------------------------------------------------------------------------------------------
 def _cpu_decode_sample(n_requests: int, seed: int = 0):
@@ -909,7 +1098,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 6])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=C2["B"],
@@ -922,6 +1111,11 @@ def main():
                     help="config 4: KV pool slots")
     ap.add_argument("--no-e2e", action="store_true",
                     help="profiling only: device-timed leg alone, short output")
+    ap.add_argument("--c5-requests", type=int, default=C5["requests"],
+                    help="config 5: concurrent requests")
+    ap.add_argument("--c5-prompt", type=int, default=C5["prompt"], help="config 5: prompt tokens")
+    ap.add_argument("--c5-gen", type=int, default=C5["gen"], help="config 5: generated tokens")
+    ap.add_argument("--c5-layers", type=int, default=C5["layers"], help="config 5: layers")
     ap.add_argument("--decode-only", action="store_true",
                     help="config 2 without the config 3 / config 4 legs that the default line carries")
     args = ap.parse_args()
@@ -940,7 +1134,7 @@ def main():
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     dev = torch.device("cuda", torch.cuda.current_device())
-    res = {2: bench_decode, 3: bench_gdn_decode, 4: bench_extend,
+    res = {2: bench_decode, 3: bench_gdn_decode, 4: bench_extend, 5: bench_e2e,
            6: bench_fp8}[args.config](args, rank, world, dev)
     if args.config == 2 and not args.no_e2e and not args.decode_only:
         # the rest of the metric in the same line: config 3 (GDN decode) and config 4 (extend

@@ -370,3 +370,100 @@ def fp8_inputs(spec: dict) -> dict:
     if spec["bias"]:
         out["bias"] = _bf.store(_normal(rng, (N,), 0.1), spec["dtype"])
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# engine-level cases: whole runs of the reference's Scheduler recorded as a trace
+# (tests/golden/make_engine_golden.py) and replayed on the GPU through the drop-in layers
+# ---------------------------------------------------------------------------------------------
+# model dims: fields of Qwen3_8Config / tokenfactory_b200.hybrid_model.HybridConfig
+ENGINE_MODELS: Dict[str, dict] = {
+    # vocab 1024, hidden 256, [lin, lin, lin, full], Hq 8 / Hkv 2 / D 64,
+    # theta 1e7, sigmoid output gate, Hk 4 / Hv 8 / dk = dv = 64, conv 4, MLP 512, fp32
+    "config1": dict(vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                    num_attention_heads=8, num_key_value_heads=2, head_dim=64,
+                    rope_theta=10000000.0, linear_num_key_heads=4, linear_key_head_dim=64,
+                    linear_num_value_heads=8, linear_value_head_dim=64,
+                    linear_conv_kernel_dim=4, output_gate_mode="sigmoid"),
+    # the mini model of the reference's prefix-reuse test (tests/test_hybrid_radix_cache.py:127-146)
+    "prefix": dict(vocab_size=500, hidden_size=128, intermediate_size=256, num_hidden_layers=4,
+                   num_attention_heads=4, num_key_value_heads=1, head_dim=32,
+                   linear_num_key_heads=2, linear_key_head_dim=16, linear_num_value_heads=6,
+                   linear_value_head_dim=16, output_gate_mode="silu"),
+    # the model of the reference's TP test (tests/test_tensor_parallel.py:104-126)
+    "tp": dict(vocab_size=500, hidden_size=128, intermediate_size=256, num_hidden_layers=4,
+               num_attention_heads=4, num_key_value_heads=2, head_dim=32, linear_num_key_heads=4,
+               linear_key_head_dim=16, linear_num_value_heads=12, linear_value_head_dim=16,
+               output_gate_mode="silu"),
+}
+
+ENGINE_WEIGHT_SEED = {"config1": 11, "prefix": 42, "tp": 2026}
+
+# scheduler scenarios: (model, scheduler kwargs, requests); the requests of a phase are queued
+# together and the scheduler is stepped until it is idle (or for `steps` steps)
+ENGINE_RUNS: Dict[str, dict] = {
+    "config1": dict(model="config1",
+                    sched=dict(max_reqs=8, max_context_len=128, max_total_tokens=512,
+                               max_snapshots=8, chunked_prefill_size=32),
+                    phases=[dict(prompts="config1", max_new_tokens=32)]),
+    # reference test_hybrid_scheduler_prefix_reuse_exact_equivalence, its cached scheduler ...
+    "prefix_cached": dict(model="prefix",
+                          sched=dict(max_reqs=4, max_context_len=32, max_total_tokens=64,
+                                     max_snapshots=4, chunked_prefill_size=4),
+                          phases=[dict(prompts=[[10, 20, 30, 40, 50, 60]], max_new_tokens=2),
+                                  dict(prompts=[[10, 20, 30, 40, 50, 60, 70, 80]],
+                                       max_new_tokens=1, steps=1)]),
+    # ... and its fresh one, which computes the whole prompt in one step
+    "prefix_fresh": dict(model="prefix",
+                         sched=dict(max_reqs=4, max_context_len=32, max_total_tokens=64,
+                                    max_snapshots=4, chunked_prefill_size=16),
+                         phases=[dict(prompts=[[10, 20, 30, 40, 50, 60, 70, 80]],
+                                      max_new_tokens=1, steps=1)]),
+}
+
+
+def engine_prompts(name) -> List[List[int]]:
+    """Config 1's four prompts: lengths 16/32/48/64 of uniform token ids in [0, 1024), seed 0."""
+    if name != "config1":
+        return name
+    rng = np.random.default_rng(0)
+    return [[int(x) for x in rng.integers(0, 1024, n)] for n in (16, 32, 48, 64)]
+
+
+def engine_weights(shapes: Dict[str, tuple], seed: int) -> Dict[str, np.ndarray]:
+    """Seeded float32 weights for a model's state_dict, by parameter name (the same for the
+    reference model and the drop-in assembly, which share names): norms 1 + 0.1 N, A_log
+    U(0, 1.5), dt_bias 0.5 N, conv taps 0.5 N, embeddings N(0, 1), lm_head N(0, 1/64) (logits of
+    a few units, so greedy choices have clear margins), other projections N(0, 1/fan_in)."""
+    import zlib
+
+    out = {}
+    for name in sorted(shapes):
+        shp = tuple(shapes[name])
+        rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+        if name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+            w = 1.0 + 0.1 * rng.standard_normal(shp)
+        elif name.endswith("A_log"):
+            w = rng.uniform(0.0, 1.5, shp)
+        elif name.endswith("dt_bias"):
+            w = 0.5 * rng.standard_normal(shp)
+        elif "conv1d" in name:
+            w = 0.5 * rng.standard_normal(shp)
+        elif "embed_tokens" in name:
+            w = rng.standard_normal(shp)
+        elif name == "lm_head.weight":
+            w = rng.standard_normal(shp) / 8.0
+        else:
+            w = rng.standard_normal(shp) / np.sqrt(shp[-1])
+        out[name] = w.astype(np.float32)
+    return out
+
+
+# the reference TP test's batches (tests/test_tensor_parallel.py:181-250): a 2-request prefill
+# (4 + 3 tokens) then one decode step
+TP_PREFILL = dict(positions=[0, 1, 2, 3, 0, 1, 2], req_pool_indices=[0, 1], seq_lens=[4, 3],
+                  prefix_lens=[0, 0], extend_lens=[4, 3], out_cache_loc=[1, 2, 3, 4, 5, 6, 7],
+                  rows={0: [1, 2, 3, 4], 1: [5, 6, 7]})
+TP_DECODE = dict(positions=[4, 3], req_pool_indices=[0, 1], seq_lens=[5, 4], prefix_lens=[4, 3],
+                 extend_lens=[1, 1], out_cache_loc=[8, 9], rows={0: [1, 2, 3, 4, 8],
+                                                                 1: [5, 6, 7, 9]})
