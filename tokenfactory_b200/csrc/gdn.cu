@@ -1242,20 +1242,26 @@ constexpr int oOT = oZ + C * D * 4;           // T [64][128] output rows (O' tra
 constexpr int oMk = oOT + C * D * 2;          // fp32 [64 j][64 i]: Mk transposed
 constexpr int oMqH = oMk + C * C * 4;         // bf16 [64 rows][128 B] K-major (SWIZZLE_128B)
 constexpr int oMqL = oMqH + C * 128;
+// The off-diagonal block Mk10 (rows 32-63, columns 0-31 of Mk) as the bf16 hi / lo B operand of
+// the solve's tensor-core step: [32 rows][128 B] K-major (SWIZZLE_128B; K = 32, the first 64
+// bytes of a row)
+constexpr int kTile = 32 * 128;
+constexpr int oM10H = oMqL + C * 128;
+constexpr int oM10L = oM10H + kTile;
 // per-token arrays [2][7][64]: gamma (log2 units), beta, 1/|k|, dk^-1/2/|q|, e^gamma/|k| (the
 // solve's right side), e^gamma dk^-1/2/|q| (O' = e^g QS'), e^(gamma_C - gamma)/|k| (U'')
-constexpr int oArr = oMqL + C * 128;
+constexpr int oArr = oM10L + kTile;
 constexpr int kArr = 7 * C * 4;
 enum { aGam = 0, aBet, aInK, aInQ, aEk, aEq, aSk };
 constexpr int oGr = oArr + 2 * kArr;          // raw g [64] (loaders)
-constexpr int oBar = oGr + C * 4;             // in_full[2] p1 l1 p2[2] tm_free chunk_free fin rows_full[2] p1x
-constexpr int oWords = oBar + 96;             // tmem holder, abort
+constexpr int oBar = oGr + C * 4;             // in_full[2] p1 l1 p2[2] tm_free chunk_free fin rows_full[2] p1x sreq sdone p2s
+constexpr int oWords = oBar + 128;            // tmem holder, abort
 constexpr int oRawZ = (oWords + 16 + 1023) & ~1023;  // next chunk's raw z rows (T)
 constexpr int kSmem = oRawZ + C * D * 2 + 1024;
 static_assert(kSmem <= 232448, "shared memory per CTA");
 constexpr int cS = 0, cSH = 128, cSL = 192, cX = 256, cY = 320, cZ = 384, cUH = 448, cUL = 480;
-static_assert(oMqH % 1024 == 0 && oMqL % 1024 == 0 && kStack % 1024 == 0,
-              "SWIZZLE_128B tiles are 1024-byte aligned");
+static_assert(oMqH % 1024 == 0 && oMqL % 1024 == 0 && kStack % 1024 == 0 && oM10H % 1024 == 0 &&
+              kTile % 1024 == 0, "SWIZZLE_128B tiles are 1024-byte aligned");
 
 // 2^x (ex2.approx.ftz: relative error about 2^-22)
 __device__ __forceinline__ float ex2(float x) {
@@ -1393,6 +1399,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   uint64_t* fin = bars + 8;            // every MMA of the CTA has completed
   uint64_t* rows_full = bars + 9;      // [2] a chunk's q, k, v rows have landed (TMA)
   uint64_t* p1x = bars + 11;           // X of the chunk is in TMEM (the rest of phase 1 follows)
+  uint64_t* sreq = bars + 12;          // U'0 (the solved first 32 tokens) is in TMEM
+  uint64_t* sdone = bars + 13;         // E = U'0 Mk10^T is in TMEM
+  uint64_t* p2s = bars + 14;           // a chunk's state-update MMAs (S' += U'' K) have completed
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
 
@@ -1419,6 +1428,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
     mbar_init(rows_full, 1);
     mbar_init(rows_full + 1, 1);
     mbar_init(p1x, 1);
+    mbar_init(sreq, 4);
+    mbar_init(sdone, 1);
+    mbar_init(p2s, 1);
     mbar_init(tm_free, 4);
     mbar_init(chunk_free, 4);
     mbar_init(fin, 1);
@@ -1696,6 +1708,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       constexpr uint32_t idYZ = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = tc::idesc_bf16(128, 64, false, false);
       constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, true);
+      constexpr uint32_t idB = tc::idesc_bf16(128, 32, false, false);
       for (int ci = 0; ci < nchunks; ++ci) {
         const int bf = ci & 1;
         const uint32_t kq = base + oKQ + bf * kStack;
@@ -1722,6 +1735,19 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           }
         }
         tc::commit(p1);
+        if (!waitb(sreq, ci & 1, abort)) break;
+        tc::fence_after_sync();
+        tc::fence_proxy_async_smem();
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          mma_ts(tmem + cX + 32, tmem + cUH + kk * 8, tc::sw128_desc(base + oM10H + kk * 32, 16, 1024), idB, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          mma_ts(tmem + cX + 32, tmem + cUH + kk * 8, tc::sw128_desc(base + oM10L + kk * 32, 16, 1024), idB, true);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          mma_ts(tmem + cX + 32, tmem + cUL + kk * 8, tc::sw128_desc(base + oM10H + kk * 32, 16, 1024), idB, true);
+        tc::commit(sdone);
         if (!waitb(l1, ci & 1, abort)) break;
         tc::fence_after_sync();
         tc::fence_proxy_async_smem();
@@ -1800,16 +1826,29 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         const float gi = gam[i];
         const float4* g4 = reinterpret_cast<const float4*>(gam);
         const float4* n4 = reinterpret_cast<const float4*>(ink);
-        if (l < 64) {  // Mk_ij = beta_i e^(g_i - g_j) k_i.k_j / (|k_i| |k_j|)
+        if (l < 64) {  // Mk_ij = beta_i e^(g_i - g_j) k_i.k_j / (|k_i| |k_j|), strictly lower
+          // stored transposed for the register solves; rows 32-63 (warp 1) also write their
+          // columns 0-31, the block Mk10, as the bf16 hi / lo B operand of the tensor-core step
           const float bi = bet[i] * ink[i];
 #pragma unroll
           for (int j4 = 0; j4 < 16; ++j4) {
             const float4 g = g4[j4], n = n4[j4];
             const float gj[4] = {g.x, g.y, g.z, g.w}, nj[4] = {n.x, n.y, n.z, n.w};
+            float m[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int j = 4 * j4 + e;
-              MkT[j * C + i] = j < i ? bi * ex2(gi - gj[e]) * (x[j] * nj[e]) : 0.f;
+              m[e] = j < i ? bi * ex2(gi - gj[e]) * (x[j] * nj[e]) : 0.f;
+              MkT[j * C + i] = m[e];
+            }
+            if (j4 < 8 && l >= 32) {
+              uint32_t h0, h1, l0, l1_;
+              split2(m[0], m[1], h0, l0);
+              split2(m[2], m[3], h1, l1_);
+              const int ib = i - 32;
+              const uint32_t off = ib * 128 + ((uint32_t)((j4 >> 1) ^ (ib & 7)) << 4) + (j4 & 1) * 8;
+              sts_v2(base + oM10H + off, h0, h1);
+              sts_v2(base + oM10L + off, l0, l1_);
             }
           }
         } else {  // Mq_ij = e^(g_i - g_j) q_i.k_j dk^-1/2 / (|q_i| |k_j|)
@@ -1837,11 +1876,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       ok = bar_and(1, 128, waitb(p1, ci & 1, abort));  // KS', QS' (and the masks are written)
       if (!ok) break;
       tc::fence_after_sync();
-      // ---- U' row l: (I + Mk) u = beta (v - e^g KS), right-looking: once u_j is final, every
-      //      later row takes its term at once (independent FMAs; column j of Mk is contiguous)
+      // ---- U' row l: (I + Mk) U' = U with U = beta (v - e^g KS), in two halves of 32 tokens:
+      //      tokens 0-31 solved in registers, their terms on tokens 32-63 (E = U'0 Mk10^T, half
+      //      of the solve's products) on the tensor core, then tokens 32-63 in registers.  The
+      //      register solves are right-looking: once u_j is final, every later row of the half
+      //      takes its term (independent FMAs; column j of Mk is contiguous), rows (2p, 2p+1)
+      //      packed in one 64-bit register and updated by one fma.rn.f32x2
       {
-        // rows (2p, 2p+1) packed in one 64-bit register and updated by one fma.rn.f32x2; the
-        // term of row j itself is multiplied by Mk[j][j] = 0 (Mk is strictly lower)
         uint64_t u2[32];
         {
           float u[64];
@@ -1856,7 +1897,38 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           for (int p = 0; p < 32; ++p) u2[p] = pack2(u[2 * p], u[2 * p + 1]);
         }
 #pragma unroll
-        for (int j = 0; j < 63; ++j) {
+        for (int j = 0; j < 31; ++j) {
+          const float uj = (j & 1) ? hi_of(u2[j >> 1]) : lo_of(u2[j >> 1]);
+          const uint64_t nuj = pack2(-uj, -uj);
+#pragma unroll
+          for (int q4 = (j + 1) >> 2; q4 < 8; ++q4) {
+            const ulonglong2 m = *reinterpret_cast<const ulonglong2*>(MkT + j * C + 4 * q4);
+            if (4 * q4 + 1 > j) u2[2 * q4] = ffma2(m.x, nuj, u2[2 * q4]);
+            u2[2 * q4 + 1] = ffma2(m.y, nuj, u2[2 * q4 + 1]);
+          }
+        }
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) split2(lo_of(u2[k]), hi_of(u2[k]), hi[k], lo[k]);
+        st16u(lb + cUH, hi);
+        st16u(lb + cUL, lo);
+        tc::wait_st();
+        tc::fence_before_sync();
+        tc::fence_proxy_async_smem();  // Mk10 is read by the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sreq);
+        ok = bar_and(1, 128, waitb(sdone, ci & 1, abort));
+        if (!ok) break;
+        tc::fence_after_sync();
+        {
+          float e[32];
+          tc::ld32(lb + cX + 32, e);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) u2[16 + k] = pack2(lo_of(u2[16 + k]) - e[2 * k], hi_of(u2[16 + k]) - e[2 * k + 1]);
+        }
+#pragma unroll
+        for (int j = 32; j < 63; ++j) {
           const float uj = (j & 1) ? hi_of(u2[j >> 1]) : lo_of(u2[j >> 1]);
           const uint64_t nuj = pack2(-uj, -uj);
 #pragma unroll
@@ -1866,16 +1938,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
             u2[2 * q4 + 1] = ffma2(m.y, nuj, u2[2 * q4 + 1]);
           }
         }
-        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            split2(lo_of(u2[16 * h + k]), hi_of(u2[16 * h + k]), hi[k], lo[k]);
-          st16u(lb + cUH + 16 * h, hi);
-          st16u(lb + cUL + 16 * h, lo);
-        }
-        // U'' = U' e^(gamma_C - gamma) / |k| (the state update's A; X is consumed)
+        for (int k = 0; k < 16; ++k) split2(lo_of(u2[16 + k]), hi_of(u2[16 + k]), hi[k], lo[k]);
+        st16u(lb + cUH + 16, hi);
+        st16u(lb + cUL + 16, lo);
+        // U'' = U' e^(gamma_C - gamma) / |k| (the state update's A) over cX
         const float2* s2 = reinterpret_cast<const float2*>(skf);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
