@@ -1007,14 +1007,18 @@ def bench_e2e(args, rank, world, dev):
 # CPU baseline: the oracle (restatement of the reference's torch algorithm) on this host
 # ---------------------------------------------------------------------------------------------
 def _cpu_decode_sample(n_requests: int, seed: int = 0):
-    """A bounded CPU sample of config 2: requests with the config's length distribution over a
-    200K-slot host pool (the GPU pool's 1.2M slots would take 5 GB of host memory)."""
+    """A bounded CPU sample of config 2: requests with the config's length distribution and heads
+    over a host pool of config 2's own size (1.2M slots, 4.9 GB of bf16 K and V), so the gathers
+    walk the same memory footprint as on the GPU.  The pool's rows repeat a random block of 64K
+    rows (finite bf16 patterns; the work does not depend on the values)."""
     rng = np.random.default_rng(seed)
-    S = 200_000
+    S = C2["slots"]
     D, Hkv, Hq = C2["D"], C2["Hkv"], C2["Hq"]
     lens = rng.integers(C2["Lmin"], C2["Lmax"] + 1, n_requests)
-    kb = rng.integers(0x3C00, 0x4000, (S, Hkv, D), dtype=np.uint16)  # finite bf16 patterns
-    vb = rng.integers(0x3C00, 0x4000, (S, Hkv, D), dtype=np.uint16)
+    blk = 1 << 16
+    reps = (S + blk - 1) // blk
+    kb = np.tile(rng.integers(0x3C00, 0x4000, (blk, Hkv, D), dtype=np.uint16), (reps, 1, 1))[:S]
+    vb = np.tile(rng.integers(0x3C00, 0x4000, (blk, Hkv, D), dtype=np.uint16), (reps, 1, 1))[:S]
     r2t = np.full((n_requests, C2["Lmax"]), -1, dtype=np.int64)
     for b in range(n_requests):
         r2t[b, :lens[b]] = rng.integers(1, S, lens[b])
@@ -1075,7 +1079,7 @@ def run_reference(args, rank, world):
         el = time.perf_counter() - t0
     v = threads * args.steps / el
     sample = (f"{threads} decode requests per step (one per thread) of config 2's length "
-              f"distribution over a 200K-slot host pool")
+              f"distribution and heads over a host pool of config 2's {C2['slots']} slots")
     return {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
@@ -1088,7 +1092,11 @@ def run_reference(args, rank, world):
                    "head_dim": C2["D"], "seq_len": f"U[{C2['Lmin']},{C2['Lmax']}]",
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "same_config": True,
+                         "why_port": "the reference's path is Python over torch; its sources "
+                                     "cannot travel to the GPU box, so the arm is the oracle's "
+                                     "restatement of _slot_based_attention, pinned to the "
+                                     "reference's own outputs by committed fixtures"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -1155,8 +1163,9 @@ def main():
         v, n = cpu_decode_baseline(args.cpu_baseline_seconds, threads)
         res["cpu_baseline"] = {
             "value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n} decode requests of config 2's length distribution "
-                      f"({args.cpu_baseline_seconds:.0f} s budget, {threads} threads)"}
+            "sample": f"{n} decode requests of config 2's length distribution and heads over "
+                      f"a {C2['slots']}-slot host pool ({args.cpu_baseline_seconds:.0f} s budget, "
+                      f"{threads} threads)", "same_config": True}
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
