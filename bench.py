@@ -94,7 +94,7 @@ _REASONS = {
 
 class ClockSampler:
     """SM clocks and throttle reasons sampled while the timed region runs: NVML read every
-    2 ms from a thread (so that even a region of a few milliseconds is covered), with
+    0.5 ms from a thread (so that even a region of a few milliseconds is covered), with
     nvidia-smi at 100 ms as the fallback when NVML cannot be loaded.  Reads only."""
 
     def __init__(self, gpu_index: int):
@@ -116,7 +116,7 @@ class ClockSampler:
     def _nvml_loop(self, handle, nv):
         while not self._stop.is_set():
             self._nvml_sample(handle, nv)
-            time.sleep(0.002)
+            time.sleep(0.0005)
 
     def __enter__(self):
         try:
