@@ -1,27 +1,33 @@
 """Benchmark of the B200 hybrid-attention hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5|6] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU, NCCL)
 
-Default workload (the configuration the headline metric is quoted on):
-paged GQA decode, bf16, 128 requests, 32 q heads / 4 kv heads, head_dim 256, seq_lens ~ U[512, 8192],
-token-granular pages: each request's slots are a random draw from a 1.2M-slot pool (slot 0 reserved),
-q and K/V ~ N(0,1), sigmoid output gate from N(0,1) logits, scale 1/16.  One step = the decode
-step of one full-attention layer: KV store of the new token (a1) + paged decode with fused gate
-(a2, a4).  With N GPUs the heads are sharded exactly like the reference's tensor-parallel split
-(qwen3_8/full_attention.py:43-52, kv heads replicated once N > 4) and every rank decodes the whole
-batch for its heads: total work is fixed, so scaling is "strong".
---config 3: Gated DeltaNet recurrent decode (B=256, Hk=16, Hv=48, dk=dv=128, fp32 state).
---config 4: extend over a radix-cached prefix (16 requests, prefix U[0,4096], extend U[512,2048]):
-            causal extend attention in TFLOP/s, and the GDN extend of the same tokens.
+Default line (the configuration the headline metric is quoted on): paged GQA
+decode, bf16, 128 requests, 32 q heads / 4 kv heads, head_dim 256, seq_lens ~ U[512, 8192],
+token-granular pages: each request's slots are a random draw from a 1.2M-slot pool (slot 0
+reserved), q and K/V ~ N(0,1), sigmoid output gate from N(0,1) logits, scale 1/16.  One step = the
+decode step of one full-attention layer: KV store of the new token (a1) + paged decode with fused
+gate (a2, a4).  With N GPUs the heads are sharded exactly like the reference's tensor-parallel
+split (qwen3_8/full_attention.py:43-52, kv heads replicated once N > 4) and every rank decodes the
+whole batch for its heads: total work is fixed, so scaling is "strong"; `value` is the whole job's
+tokens/s, `value_per_gpu` beside it.  The rest of the metric rides in the same line, each leg timed
+on its own: `gdn_decode` (config 3: Gated DeltaNet recurrent decode, B=256, Hk=16, Hv=48,
+dk=dv=128, fp32 state) and `extend` (config 4: 16 requests, prefix U[0,4096], extend U[512,2048]:
+causal extend attention in TFLOP/s, the GDN extend of the same tokens, the fused prologue and the
+admission-time state snapshots).
+--config 3 / 4: those legs alone, with their own headline.
+--config 5: the 27B-shape hybrid model end to end (256 requests x (1024 + 256) tokens).
+--config 6: the block-FP8 GEMM of the 27B MLP up projection.
 
 Timing: W warm-up steps, then K steps between CUDA events on the launching stream, bracketed by a
 barrier and synchronize; the max over ranks is reported.  The K/V read per step (2.3 GB) is far
 larger than L2, so no flush is needed.  `e2e` repeats the measurement through the public API with
 the step's inputs copied from pinned host memory and its output copied back inside the timed
 region, the copies of neighbouring steps overlapping the kernels (runner.PipelinedStep);
-`e2e_serial` is the same with the copies in series.  `cpu_baseline` times the CPU oracle (a restatement of the reference's torch algorithm) on a
-bounded sample on this host; `--impl reference` times only that.
+`e2e_serial` is the same with the copies in series, `e2e_eager` the step issued call by call.
+`cpu_baseline` times the CPU oracle (a restatement of the reference's torch algorithm, pinned to
+its outputs) on a bounded sample on this host's cores; `--impl reference` times only that.
 """
 
 import argparse
