@@ -150,7 +150,8 @@ def test_decode_many_items_with_a_skipped_request():
 def test_extend_long_request_27b_heads_vs_oracle():
     """A 1000-token request (16 chunks: the tensor-core chunk kernel alternates its two sets of
     chunk buffers and barriers many times) between short ones, against the oracle.  The gated
-    outputs are rounded twice by the reference: two bf16 steps allowed (tests/helpers.py)."""
+    outputs are rounded twice by the reference: two bf16 steps allowed (tests/helpers.py); the
+    un-normed outputs, rounded once, are held to the plain bound."""
     ext = [3, 1000, 130]
     spec = dict(dtype="bf16", nk=2, nv=6, dk=128, dv=128, kc=4, ext=ext, req=[2, 0, 3],
                 slots=5, seed=1133)
@@ -161,6 +162,11 @@ def test_extend_long_request_27b_heads_vs_oracle():
     assert_close(out, orc, "bf16", what="extend with a 1000-token request", bf16_steps=2)
     np.testing.assert_array_equal(to_numpy(t["conv_state"]), cs)
     np.testing.assert_allclose(to_numpy(t["ssm_state"]), ss, rtol=2e-3, atol=2e-5)
+    # the un-normed outputs (one rounding) at the plain bound
+    t_raw = _tensors(inp, "bf16")
+    raw = values(_run(spec, t_raw, False), "bf16")
+    orc_raw, _, _ = _oracle(spec, inp, False)
+    assert_close(raw, orc_raw, "bf16", what="extend with a 1000-token request, raw outputs")
 
 
 def test_extend_more_ctas_than_sms_vs_oracle():
