@@ -62,3 +62,26 @@ def test_larger_shapes_match_oracle(M, N, K, scales, bias):
                               BF.as_f32(inp["bias"], "bf16") if bias else None)
     got = BF.as_f32(to_numpy(out), "bf16")
     assert np.all(np.abs(got - ref) <= _tol(ref, "bf16")), np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("M,N,K,scales,bias", [(1100, 4400, 1008, True, True),
+                                               (2048, 4352, 512, True, False),
+                                               (1300, 4608, 256, False, True)])
+def test_wide_tiles_match_oracle(M, N, K, scales, bias):
+    """Problems with at least one 128 x 256 tile per SM take the persistent wide-tile kernel:
+    row and column tails (a 256-column tile whose second half lies past N), a ragged last K block,
+    more tiles than SMs (CTAs that walk several tiles through one stage ring), and both halves of
+    a tile with their own weight-scale rows."""
+    from tokenfactory_b200 import ops
+    tiles = -(-M // 128) * -(-N // 256)
+    assert tiles >= torch.cuda.get_device_properties(0).multi_processor_count
+    spec = dict(dtype="bf16", M=M, N=N, K=K, scales=scales, bias=bias, seed=M + N + K)
+    inp = C.fp8_inputs(spec)
+    x, w, ws, b = _tensors(inp, "bf16")
+    out = ops.block_fp8_linear(x.view(M, K), w, ws, b)
+    torch.cuda.synchronize()
+    qn, sn = OF.quantize_act(inp["x"], "bf16")
+    ref = OF.block_fp8_linear(qn, sn, inp["w"], inp.get("w_scale"),
+                              BF.as_f32(inp["bias"], "bf16") if bias else None)
+    got = BF.as_f32(to_numpy(out), "bf16")
+    assert np.all(np.abs(got - ref) <= _tol(ref, "bf16")), np.abs(got - ref).max()

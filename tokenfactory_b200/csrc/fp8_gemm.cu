@@ -352,6 +352,207 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
   if (warp == kMmaWarp) tc::tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Prefill-sized M: 128 x 256 tiles, one persistent CTA per SM.  A K block of a 256-column tile
+// moves 48 KB (16 KB of q, 32 KB of w) for twice the products of a 128 x 128 tile's 32 KB, a
+// quarter less L2 -> SM traffic per product, which is what bounds the 128 x 128 kernel.  Each CTA
+// walks the tiles blockIdx.x, blockIdx.x + gridDim.x, ... (n fastest), with one running count of
+// K blocks for the stage ring and the accumulator pair, so the next tile's loads and first
+// products overlap the current tile's output writes.  TMEM holds two 256-column accumulators;
+// epilogue warp w reads lanes 32 (w % 4) .. +31 and the 128 columns 128 (w / 4) .. +127, the span
+// of one weight-scale row block (block_h is a multiple of 128).
+// ---------------------------------------------------------------------------------------------
+constexpr int kBNW = 256;
+constexpr int kStagesW = 4;
+constexpr int kTileW = kBNW * kBK;              // 32 KB of w rows per stage
+constexpr int kStageBytesW = kTile + kTileW;    // 48 KB
+constexpr int kAccW = 2;                        // TMEM accumulators of 256 columns (all 512)
+constexpr int kSmemW = kStagesW * kStageBytesW + 256 + 1024;
+static_assert(kSmemW <= 232448, "shared memory per CTA");
+
+struct BarsW {
+  uint64_t full[kStagesW], empty[kStagesW], pfull[kAccW], pfree[kAccW], fin;
+  uint32_t tmem;
+  int abort;
+};
+static_assert(sizeof(BarsW) <= 256, "barriers overflow their shared-memory slot");
+
+template <typename TO>
+__global__ void __launch_bounds__(kThreads, 1) block_gemm_wide_kernel(tf_fp8_gemm_args a,
+                                                                      const __grid_constant__ CUtensorMap map_q,
+                                                                      const __grid_constant__ CUtensorMap map_w,
+                                                                      int tiles_n, int tiles) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;
+  unsigned char* sb = smem_raw + (base - raw);
+  BarsW* bars = reinterpret_cast<BarsW*>(sb + kStagesW * kStageBytesW);
+  volatile int* abort = &bars->abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nkb = (a.K + kBK - 1) / kBK;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStagesW; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < kAccW; ++b) {
+      mbar_init(&bars->pfull[b], 1);
+      mbar_init(&bars->pfree[b], 8);
+    }
+    mbar_init(&bars->fin, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) tc::tmem_alloc(&bars->tmem, 512);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == kLoadWarp) {
+    // ============ loads: a q box and a 256-row w box per stage, over all of this CTA's tiles ============
+    if (lane == 0) {
+      uint32_t g = 0;  // K blocks issued so far
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int n0 = (t % tiles_n) * kBNW, m0 = (t / tiles_n) * kBM;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const uint32_t s = g % kStagesW;
+          if (g >= kStagesW && !wait_b(&bars->empty[s], ((g / kStagesW) - 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = base + s * kStageBytesW;
+          mbar_arrive_expect_tx(&bars->full[s], kStageBytesW);
+          tma_load_box(st, &map_q, kb * kBK, m0, &bars->full[s]);
+          tma_load_box(st + kTile, &map_w, kb * kBK, n0, &bars->full[s]);
+        }
+      }
+      // after an abort, boxes still in flight land (bounded wait) before the CTA ends
+      for (uint32_t j = g > (uint32_t)kStagesW ? g - kStagesW : 0; j < g; ++j)
+        mbar_wait(&bars->full[j % kStagesW], (j / kStagesW) & 1);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ============ MMA issue (one thread): K block g into accumulator g % 2 ============
+    if (lane == 0) {
+      constexpr uint32_t idesc = (1u << 4)                       // D: f32
+                                 | (0u << 7) | (0u << 10)         // A, B: e4m3
+                                 | ((uint32_t)(kBNW >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const uint32_t s = g % kStagesW, b = g % kAccW;
+          if (!wait_b(&bars->full[s], (g / kStagesW) & 1, abort) ||
+              (g >= kAccW && !wait_b(&bars->pfree[b], ((g / kAccW) - 1) & 1, abort))) {
+            ok = false;
+            break;
+          }
+          tc::fence_proxy_async_smem();
+          tc::fence_after_sync();
+          const uint32_t st = base + s * kStageBytesW;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {  // K = 32 e4m3 values = 32 bytes per MMA
+            const uint64_t da = tc::sw128_desc(st + kk * 32, 16, 1024);
+            const uint64_t db = tc::sw128_desc(st + kTile + kk * 32, 16, 1024);
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem + b * kBNW),
+                "l"(da), "l"(db), "r"(idesc), "r"(kk > 0 ? 1u : 0u)
+                : "memory");
+          }
+          tc::commit(&bars->empty[s]);
+          tc::commit(&bars->pfull[b]);
+        }
+      }
+      // every MMA issued has completed before TMEM is released, also after an abort (bounded)
+      tc::commit(&bars->fin);
+      mbar_wait(&bars->fin, 0);
+    }
+    __syncwarp();
+  } else {
+    // ============ epilogue: acc += w_scale * partial per K block, then out = acc * x_scale + bias ============
+    const int q = warp & 3, h = warp >> 2;
+    const int row = 32 * q + lane;
+    const uint32_t lb = tmem + ((uint32_t)(32 * q) << 16) + 128 * h;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const int n0 = (t % tiles_n) * kBNW + 128 * h;  // this warp's first column
+      const int64_t m0 = (int64_t)(t / tiles_n) * kBM;
+      // a half that starts past N has no output columns and reads no weight scale
+      const float* wsrow = a.w_scale && n0 < a.N ? a.w_scale + (int64_t)(n0 / a.block_h) * a.ws_stride_n
+                                                 : nullptr;
+      auto scale_of = [&](int kb) -> float {
+        return wsrow ? __ldg(wsrow + (int64_t)(kb * kBK / a.block_w) * a.ws_stride_k) : 1.f;
+      };
+      float acc[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      float sc_next = scale_of(0);
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const uint32_t b = g % kAccW;
+        const float sc = sc_next;
+        if (kb + 1 < nkb) sc_next = scale_of(kb + 1);  // in flight while this block's MMAs finish
+        if (!wait_b_backoff(&bars->pfull[b], (g / kAccW) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float p[32];
+          tc::ld32(lb + b * kBNW + 32 * c, p);
+          tc::wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[32 * c + j] = fmaf(p[j], sc, acc[32 * c + j]);
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->pfree[b]);
+      }
+      if (!ok || m0 + row >= a.M || n0 >= a.N) continue;
+      const float xs = *a.x_scale;
+      TO* out = reinterpret_cast<TO*>(a.out) + (m0 + row) * a.out_stride + n0;
+      const int ncol = a.N - n0 < 128 ? a.N - n0 : 128;
+      const bool vec = ncol == 128 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && sizeof(TO) == 2;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int n = c8 * 8 + e;
+          float bias = 0.f;
+          if (a.bias && n < ncol) {
+            const int64_t bn = n0 + n;
+            bias = a.bias_dtype == TF_DTYPE_F32 ? reinterpret_cast<const float*>(a.bias)[bn]
+                 : a.bias_dtype == TF_DTYPE_BF16 ? to_f(reinterpret_cast<const __nv_bfloat16*>(a.bias)[bn])
+                                                 : to_f(reinterpret_cast<const __half*>(a.bias)[bn]);
+          }
+          v[e] = fmaf(acc[n], xs, bias);
+        }
+        if (vec) {
+          TO pk[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pk[e] = from_f<TO>(v[e]);
+          *reinterpret_cast<uint4*>(out + c8 * 8) = *reinterpret_cast<const uint4*>(pk);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (c8 * 8 + e < ncol) out[c8 * 8 + e] = from_f<TO>(v[e]);
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && *abort && a.err) record_err(a.err, TF_KERR_TIMEOUT);
+  tc::fence_after_sync();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, 512);
+}
+
 }  // namespace fp8
 
 size_t fp8_quantize_workspace() { return 256; }
@@ -399,13 +600,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// [rows, cols] bytes with a row stride, read in 128 x 128 boxes, SWIZZLE_128B, zero fill outside
-bool box_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t stride) {
+// [rows, cols] bytes with a row stride, read in boxes of 128 bytes x box_rows rows, SWIZZLE_128B,
+// zero fill outside
+bool box_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t stride,
+             uint32_t box_rows = 128) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {stride};
-  cuuint32_t box[2] = {(cuuint32_t)fp8::kBK, 128};
+  cuuint32_t box[2] = {(cuuint32_t)fp8::kBK, box_rows};
   cuuint32_t elem[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -414,34 +617,44 @@ bool box_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uin
 
 }  // namespace
 
+template <typename TO>
+cudaError_t gemm_t(const tf_fp8_gemm_args& a, cudaStream_t s) {
+  CUtensorMap mq, mw;
+  if (!box_map(&mq, a.q, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.q_stride))
+    return cudaErrorNotSupported;
+  // 128 x 256 tiles once they fill every SM at least once; smaller problems (decode batches) keep
+  // the 128 x 128 tiles, which give twice as many CTAs to stream the weights
+  const int sms = device_sm_count();
+  const int64_t tiles_m = (a.M + fp8::kBM - 1) / fp8::kBM;
+  const int64_t tiles_nw = (a.N + fp8::kBNW - 1) / fp8::kBNW;
+  if (tiles_m * tiles_nw >= sms && tiles_m * tiles_nw <= INT32_MAX) {
+    if (!box_map(&mw, a.w, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.w_stride, fp8::kBNW))
+      return cudaErrorNotSupported;
+    cudaError_t e = cudaFuncSetAttribute(fp8::block_gemm_wide_kernel<TO>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmemW);
+    if (e != cudaSuccess) return e;
+    const int tiles = (int)(tiles_m * tiles_nw);
+    fp8::block_gemm_wide_kernel<TO><<<tiles < sms ? tiles : sms, fp8::kThreads, fp8::kSmemW, s>>>(
+        a, mq, mw, (int)tiles_nw, tiles);
+    return cudaGetLastError();
+  }
+  if (!box_map(&mw, a.w, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.w_stride))
+    return cudaErrorNotSupported;
+  dim3 grid((a.N + fp8::kBN - 1) / fp8::kBN, (unsigned)tiles_m);
+  cudaError_t e = cudaFuncSetAttribute(fp8::block_gemm_kernel<TO>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
+  if (e != cudaSuccess) return e;
+  fp8::block_gemm_kernel<TO><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_fp8_block_gemm(const tf_fp8_gemm_args& a, cudaStream_t s) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
-  CUtensorMap mq, mw;
-  if (!box_map(&mq, a.q, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.q_stride) ||
-      !box_map(&mw, a.w, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.w_stride))
-    return cudaErrorNotSupported;
-  dim3 grid((a.N + fp8::kBN - 1) / fp8::kBN, (unsigned)((a.M + fp8::kBM - 1) / fp8::kBM));
-  cudaError_t e;
   switch (a.out_dtype) {
-    case TF_DTYPE_BF16:
-      e = cudaFuncSetAttribute(fp8::block_gemm_kernel<__nv_bfloat16>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
-      if (e != cudaSuccess) return e;
-      fp8::block_gemm_kernel<__nv_bfloat16><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
-      break;
-    case TF_DTYPE_F16:
-      e = cudaFuncSetAttribute(fp8::block_gemm_kernel<__half>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
-      if (e != cudaSuccess) return e;
-      fp8::block_gemm_kernel<__half><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
-      break;
-    default:
-      e = cudaFuncSetAttribute(fp8::block_gemm_kernel<float>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, fp8::kSmem);
-      if (e != cudaSuccess) return e;
-      fp8::block_gemm_kernel<float><<<grid, fp8::kThreads, fp8::kSmem, s>>>(a, mq, mw);
+    case TF_DTYPE_BF16: return gemm_t<__nv_bfloat16>(a, s);
+    case TF_DTYPE_F16: return gemm_t<__half>(a, s);
+    default: return gemm_t<float>(a, s);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace tf
