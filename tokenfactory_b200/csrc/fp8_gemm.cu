@@ -356,7 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_kernel(tf_fp8_gemm_arg
 // Prefill-sized M: 128 x 256 tiles, one persistent CTA per SM.  A K block of a 256-column tile
 // moves 48 KB (16 KB of q, 32 KB of w) for twice the products of a 128 x 128 tile's 32 KB, a
 // quarter less L2 -> SM traffic per product, which is what bounds the 128 x 128 kernel.  Each CTA
-// walks the tiles blockIdx.x, blockIdx.x + gridDim.x, ... (n fastest), with one running count of
+// walks the tiles blockIdx.x, blockIdx.x + gridDim.x, ... (m fastest: the CTAs resident at once
+// share a few 256-row weight blocks and re-read the activations, which stay in L2, instead of
+// streaming the whole weight matrix from DRAM once per two row blocks), with one running count of
 // K blocks for the stage ring and the accumulator pair, so the next tile's loads and first
 // products overlap the current tile's output writes.  TMEM holds two 256-column accumulators;
 // epilogue warp w reads lanes 32 (w % 4) .. +31 and the 128 columns 128 (w / 4) .. +127, the span
@@ -381,7 +383,7 @@ template <typename TO>
 __global__ void __launch_bounds__(kThreads, 1) block_gemm_wide_kernel(tf_fp8_gemm_args a,
                                                                       const __grid_constant__ CUtensorMap map_q,
                                                                       const __grid_constant__ CUtensorMap map_w,
-                                                                      int tiles_n, int tiles) {
+                                                                      int tiles_m, int tiles) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;
@@ -416,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_wide_kernel(tf_fp8_gem
       uint32_t g = 0;  // K blocks issued so far
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int n0 = (t % tiles_n) * kBNW, m0 = (t / tiles_n) * kBM;
+        const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * kBNW;
         for (int kb = 0; kb < nkb; ++kb, ++g) {
           const uint32_t s = g % kStagesW;
           if (g >= kStagesW && !wait_b(&bars->empty[s], ((g / kStagesW) - 1) & 1, abort)) {
@@ -480,8 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1) block_gemm_wide_kernel(tf_fp8_gem
     uint32_t g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      const int n0 = (t % tiles_n) * kBNW + 128 * h;  // this warp's first column
-      const int64_t m0 = (int64_t)(t / tiles_n) * kBM;
+      const int n0 = (t / tiles_m) * kBNW + 128 * h;  // this warp's first column
+      const int64_t m0 = (int64_t)(t % tiles_m) * kBM;
       // a half that starts past N has no output columns and reads no weight scale
       const float* wsrow = a.w_scale && n0 < a.N ? a.w_scale + (int64_t)(n0 / a.block_h) * a.ws_stride_n
                                                  : nullptr;
@@ -635,7 +637,7 @@ cudaError_t gemm_t(const tf_fp8_gemm_args& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const int tiles = (int)(tiles_m * tiles_nw);
     fp8::block_gemm_wide_kernel<TO><<<tiles < sms ? tiles : sms, fp8::kThreads, fp8::kSmemW, s>>>(
-        a, mq, mw, (int)tiles_nw, tiles);
+        a, mq, mw, (int)tiles_m, tiles);
     return cudaGetLastError();
   }
   if (!box_map(&mw, a.w, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.w_stride))
