@@ -658,6 +658,39 @@ __global__ void __launch_bounds__(kConvVecThreads, 6) conv4_vec_kernel(tf_gdn_ar
   const int64_t t_begin = (int64_t)blockIdx.y * kConvVecTok;
   if (t_begin >= T_all) return;
   const int n = (int)(T_all - t_begin < kConvVecTok ? T_all - t_begin : kConvVecTok);
+  const bool live = c < conv_dim;
+  // the window rows t_begin-3 .. t_begin+n-1 (rows before token 0 are never used), the taps and
+  // the bias are requested before the request lookup below, so their latency overlaps it
+  const T* x = reinterpret_cast<const T*>(a.qkv) + c;
+  uint2 win[kConvVecTok + 3];
+#pragma unroll
+  for (int r = 0; r < kConvVecTok + 3; ++r) {
+    const int64_t t = t_begin - 3 + r;
+    win[r] = (live && t >= 0 && r < n + 3) ? __ldcs(reinterpret_cast<const uint2*>(x + t * a.qkv_stride_tok))
+                                           : make_uint2(0u, 0u);
+  }
+  float w[4][4], bias[4];
+  const T* wt = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)(live ? c : 0) * 4;
+  const T* cb = reinterpret_cast<const T*>(a.conv_bias);
+  if ((reinterpret_cast<uintptr_t>(a.conv_weight) & 15) == 0) {  // 4 channels x 4 taps: 32 bytes
+    const uint4 w01 = __ldg(reinterpret_cast<const uint4*>(wt));
+    const uint4 w23 = __ldg(reinterpret_cast<const uint4*>(wt) + 1);
+    const uint32_t wv[8] = {w01.x, w01.y, w01.z, w01.w, w23.x, w23.y, w23.z, w23.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      w[e][0] = unpack_lo<T>(wv[2 * e]);
+      w[e][1] = unpack_hi<T>(wv[2 * e]);
+      w[e][2] = unpack_lo<T>(wv[2 * e + 1]);
+      w[e][3] = unpack_hi<T>(wv[2 * e + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) w[e][j] = to_f(wt[e * 4 + j]);
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) bias[e] = cb && live ? to_f(cb[c + e]) : 0.f;
   __shared__ int s_b;
   if (threadIdx.x == 0) {  // request of the block's first token
     int lo = 0, hi = a.batch_size - 1;
@@ -668,25 +701,7 @@ __global__ void __launch_bounds__(kConvVecThreads, 6) conv4_vec_kernel(tf_gdn_ar
     s_b = lo;
   }
   __syncthreads();
-  if (c >= conv_dim) return;
-  const T* x = reinterpret_cast<const T*>(a.qkv) + c;
-  // window rows t_begin-3 .. t_begin+n-1 (rows before token 0 are never used)
-  uint2 win[kConvVecTok + 3];
-#pragma unroll
-  for (int r = 0; r < kConvVecTok + 3; ++r) {
-    const int64_t t = t_begin - 3 + r;
-    win[r] = (t >= 0 && r < n + 3) ? __ldcs(reinterpret_cast<const uint2*>(x + t * a.qkv_stride_tok))
-                                   : make_uint2(0u, 0u);
-  }
-  float w[4][4], bias[4];
-  const T* wt = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * 4;
-  const T* cb = reinterpret_cast<const T*>(a.conv_bias);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[e][j] = to_f(wt[e * 4 + j]);
-    bias[e] = cb ? to_f(cb[c + e]) : 0.f;
-  }
+  if (!live) return;
   int b = s_b;
   int64_t rs = start[b], re = start[b + 1];
 #pragma unroll
