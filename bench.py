@@ -240,7 +240,7 @@ def _decode_bytes(lens, lq, lkv, D):
 def bench_decode(args, rank, world, dev):
     from tokenfactory_b200 import ops
 
-    inp = _decode_inputs(0, rank, world, dev)
+    inp = _decode_inputs(0, rank, args.head_split or world, dev)
     B, D = C2["B"], C2["D"]
     lens_d = inp["lens"].to(dev)
     r2t_d = inp["r2t"].to(dev)
@@ -1132,6 +1132,9 @@ def main():
     ap.add_argument("--c5-layers", type=int, default=C5["layers"], help="config 5: layers")
     ap.add_argument("--decode-only", action="store_true",
                     help="config 2 without the config 3 / config 4 legs that the default line carries")
+    ap.add_argument("--head-split", type=int, default=0,
+                    help="profiling only: config 2's decode on the heads rank 0 owns in an N-GPU "
+                         "run, timed on this one GPU")
     args = ap.parse_args()
     C2["B"], C2["slots"] = args.batch, args.pool_slots
     args.warmup = max(3, args.warmup)

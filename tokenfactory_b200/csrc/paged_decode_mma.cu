@@ -62,6 +62,8 @@ struct Cfg {
 
 struct Ws {
   int32_t* status;
+  int64_t* cta_g;       // [nctas+1] first tile of each CTA's range (the last entry: the total)
+  int32_t* cta_b;       // [nctas][2] first and last request a CTA's range touches
   int32_t* tile_start;  // [B+1]
   float* part_ml;       // [2*nctas][kHeads][2]  (max in log2 domain, sum)
   float* part_o;        // [2*nctas][kHeads][D]
@@ -74,6 +76,10 @@ __host__ __device__ inline Ws carve(void* base, int B, int nctas, int D) {
   Ws w;
   w.status = (int32_t*)p;
   p += 256;
+  w.cta_g = (int64_t*)p;
+  p += align256((size_t)(nctas + 1) * 8);
+  w.cta_b = (int32_t*)p;
+  p += align256((size_t)2 * nctas * 4);
   w.tile_start = (int32_t*)p;
   p += align256((size_t)(B + 1) * 4);
   w.part_ml = (float*)p;
@@ -83,23 +89,54 @@ __host__ __device__ inline Ws carve(void* base, int B, int nctas, int D) {
 }
 
 inline size_t ws_bytes(int B, int nctas, int D) {
-  return 256 + align256((size_t)(B + 1) * 4) + align256((size_t)2 * nctas * kHeads * 2 * 4) +
+  return 256 + align256((size_t)(nctas + 1) * 8) + align256((size_t)2 * nctas * 4) +
+         align256((size_t)(B + 1) * 4) + align256((size_t)2 * nctas * kHeads * 2 * 4) +
          (size_t)2 * nctas * kHeads * D * 4;
 }
 
 // ---------------------------------------------------------------------------------------------
-// plan: tile_start[b] = sum_{b'<b} ceil(seq_lens[b'] / kTileTok)
+// plan: tile_start[b] = sum_{b'<b} ceil(seq_lens[b'] / kTileTok), then the CTAs' ranges.
+//
+// The work is the sequence of (request, kv head) units in request order, each ceil(len / kTileTok)
+// tiles; a CTA takes a contiguous range of it, and a unit cut by range boundaries is merged by the
+// combine kernel.  Besides its tiles, every piece of a unit that a CTA runs costs a fixed amount:
+// its Q rows, the first slot and K/V round trips and the cross-warp epilogue (measured on config 2:
+// CTA time = 290 us + 10.8 us per piece at 944 tiles, i.e. a piece ~ 35 tiles; 8.1 us ~ 25 tiles
+// on the heads of one rank of four).  Ranges of equal tile counts therefore finish up to 25% apart
+// when one CTA's range holds many short requests; the plan balances tiles + kPieceCost per unit
+// instead.  Boundaries are strictly increasing (every CTA has at least one tile).  Batches of more
+// than kPlanSmemReqs requests keep equal tile counts.
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int B,
-                                                    int64_t max_len, int32_t* tile_start) {
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanSmemReqs = 8192;
+constexpr int kPlanMaxCtas = 1024;
+template <int D> struct PieceCost { static constexpr int64_t v = D >= 256 ? 32 : (D >= 128 ? 48 : 64); };
+
+// first b with ts[b+1] * Hkv > g (b in [0, B-1])
+__device__ int first_req_after(const int32_t* ts, int B, int Hkv, int64_t g) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((int64_t)ts[mid + 1] * Hkv > g) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* seq_lens, int B,
+                                                            int64_t max_len, int Hkv,
+                                                            int nctas_launched, int64_t piece_cost,
+                                                            Ws ws) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
+  __shared__ int32_t ts_s[kPlanSmemReqs + 1];
+  __shared__ int64_t cg[kPlanMaxCtas + 1];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // the decode grid may be launched now: its CTAs wait for this grid before reading the plan
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const bool small = B <= kPlanSmemReqs;
   if (tid == 0) carry = 0;
   __syncthreads();
-  for (int b0 = 0; b0 < B; b0 += 1024) {
+  for (int b0 = 0; b0 < B; b0 += kPlanThreads) {
     const int b = b0 + tid;
     int64_t L = b < B ? seq_lens[b] : 0;
     if (L < 0) L = 0;
@@ -125,12 +162,70 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int64_t* seq_lens, int
     }
     __syncthreads();
     const int32_t excl = carry + warp_tot[warp] + incl - v;
-    if (b < B) tile_start[b] = excl;
+    if (b < B) {
+      ws.tile_start[b] = excl;
+      if (small) ts_s[b] = excl;
+    }
     __syncthreads();
-    if (tid == 1023) carry = excl + v;
+    if (tid == kPlanThreads - 1) carry = excl + v;
     __syncthreads();
   }
-  if (tid == 0) tile_start[B] = carry;
+  if (tid == 0) {
+    ws.tile_start[B] = carry;
+    if (small) ts_s[B] = carry;
+  }
+  __syncthreads();  // the tile starts (shared and, for this CTA, global) are complete
+  const int32_t* ts = small ? ts_s : ws.tile_start;
+  const int64_t total = (int64_t)carry * Hkv;
+  const int nctas = (int64_t)nctas_launched < total ? nctas_launched : (int)total;
+  if (nctas <= 0) return;
+  const int64_t beta = small ? piece_cost : 0;
+  const int64_t U = (int64_t)B * Hkv;
+  const int64_t ctot = total + beta * U;
+  auto unit_start = [&](int64_t u) -> int64_t {  // first tile of unit u
+    const int b = (int)(u / Hkv), h = (int)(u - (int64_t)b * Hkv);
+    return (int64_t)ts[b] * Hkv + (int64_t)h * (ts[b + 1] - ts[b]);
+  };
+  for (int c = tid; c <= nctas; c += kPlanThreads) {
+    int64_t g;
+    if (c == nctas) {
+      g = total;
+    } else if (beta == 0) {
+      g = (int64_t)c * total / nctas;
+    } else {
+      // cost position x: the unit u whose [cost start, next cost start) holds it, where a unit's
+      // cost start is its first tile + beta * u; its first beta of cost is the piece's fixed part
+      const int64_t x = (int64_t)c * ctot / nctas;
+      int64_t lo = 0, hi = U - 1;
+      while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (unit_start(mid) + beta * mid <= x) lo = mid; else hi = mid - 1;
+      }
+      const int b = (int)(lo / Hkv);
+      const int64_t gs = unit_start(lo), nt = ts[b + 1] - ts[b];
+      int64_t off = x - gs - beta * lo - beta;
+      off = off < 0 ? 0 : (off > nt ? nt : off);
+      g = gs + off;
+    }
+    cg[c] = g;
+  }
+  __syncthreads();
+  if (tid == 0) {  // strictly increasing: every CTA gets at least one tile
+    cg[0] = 0;
+    for (int c = 1; c < nctas; ++c)
+      if (cg[c] <= cg[c - 1]) cg[c] = cg[c - 1] + 1;
+    cg[nctas] = total;
+    for (int c = nctas - 1; c >= 1; --c)
+      if (cg[c] >= cg[c + 1]) cg[c] = cg[c + 1] - 1;
+  }
+  __syncthreads();
+  for (int c = tid; c <= nctas; c += kPlanThreads) {
+    ws.cta_g[c] = cg[c];
+    if (c < nctas) {
+      ws.cta_b[2 * c] = first_req_after(ts, B, Hkv, cg[c]);
+      ws.cta_b[2 * c + 1] = first_req_after(ts, B, Hkv, cg[c + 1] - 1);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -163,16 +258,6 @@ struct Meta {
   }
 };
 
-// first b with ts[b+1] * Hkv > g (b in [0, B-1])
-__device__ int first_req_after(const int32_t* ts, int B, int Hkv, int64_t g) {
-  int lo = 0, hi = B - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if ((int64_t)ts[mid + 1] * Hkv > g) hi = mid; else lo = mid + 1;
-  }
-  return lo;
-}
-
 struct Piece {
   int b, h, t0, n;  // tiles [t0, t0+n) of unit (b, h)
   int nt;           // tiles of the whole unit
@@ -204,8 +289,14 @@ struct Walker {
   }
 };
 
-__device__ __forceinline__ int64_t cta_range(int c, int64_t total, int nctas) {
-  return (int64_t)c * total / nctas;
+// the CTA whose range [cg[c], cg[c+1]) holds tile g (cg strictly increasing, cg[0] = 0)
+__device__ __forceinline__ int cta_of(const int64_t* cg, int nctas, int64_t g) {
+  int lo = 0, hi = nctas - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cg[mid] <= g) lo = mid; else hi = mid - 1;
+  }
+  return lo;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -273,11 +364,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nctas = (int64_t)nctas_launched < total ? nctas_launched : (int)total;
   const int c = blockIdx.x;
   if (c >= nctas) return;
-  const int64_t g0 = cta_range(c, total, nctas), g1 = cta_range(c + 1, total, nctas);
+  const int64_t g0 = ws.cta_g[c], g1 = ws.cta_g[c + 1];  // the plan's range and its requests
 
   if (tid == 0) {
-    const int bf = first_req_after(ws.tile_start, B, Hkv, g0);
-    const int bl = first_req_after(ws.tile_start, B, Hkv, g1 - 1);
+    const int bf = ws.cta_b[2 * c], bl = ws.cta_b[2 * c + 1];
     rc->bf = bf;
     rc->n = min(bl - bf + 1, kMaxCachedReqs);
   }
@@ -497,12 +587,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws ws,
                                                       int nctas_launched) {
-  // w[nctas][kHeads], ml[nctas][kHeads][2], then int sl[nctas], ts[B+1]
-  extern __shared__ float csm[];
+  // int64 cg[nctas+1], then w[nctas][kHeads], ml[nctas][kHeads][2], int sl[nctas], ts[B+1]
+  extern __shared__ __align__(16) float csm[];
   const int B = a.batch_size, Hkv = a.num_kv_heads;
   const int G = a.num_q_heads / Hkv;
   const int tid = threadIdx.x;
-  float* w = csm;
+  int64_t* cgs = reinterpret_cast<int64_t*>(csm);
+  float* w = reinterpret_cast<float*>(cgs + nctas_launched + 1);
   float* ml = w + nctas_launched * kHeads;
   int* sl = reinterpret_cast<int*>(ml + nctas_launched * kHeads * 2);
   int* ts = sl + nctas_launched;
@@ -520,20 +611,21 @@ __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws w
   }
   const int64_t total = (int64_t)ts[B] * Hkv;
   const int nctas = (int64_t)nctas_launched < total ? nctas_launched : (int)total;
+  for (int i = tid; i <= nctas; i += blockDim.x) cgs[i] = ws.cta_g[i];
+  __syncthreads();
   const int c = blockIdx.x;
   if (c == 0 || c >= nctas) return;
-  const int64_t g = cta_range(c, total, nctas);
+  const int64_t g = cgs[c];  // this CTA's boundary: the unit cut there, merged if this is its first cut
   const int b = first_req_after(ts, B, Hkv, g);
   const int nt = ts[b + 1] - ts[b];
   const int h = (int)((g - (int64_t)ts[b] * Hkv) / nt);
   const int64_t su = (int64_t)ts[b] * Hkv + (int64_t)h * nt, eu = su + nt;
-  const int c0 = (int)(((su + 1) * nctas - 1) / total);
-  const int c1 = (int)((eu * nctas - 1) / total);
+  const int c0 = cta_of(cgs, nctas, su), c1 = cta_of(cgs, nctas, eu - 1);
   if (c0 == c1 || c != c0 + 1) return;  // finished inside one CTA, or merged at its first boundary
   const int np = c1 - c0 + 1;
   for (int i = tid; i < np; i += blockDim.x) {
     const int cc = c0 + i;
-    const int64_t rc = cta_range(cc, total, nctas);
+    const int64_t rc = cgs[cc];
     sl[i] = 2 * cc + ((su > rc ? su : rc) == rc ? 0 : 1);
   }
   // everything above reads only the plan; the decode grid's partials are complete and visible
@@ -604,17 +696,21 @@ __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws w
 template <int D>
 static cudaError_t launch_d(const tf_paged_attn_args& a, void* wsp, int nctas, cudaStream_t s) {
   Ws ws = carve(wsp, a.batch_size, nctas, D);
-  // a unit spans at most every CTA: the combine holds weights [nctas][kHeads], (max, sum)
-  // [nctas][kHeads][2] and slot ids [nctas], then the schedule tile_start[B+1]; checked before
-  // the first launch so that a batch it cannot hold leaves nothing enqueued
-  const size_t csmem = (size_t)nctas * (3 * kHeads * 4 + 4) + (size_t)(a.batch_size + 1) * 4;
+  // a unit spans at most every CTA: the combine holds the CTA boundaries [nctas+1], weights
+  // [nctas][kHeads], (max, sum) [nctas][kHeads][2] and slot ids [nctas], then the schedule
+  // tile_start[B+1]; checked before the first launch so that a batch it cannot hold leaves nothing
+  // enqueued
+  const size_t csmem = (size_t)(nctas + 1) * 8 + (size_t)nctas * (3 * kHeads * 4 + 4) +
+                       (size_t)(a.batch_size + 1) * 4;
+  if (nctas > kPlanMaxCtas) return cudaErrorInvalidValue;
   if (csmem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
   if (e != cudaSuccess) return e;
-  plan_kernel<<<1, 1024, 0, s>>>(a.seq_lens, a.batch_size, a.r2t_cols, ws.tile_start);
+  plan_kernel<<<1, kPlanThreads, 0, s>>>(a.seq_lens, a.batch_size, a.r2t_cols, a.num_kv_heads, nctas,
+                                         PieceCost<D>::v, ws);
   // the decode CTAs are scheduled while the plan runs and wait for it before their first read
   cudaLaunchAttribute dep[1];
   dep[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
