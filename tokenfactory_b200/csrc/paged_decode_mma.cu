@@ -109,7 +109,7 @@ inline size_t ws_bytes(int B, int nctas, int D) {
 // ---------------------------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanSmemReqs = 8192;
-constexpr int kPlanMaxCtas = 1024;
+constexpr int kPlanMaxCtas = kPlanThreads - 1;  // one thread per boundary in the fix-up scan
 template <int D> struct PieceCost { static constexpr int64_t v = D >= 256 ? 32 : (D >= 128 ? 48 : 64); };
 
 // first b with ts[b+1] * Hkv > g (b in [0, B-1])
@@ -210,13 +210,35 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* seq_l
     cg[c] = g;
   }
   __syncthreads();
-  if (tid == 0) {  // strictly increasing: every CTA gets at least one tile
-    cg[0] = 0;
-    for (int c = 1; c < nctas; ++c)
-      if (cg[c] <= cg[c - 1]) cg[c] = cg[c - 1] + 1;
-    cg[nctas] = total;
-    for (int c = nctas - 1; c >= 1; --c)
-      if (cg[c] >= cg[c + 1]) cg[c] = cg[c + 1] - 1;
+  {  // strictly increasing, every CTA at least one tile: f[c] = c + max_{k <= c}(cg[k] - k) (a
+     // prefix maximum; cg[0] = 0), then min(f[c], total - nctas + c), and cg[nctas] = total
+    __shared__ int64_t wmax[32];
+    const int c = tid;
+    int64_t v = c <= nctas ? cg[c] - c : INT64_MIN;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v = v > y ? v : y;
+    }
+    if (lane == 31) wmax[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int64_t wv = wmax[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, wv, o);
+        if (lane >= o) wv = wv > y ? wv : y;
+      }
+      const int64_t prev = __shfl_up_sync(0xffffffffu, wv, 1);
+      wmax[lane] = lane == 0 ? INT64_MIN : prev;  // max over the warps before this one
+    }
+    __syncthreads();
+    if (c <= nctas) {
+      const int64_t before = wmax[warp];
+      const int64_t f = (int64_t)c + (v > before ? v : before);
+      const int64_t cap = total - nctas + c;
+      cg[c] = c == nctas ? total : (f < cap ? f : cap);
+    }
   }
   __syncthreads();
   for (int c = tid; c <= nctas; c += kPlanThreads) {
