@@ -151,6 +151,41 @@ def test_decode_batch_beyond_the_tensor_core_schedule():
     assert_close(values(out, "bf16"), want.cpu().numpy(), "bf16", what="decode B=60000")
 
 
+@pytest.mark.parametrize("B,lmax,d,hkv", [(9000, 40, 64, 2), (8192, 300, 128, 1)])
+def test_decode_large_batch_schedules(B, lmax, d, hkv):
+    """Batches of up to 8192 requests compute their cost-balanced schedule in every decode and
+    combine CTA; above that a 1-CTA plan kernel computes equal tile ranges once (9,000 requests,
+    lengths up to 40: many requests per CTA range, ranges cut inside requests).  Both against a
+    vectorised fp32 torch evaluation of the reference's batched decode
+    (qwen3_8/full_attention.py:215-242), with lengths of 0 (NaN rows) among them."""
+    from tokenfactory_b200 import ops
+    hq = 8 * hkv
+    g = torch.Generator(device="cuda").manual_seed(B + lmax)
+    lens = torch.randint(1, lmax + 1, (B,), generator=g, device="cuda")
+    lens[::997] = 0
+    slots = B * lmax + 1
+    r2t = (torch.randperm(slots - 1, generator=g, device="cuda") + 1)[:B * lmax].view(B, lmax)
+    r2t = torch.where(torch.arange(lmax, device="cuda")[None] < lens[:, None], r2t, -1)
+    kb = torch.randn((slots, hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    vb = torch.randn((slots, hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn((B, hq, d), generator=g, device="cuda").to(torch.bfloat16)
+    rpi = torch.arange(B, device="cuda")
+    out = ops.paged_decode(q, kb, vb, r2t, rpi, lens, d ** -0.5, lmax)
+    idx = r2t.clamp(min=0)
+    k = kb[idx].float()                               # [B, L, Hkv, D]
+    v = vb[idx].float()
+    qh = q.float().view(B, hkv, hq // hkv, d)
+    s = torch.einsum("bkgd,blkd->bkgl", qh, k) * d ** -0.5
+    s = s.masked_fill(torch.arange(lmax, device="cuda")[None, None, None] >= lens[:, None, None, None],
+                      float("-inf"))
+    want = torch.einsum("bkgl,blkd->bkgd", torch.softmax(s, -1), v).reshape(B, hq, d)
+    torch.cuda.synchronize()
+    got = values(out, "bf16").reshape(B, hq, d)
+    empty = (lens == 0).cpu().numpy()
+    assert np.isnan(got[empty]).all()
+    assert_close(got[~empty], want.cpu().numpy()[~empty], "bf16", what=f"decode B={B}")
+
+
 def test_decode_request_without_keys_gives_nan_rows():
     """A request with no keys (seq_len 0) among others: its output rows are NaN, as the
     reference's softmax over an empty row, and the other rows match the batch where it has keys

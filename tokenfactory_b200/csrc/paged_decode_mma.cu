@@ -111,6 +111,10 @@ constexpr int kPlanThreads = 1024;
 constexpr int kPlanSmemReqs = 8192;
 constexpr int kPlanMaxCtas = kPlanThreads - 1;  // one thread per boundary in the fix-up scan
 template <int D> struct PieceCost { static constexpr int64_t v = D >= 256 ? 32 : (D >= 128 ? 48 : 64); };
+// The decode CTA that the plan kernel's SM receives starts when the plan ends (the other SMs take
+// theirs at once: CTAs are dispatched in index order, so it is the last one): the last range is
+// shortened by about the plan's duration in tiles (4-5 us, at 0.31-0.38 us per tile).
+constexpr int64_t kPlanLagTiles = 12;
 
 // first b with ts[b+1] * Hkv > g (b in [0, B-1])
 __device__ int first_req_after(const int32_t* ts, int B, int Hkv, int64_t g) {
@@ -182,8 +186,9 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* seq_l
   const int64_t beta = small ? piece_cost : 0;
   const int64_t U = (int64_t)B * Hkv;
   const int64_t ctot = total + beta * U;
-  auto unit_start = [&](int64_t u) -> int64_t {  // first tile of unit u
-    const int b = (int)(u / Hkv), h = (int)(u - (int64_t)b * Hkv);
+  const int64_t lag = small ? kPlanLagTiles : 0;
+  auto unit_start = [&](int64_t u) -> int64_t {  // first tile of unit u (u < 2^31 here: B is small)
+    const int b = (int)u / Hkv, h = (int)u - b * Hkv;
     return (int64_t)ts[b] * Hkv + (int64_t)h * (ts[b + 1] - ts[b]);
   };
   for (int c = tid; c <= nctas; c += kPlanThreads) {
@@ -195,13 +200,13 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* seq_l
     } else {
       // cost position x: the unit u whose [cost start, next cost start) holds it, where a unit's
       // cost start is its first tile + beta * u; its first beta of cost is the piece's fixed part
-      const int64_t x = (int64_t)c * ctot / nctas;
+      const int64_t x = (int64_t)c * (ctot + lag) / nctas;
       int64_t lo = 0, hi = U - 1;
       while (lo < hi) {
         const int64_t mid = (lo + hi + 1) >> 1;
         if (unit_start(mid) + beta * mid <= x) lo = mid; else hi = mid - 1;
       }
-      const int b = (int)(lo / Hkv);
+      const int b = (int)lo / Hkv;
       const int64_t gs = unit_start(lo), nt = ts[b + 1] - ts[b];
       int64_t off = x - gs - beta * lo - beta;
       off = off < 0 ? 0 : (off > nt ? nt : off);
