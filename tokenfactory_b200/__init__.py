@@ -16,7 +16,15 @@ Layers:
   forward_batch             - ForwardBatch with the reference's fields
 """
 
-from . import ops  # noqa: F401
 from .forward_batch import ForwardBatch  # noqa: F401
 
 __all__ = ["ops", "ForwardBatch"]
+
+
+def __getattr__(name):
+    # ops loads the compiled extension; it is imported on first use, so that the package (and
+    # its build module, `python -m tokenfactory_b200.build`) imports before anything is built
+    if name == "ops":
+        import importlib
+        return importlib.import_module(__name__ + ".ops")
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
