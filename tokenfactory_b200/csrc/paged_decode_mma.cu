@@ -110,6 +110,9 @@ inline size_t ws_bytes(int B, int nctas, int D) {
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanSmemReqs = 8192;
 constexpr int kPlanMaxCtas = kPlanThreads - 1;  // one thread per boundary in the fix-up scan
+// kPieceCost in tiles: 32 at head_dim 256 (between the two fits above); smaller heads make a tile
+// cheaper and leave most of a piece's latency-bound cost, so it is set higher there (48 at 128,
+// 64 at 64: scaled, not measured)
 template <int D> struct PieceCost { static constexpr int64_t v = D >= 256 ? 32 : (D >= 128 ? 48 : 64); };
 // The decode CTA that the plan kernel's SM receives starts when the plan ends (the other SMs take
 // theirs at once: CTAs are dispatched in index order, so it is the last one): the last range is
@@ -695,17 +698,28 @@ __global__ void __launch_bounds__(256) combine_kernel(tf_paged_attn_args a, Ws w
     }
   }
   __syncthreads();
-  for (int i = 0; i < np; ++i) {
-    float po[kPer];
+  // up to four pieces' partial sums requested together, then added in piece order
+  constexpr int kBatch = 4;
+  for (int i0 = 0; i0 < np; i0 += kBatch) {
+    float po[kBatch][kPer];
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int e = tid + k * 256;
-      if (e < G * D) po[k] = ws.part_o[((int64_t)sl[i] * kHeads + e / D) * D + (e - (e / D) * D)];
+    for (int j = 0; j < kBatch; ++j) {
+      if (i0 + j >= np) break;
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int e = tid + k * 256;
+        if (e < G * D)
+          po[j][k] = ws.part_o[((int64_t)sl[i0 + j] * kHeads + e / D) * D + (e - (e / D) * D)];
+      }
     }
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int e = tid + k * 256;
-      if (e < G * D) o[k] = fmaf(w[i * kHeads + e / D], po[k], o[k]);
+    for (int j = 0; j < kBatch; ++j) {
+      if (i0 + j >= np) break;
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int e = tid + k * 256;
+        if (e < G * D) o[k] = fmaf(w[(i0 + j) * kHeads + e / D], po[j][k], o[k]);
+      }
     }
   }
 #pragma unroll
