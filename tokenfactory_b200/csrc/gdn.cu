@@ -1417,6 +1417,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
   uint64_t* sreq = bars + 12;          // U'0 (the solved first 32 tokens) is in TMEM
   uint64_t* sdone = bars + 13;         // E = U'0 Mk10^T is in TMEM
   uint64_t* p2s = bars + 14;           // a chunk's state-update MMAs (S' += U'' K) have completed
+                                       // (p2 of the chunk's parity: all its phase-2 MMAs)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sb + oWords);
   volatile int* abort = reinterpret_cast<volatile int*>(sb + oWords + 4);
 
@@ -1768,17 +1769,23 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
         tc::fence_proxy_async_smem();
         // O' += U' Mq^T (N = 64 tokens, hi.hi + hi.lo + lo.hi) and S' += U'' K (N = 128 dk, the
         // raw K rows MN-major; U'' = U' e^(gamma_C - gamma) / |k| as hi + lo over cX)
+        // the state update first, committed on its own (p2s): the lanes split S' while the output
+        // products run; p2 then completes once every phase-2 product has
+#pragma unroll 1
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t aK = tmem + cX + (part ? 32 : 0);
+#pragma unroll
+          for (int kk = 0; kk < C / 16; ++kk)
+            mma_ts(tmem + cS, aK + kk * 8, tc::sw128_desc(kq + kk * 2048, kKQBlk, 1024), idS, true);
+        }
+        tc::commit(p2s);
 #pragma unroll 1
         for (int part = 0; part < 3; ++part) {
           const uint32_t aT = tmem + (part == 2 ? cUL : cUH);
           const uint32_t mq = base + (part == 1 ? oMqL : oMqH);
-          const uint32_t aK = tmem + cX + (part == 2 ? 32 : 0);
 #pragma unroll
-          for (int kk = 0; kk < C / 16; ++kk) {
+          for (int kk = 0; kk < C / 16; ++kk)
             mma_ts(tmem + cZ, aT + kk * 8, tc::sw128_desc(mq + kk * 32, 16, 1024), idO, true);
-            if (part != 1)
-              mma_ts(tmem + cS, aK + kk * 8, tc::sw128_desc(kq + kk * 2048, kKQBlk, 1024), idS, true);
-          }
         }
         tc::commit(p2 + bf);
       }
@@ -1996,12 +2003,27 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
       tc::fence_proxy_async_smem();  // Mq is read by the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(l1);
+      // ---- S' hi / lo for the next chunk once the state update has completed (the output
+      //      products may still run), then O' rounded to T into the transposed output rows; then
+      //      the next chunk's products start while the loaders write the output rows
+      ok = bar_and(1, 128, waitb(p2s, ci & 1, abort));
+      if (!ok) break;
+      tc::fence_after_sync();
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float sv[32];
+        tc::ld32(lb + cS + 32 * cc, sv);
+        tc::wait_ld();
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) split2(sv[2 * k], sv[2 * k + 1], hi[k], lo[k]);
+        st16u(lb + cSH + 16 * cc, hi);
+        st16u(lb + cSL + 16 * cc, lo);
+      }
       // the previous chunk's output rows are written by the loaders before O' replaces them
       ok = bar_and(1, 128, waitb(p2 + bf, (ci >> 1) & 1, abort) && waitb(chunk_free, ci & 1, abort));
       if (!ok) break;
       tc::fence_after_sync();
-      // ---- O' rounded to T into the transposed output rows, S' hi / lo for the next chunk; then
-      //      the next chunk's products start while the loaders write the output rows
       T* ot = reinterpret_cast<T*>(sb + oOT);
       {
         float o[32];
@@ -2011,17 +2033,6 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_tc_kernel(tf_gdn_args a, co
           tc::wait_ld();
 #pragma unroll
           for (int k = 0; k < 32; ++k) ot[(32 * h + k) * D + l] = from_f<T>(o[k]);
-        }
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          float sv[32];
-          tc::ld32(lb + cS + 32 * cc, sv);
-          tc::wait_ld();
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) split2(sv[2 * k], sv[2 * k + 1], hi[k], lo[k]);
-          st16u(lb + cSH + 16 * cc, hi);
-          st16u(lb + cSL + 16 * cc, lo);
         }
       }
       tc::wait_st();
