@@ -637,40 +637,42 @@ __global__ void __launch_bounds__(kConvThreads) conv4_tiled_kernel(tf_gdn_args a
   }
 }
 
-// K = 4 conv for 16-bit activations with 8-byte rows: a thread takes 4 channels of a 16-token
-// block and issues the loads of the whole window (3 history rows + 16 rows) before any
-// arithmetic, so 19 independent loads are in flight per thread.  Same FMA order and roundings
-// as conv4_tiled_kernel; SiLU with a hardware exponential and an approximate division (the result
-// is rounded to the 16-bit type, where the two differ in rare last-place cases).
+// K = 4 conv for 16-bit activations with 8-byte rows (4 channels per thread).  Same FMA order and
+// roundings as conv4_tiled_kernel; SiLU with a hardware exponential and an approximate division
+// (the result is rounded to the 16-bit type, where the two differ in rare last-place cases).
 constexpr int kConvVecTok = 8;
 constexpr int kConvVecThreads = 128;
 
 __device__ __forceinline__ float silu_rt(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// Sliding window: a thread takes 4 channels of kConvPipeBlocks consecutive 8-token blocks.  The
+// next block's 8 new rows are requested before the current block is computed (the 3 rows before
+// them are the current window's last), so every warp keeps loads in flight while it computes, and
+// each row is loaded once per thread (one 11-row window per block measured 240 us against 215 us
+// at config 4).
+constexpr int kConvPipeBlocks = 8;
+
 template <typename T>
-__global__ void __launch_bounds__(kConvVecThreads, 6) conv4_vec_kernel(tf_gdn_args a,
-                                                                       const int64_t* start,
-                                                                       T* conv_out) {
+__global__ void __launch_bounds__(kConvVecThreads, 5) conv4_pipe_kernel(tf_gdn_args a,
+                                                                        const int64_t* start,
+                                                                        T* conv_out) {
   static_assert(sizeof(T) == 2, "16-bit activations");
   const int conv_dim = 2 * a.num_k_heads * a.head_k_dim + a.num_v_heads * a.head_v_dim;
   const int c = (blockIdx.x * kConvVecThreads + threadIdx.x) * 4;
+  if (c >= conv_dim) return;  // no barrier in this kernel
   const int64_t T_all = start[a.batch_size] < a.num_tokens ? start[a.batch_size] : a.num_tokens;
-  const int64_t t_begin = (int64_t)blockIdx.y * kConvVecTok;
-  if (t_begin >= T_all) return;
-  const int n = (int)(T_all - t_begin < kConvVecTok ? T_all - t_begin : kConvVecTok);
-  const bool live = c < conv_dim;
-  // the window rows t_begin-3 .. t_begin+n-1 (rows before token 0 are never used), the taps and
-  // the bias are requested before the request lookup below, so their latency overlaps it
+  const int64_t t0 = (int64_t)blockIdx.y * (kConvVecTok * kConvPipeBlocks);
+  if (t0 >= T_all) return;
   const T* x = reinterpret_cast<const T*>(a.qkv) + c;
-  uint2 win[kConvVecTok + 3];
+  auto row = [&](int64_t t) -> uint2 {
+    return (t >= 0 && t < T_all) ? __ldcs(reinterpret_cast<const uint2*>(x + t * a.qkv_stride_tok))
+                                 : make_uint2(0u, 0u);
+  };
+  uint2 win[kConvVecTok + 3];  // rows tb-3 .. tb+7 of the current block
 #pragma unroll
-  for (int r = 0; r < kConvVecTok + 3; ++r) {
-    const int64_t t = t_begin - 3 + r;
-    win[r] = (live && t >= 0 && r < n + 3) ? __ldcs(reinterpret_cast<const uint2*>(x + t * a.qkv_stride_tok))
-                                           : make_uint2(0u, 0u);
-  }
+  for (int r = 0; r < kConvVecTok + 3; ++r) win[r] = row(t0 - 3 + r);
   float w[4][4], bias[4];
-  const T* wt = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)(live ? c : 0) * 4;
+  const T* wt = reinterpret_cast<const T*>(a.conv_weight) + (int64_t)c * 4;
   const T* cb = reinterpret_cast<const T*>(a.conv_bias);
   if ((reinterpret_cast<uintptr_t>(a.conv_weight) & 15) == 0) {  // 4 channels x 4 taps: 32 bytes
     const uint4 w01 = __ldg(reinterpret_cast<const uint4*>(wt));
@@ -690,64 +692,73 @@ __global__ void __launch_bounds__(kConvVecThreads, 6) conv4_vec_kernel(tf_gdn_ar
       for (int j = 0; j < 4; ++j) w[e][j] = to_f(wt[e * 4 + j]);
   }
 #pragma unroll
-  for (int e = 0; e < 4; ++e) bias[e] = cb && live ? to_f(cb[c + e]) : 0.f;
-  __shared__ int s_b;
-  if (threadIdx.x == 0) {  // request of the block's first token
+  for (int e = 0; e < 4; ++e) bias[e] = cb ? to_f(cb[c + e]) : 0.f;
+  int b;  // request of the first token (start[] is small and stays in cache)
+  {
     int lo = 0, hi = a.batch_size - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (start[mid] <= t_begin) lo = mid; else hi = mid - 1;
+      if (start[mid] <= t0) lo = mid; else hi = mid - 1;
     }
-    s_b = lo;
+    b = lo;
   }
-  __syncthreads();
-  if (!live) return;
-  int b = s_b;
   int64_t rs = start[b], re = start[b + 1];
+#pragma unroll 1
+  for (int k = 0; k < kConvPipeBlocks; ++k) {
+    const int64_t tb = t0 + (int64_t)k * kConvVecTok;
+    if (tb >= T_all) break;
+    uint2 nxt[kConvVecTok];  // the next block's new rows, in flight while this block computes
+    const bool more = k + 1 < kConvPipeBlocks;
 #pragma unroll
-  for (int i = 0; i < kConvVecTok; ++i) {
-    if (i >= n) break;
-    const int64_t t = t_begin + i;
-    while (t >= re) {  // next request (uniform over the CTA)
-      ++b;
-      rs = re;
-      re = start[b + 1];
-    }
-    float h[3][4];
+    for (int r = 0; r < kConvVecTok; ++r) nxt[r] = more ? row(tb + kConvVecTok + r) : make_uint2(0u, 0u);
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {  // history rows t-3+k
-      const T* hv = reinterpret_cast<const T*>(&win[i + k]);
+    for (int i = 0; i < kConvVecTok; ++i) {
+      const int64_t t = tb + i;
+      if (t >= T_all) break;
+      while (t >= re) {  // next request
+        ++b;
+        rs = re;
+        re = start[b + 1];
+      }
+      float h[3][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) h[k][e] = to_f(hv[e]);
-    }
-    if (t - rs < 3) {  // the first tokens of a request read its conv_state
-      const int64_t slot = a.req_pool_indices[b];
-      const bool ok = slot >= 0 && slot < a.num_slots;
-      if (!ok && c == 0) record_err(a.err, TF_KERR_REQ_RANGE);
-      const T* st = reinterpret_cast<const T*>(a.conv_state) + (ok ? slot : 0) * a.conv_stride_slot;
+      for (int q = 0; q < 3; ++q) {  // history rows t-3+q
+        const T* hv = reinterpret_cast<const T*>(&win[i + q]);
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const int64_t p = t - rs - 3 + k;  // position inside the request
-        if (p < 0) {
+        for (int e = 0; e < 4; ++e) h[q][e] = to_f(hv[e]);
+      }
+      if (t - rs < 3) {  // the first tokens of a request read its conv_state
+        const int64_t slot = a.req_pool_indices[b];
+        const bool ok = slot >= 0 && slot < a.num_slots;
+        if (!ok && c == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+        const T* st = reinterpret_cast<const T*>(a.conv_state) + (ok ? slot : 0) * a.conv_stride_slot;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) h[k][e] = ok ? to_f(st[(int64_t)(c + e) * 3 + 3 + p]) : 0.f;
+        for (int q = 0; q < 3; ++q) {
+          const int64_t p = t - rs - 3 + q;  // position inside the request
+          if (p < 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[q][e] = ok ? to_f(st[(int64_t)(c + e) * 3 + 3 + p]) : 0.f;
+          }
         }
       }
-    }
-    const T* xv = reinterpret_cast<const T*>(&win[i + 3]);
-    float acc[4];
+      const T* xv = reinterpret_cast<const T*>(&win[i + 3]);
+      float acc[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
-      acc[e] = fmaf(w[e][0], h[0][e], fmaf(w[e][1], h[1][e],
-                    fmaf(w[e][2], h[2][e], fmaf(w[e][3], to_f(xv[e]), bias[e]))));
-    // both roundings in pairs (one conversion per two channels)
-    uint32_t ow[2];
+      for (int e = 0; e < 4; ++e)
+        acc[e] = fmaf(w[e][0], h[0][e], fmaf(w[e][1], h[1][e],
+                      fmaf(w[e][2], h[2][e], fmaf(w[e][3], to_f(xv[e]), bias[e]))));
+      uint32_t ow[2];
 #pragma unroll
-    for (int e2 = 0; e2 < 2; ++e2) {
-      const uint32_t r = pack2_rn<T>(acc[2 * e2], acc[2 * e2 + 1]);
-      ow[e2] = pack2_rn<T>(silu_rt(unpack_lo<T>(r)), silu_rt(unpack_hi<T>(r)));
+      for (int e2 = 0; e2 < 2; ++e2) {
+        const uint32_t r = pack2_rn<T>(acc[2 * e2], acc[2 * e2 + 1]);
+        ow[e2] = pack2_rn<T>(silu_rt(unpack_lo<T>(r)), silu_rt(unpack_hi<T>(r)));
+      }
+      __stcs(reinterpret_cast<uint2*>(conv_out + t * conv_dim + c), make_uint2(ow[0], ow[1]));
     }
-    __stcs(reinterpret_cast<uint2*>(conv_out + t * conv_dim + c), make_uint2(ow[0], ow[1]));
+#pragma unroll
+    for (int r = 0; r < 3; ++r) win[r] = win[kConvVecTok + r];
+#pragma unroll
+    for (int r = 0; r < kConvVecTok; ++r) win[3 + r] = nxt[r];
   }
 }
 
@@ -2089,9 +2100,10 @@ cudaError_t launch_extend_t(const tf_gdn_args& a, void* ws, cudaStream_t s) {
                         a.qkv_stride_tok % 4 == 0 && (reinterpret_cast<uintptr_t>(a.qkv) & 7) == 0;
   if (conv_vec) {
     if constexpr (sizeof(T) == 2) {
+      constexpr int kSpan = kConvVecTok * kConvPipeBlocks;
       dim3 cg((conv_dim / 4 + kConvVecThreads - 1) / kConvVecThreads,
-              (unsigned)((a.num_tokens + kConvVecTok - 1) / kConvVecTok));
-      conv4_vec_kernel<T><<<cg, kConvVecThreads, 0, s>>>(a, w.start, (T*)w.conv_out);
+              (unsigned)((a.num_tokens + kSpan - 1) / kSpan));
+      conv4_pipe_kernel<T><<<cg, kConvVecThreads, 0, s>>>(a, w.start, (T*)w.conv_out);
     }
   } else if (a.conv_kernel == 4 && conv_dim % 2 == 0) {
     dim3 cg((conv_dim / 2 + kConvThreads - 1) / kConvThreads,
