@@ -348,3 +348,41 @@ def test_extend_at_config4_lengths_vs_oracle(growing):
     want = orc.reshape(t, -1) if growing else OA.output_gate(
         BF.round_f32(orc).reshape(t, -1), inp["gate"].reshape(t, -1), "sigmoid", "bf16")
     assert_close(out, want, "bf16", what=f"extend config-4 lengths growing={growing}")
+
+
+@pytest.mark.parametrize("d,hq,hkv", [(128, 16, 8), (256, 8, 1)])
+def test_extend_unaligned_gate_rows_vs_oracle(d, hq, hkv):
+    """A gate view whose head rows do not start on 16-byte boundaries (rows d + 1 elements apart,
+    one element into their buffer) takes the SM-pair kernel's element-by-element epilogue; the
+    aligned gate takes the vector one.  Both match the oracle at the bf16 bound."""
+    from tokenfactory_b200 import ops
+    reqs = [(250, 200), (5, 3)]
+    seq = [p + e for p, e in reqs]
+    ext = [e for _, e in reqs]
+    B = len(reqs)
+    spec = dict(dtype="bf16", hq=hq, hkv=hkv, d=d, seq=seq, ext=ext, req=[2, 0],
+                slots=sum(seq) + 11, rows=B + 2, cols=max(seq) + 5, seed=d + 5 * hq)
+    inp = C.attn_inputs(spec)
+    aligned = values(_run(inp, spec, gate_mode="silu"), "bf16").reshape(sum(ext), -1)
+    q = to_torch(inp["q"], "bf16")
+    kb, vb = to_torch(inp["k_buf"], "bf16"), to_torch(inp["v_buf"], "bf16")
+    r2t = to_torch(inp["req_to_token"], "bf16")
+    rpi, sl = to_torch(inp["req_pool_indices"], "bf16"), to_torch(inp["seq_lens"], "bf16")
+    el = to_torch(inp["extend_lens"], "bf16")
+    g = to_torch(inp["gate"], "bf16")
+    wide = torch.zeros((g.shape[0], hq, d + 1), dtype=g.dtype, device=g.device)
+    wide[:, :, 1:] = g
+    g_view = wide[:, :, 1:]
+    assert g_view.data_ptr() % 16 != 0 and g_view.stride(1) == d + 1
+    out = ops.paged_extend(q, kb, vb, r2t, rpi, sl, el, d ** -0.5, max(seq), max(ext), gate=g_view,
+                           gate_mode="silu")
+    torch.cuda.synchronize()
+    unaligned = values(out, "bf16").reshape(sum(ext), -1)
+    orc = OA.slot_based_attention(inp["q"], inp["k_buf"], inp["v_buf"], inp["req_to_token"],
+                                  inp["req_pool_indices"], inp["seq_lens"], inp["extend_lens"],
+                                  d ** -0.5, "bf16")
+    t = orc.shape[0]
+    want = OA.output_gate(BF.round_f32(orc).reshape(t, -1), inp["gate"].reshape(t, -1), "silu",
+                          "bf16")
+    assert_close(aligned, want, "bf16", what=f"extend d={d} aligned gate")
+    assert_close(unaligned, want, "bf16", what=f"extend d={d} unaligned gate")

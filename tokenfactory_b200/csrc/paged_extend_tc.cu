@@ -803,7 +803,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     // Output gate, off the softmax's critical path: once the last S MMA has completed (q_dead), the
     // Q region is free; each producer warp copies 32 gate rows of this CTA into it (whole rows,
-    // coalesced) while the last tiles still run.  Every producer thread reaches the closing barrier.
+    // coalesced; the 16-byte chunks XOR-swizzled by the row) while the last tiles still run.  Every
+    // producer thread reaches the closing barrier.
     const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
     const bool gated = a.gate_mode != TF_GATE_NONE && gate != nullptr && gate_vec(a);
     constexpr int kChunks = D / 8, kRowsPerInstr = 32 / kChunks;
@@ -816,7 +817,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int row = pw * 32 + i + gsub;
         const int ti = row / G, g = row - (row / G) * G;
         if (ti < n_tok)
-          cp_async16(base + row * (D * 2) + gch * 16,
+          cp_async16(base + row * (D * 2) + ((gch ^ (row & (kChunks - 1))) << 4),
                      gate + (q0 + ti) * a.gate_stride_tok + (int64_t)(h * G + g) * a.gate_stride_head + gch * 8);
       }
     }
@@ -999,72 +1000,97 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const uint32_t gstage = base;  // gate rows, staged in the Q region by the producers
     if (ok) ok = __all_sync(0xffffffffu, wait_l(fin, 0, abort, peer_abort));
     // ---- epilogue.  Once fin completed, no MMA reads Q or the ring any more: the two halves' row
-    // sums meet in the Q region, and O (normalised, bf16) is staged row-major in the ring with the
-    // 16-byte chunk index XOR-swizzled by the row, so that warps then walk whole rows: gate loads
-    // and output stores are full coalesced rows.  Every softmax thread reaches both barriers.
+    // sums meet in the ring.  Every softmax thread reaches every barrier of its path.
     float* l_part = reinterpret_cast<float*>(sbase + C::kOffRing + kRows * D * 2);  // after the O stage
     if (ok) l_part[half * kRows + r] = l_sum;
     named_barrier(5, kSmWarps * 32);
     const float l_tot = ok ? l_part[r] + l_part[kRows + r] : 0.f;
     const uint32_t stage = base + C::kOffRing;
-    if (ok) {
-      tc::fence_after_sync();
-      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+    if (vec) {
+      // 16-byte gate and output pieces: each thread writes its own row's half straight from TMEM,
+      // out = bf16(bf16(O / l) * bf16(act(gate))) (a bf16 x bf16 product is exact in fp32), with
+      // the gate row read from the producers' staging (16-byte chunks XOR-swizzled by the row, so
+      // the 32 rows of a warp read conflict-free)
+      named_barrier(6, (kSmWarps + kProducerWarps) * 32);  // gate rows are staged
+      if (ok) {
+        tc::fence_after_sync();
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        const int g = r - ri * G;
+        __nv_bfloat16* orow =
+            row_valid ? out + (q0 + ri) * a.out_stride_tok + (int64_t)(h * G + g) * a.out_stride_head +
+                            half * kOHalf
+                      : nullptr;
 #pragma unroll 1
-      for (int cc = 0; cc < kOHalf / 32; ++cc) {
-        float o[32];
-        tc::ld32(tmem + lane_base + C::kColO + half * kOHalf + cc * 32, o);
-        tc::wait_ld();
+        for (int cc = 0; cc < kOHalf / 32; ++cc) {
+          float o[32];
+          tc::ld32(tmem + lane_base + C::kColO + half * kOHalf + cc * 32, o);
+          uint32_t gw[4][4];
+          if (gated && row_valid) {
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2) {
-            const float x0 = l_tot > 0.f ? o[c8 * 8 + 2 * q2] * inv : NAN;
-            const float x1 = l_tot > 0.f ? o[c8 * 8 + 2 * q2 + 1] * inv : NAN;
-            __nv_bfloat162 pv = __floats2bfloat162_rn(x0, x1);
-            w[q2] = *reinterpret_cast<uint32_t*>(&pv);
+            for (int c8 = 0; c8 < 4; ++c8) {
+              const int chunk = (half * kOHalf + cc * 32) / 8 + c8;
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(gw[c8][0]), "=r"(gw[c8][1]), "=r"(gw[c8][2]), "=r"(gw[c8][3])
+                           : "r"(gstage + r * (D * 2) + ((chunk ^ (r & (kChunks - 1))) << 4)));
+            }
           }
-          const int chunk = (half * kOHalf + cc * 32 + c8 * 8) / 8;
-          const uint32_t dst = stage + r * (D * 2) + ((chunk ^ (r & (kChunks - 1))) << 4);
-          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(w[0]), "r"(w[1]),
-                       "r"(w[2]), "r"(w[3])
-                       : "memory");
+          tc::wait_ld();
+          if (row_valid) {
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              uint4 ov;
+              uint32_t* w = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+              for (int q2 = 0; q2 < 4; ++q2) {
+                const float x0 = l_tot > 0.f ? o[c8 * 8 + 2 * q2] * inv : NAN;
+                const float x1 = l_tot > 0.f ? o[c8 * 8 + 2 * q2 + 1] * inv : NAN;
+                __nv_bfloat162 pv = __floats2bfloat162_rn(x0, x1);
+                if (gated) {
+                  const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(&gw[c8][q2]);
+                  const __nv_bfloat162 av = __floats2bfloat162_rn(
+                      act_fast(__low2float(gv), a.gate_mode), act_fast(__high2float(gv), a.gate_mode));
+                  pv = __hmul2(pv, av);
+                }
+                w[q2] = *reinterpret_cast<uint32_t*>(&pv);
+              }
+              *reinterpret_cast<uint4*>(orow + cc * 32 + c8 * 8) = ov;
+            }
+          }
         }
       }
+    } else {
+      // unaligned gate or output rows: O (normalised, bf16) is staged row-major in the ring with
+      // the 16-byte chunk index XOR-swizzled by the row, then written element by element
+      if (ok) {
+        tc::fence_after_sync();
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < kOHalf / 32; ++cc) {
+          float o[32];
+          tc::ld32(tmem + lane_base + C::kColO + half * kOHalf + cc * 32, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+              const float x0 = l_tot > 0.f ? o[c8 * 8 + 2 * q2] * inv : NAN;
+              const float x1 = l_tot > 0.f ? o[c8 * 8 + 2 * q2 + 1] * inv : NAN;
+              __nv_bfloat162 pv = __floats2bfloat162_rn(x0, x1);
+              w[q2] = *reinterpret_cast<uint32_t*>(&pv);
+            }
+            const int chunk = (half * kOHalf + cc * 32 + c8 * 8) / 8;
+            const uint32_t dst = stage + r * (D * 2) + ((chunk ^ (r & (kChunks - 1))) << 4);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(w[0]), "r"(w[1]),
+                         "r"(w[2]), "r"(w[3])
+                         : "memory");
+          }
+        }
+      }
+      named_barrier(5, kSmWarps * 32);
+      named_barrier(6, (kSmWarps + kProducerWarps) * 32);  // the producers' closing barrier
     }
-    named_barrier(5, kSmWarps * 32);
-    named_barrier(6, (kSmWarps + kProducerWarps) * 32);  // gate rows are staged
-    // (cold code, run once per CTA: kept compact, since it is fetched after the main loop has
-    // filled the instruction cache)
-    if (ok && vec) {
-#pragma unroll 1
-      for (int i = 0; i < kRowIters; ++i) {
-        const int row = warp * kRowsPerWarp + i * kRowsPerInstr + sub;
-        const int ti = row / G, g = row - (row / G) * G;
-        if (ti >= n_tok) continue;
-        uint4 ov;
-        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(ov.x), "=r"(ov.y), "=r"(ov.z), "=r"(ov.w)
-                     : "r"(stage + row * (D * 2) + ((ch ^ (row & (kChunks - 1))) << 4)));
-        if (gated) {  // out = bf16(attn * bf16(act(gate))): a bf16 x bf16 product is exact in fp32
-          uint32_t gw[4];
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(gw[0]), "=r"(gw[1]), "=r"(gw[2]), "=r"(gw[3])
-                       : "r"(gstage + row * (D * 2) + ch * 16));
-          __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
-#pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2) {
-            const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(&gw[q2]);
-            const __nv_bfloat162 av = __floats2bfloat162_rn(act_fast(__low2float(gv), a.gate_mode),
-                                                            act_fast(__high2float(gv), a.gate_mode));
-            o2[q2] = __hmul2(o2[q2], av);
-          }
-        }
-        *reinterpret_cast<uint4*>(out + (q0 + ti) * a.out_stride_tok +
-                                  (int64_t)(h * G + g) * a.out_stride_head + ch * 8) = ov;
-      }
-    } else if (ok) {  // unaligned gate/output rows: element by element
+    if (!vec && ok) {
 #pragma unroll 1
       for (int i = 0; i < kRowIters; ++i) {
         const int row = warp * kRowsPerWarp + i * kRowsPerInstr + sub;
