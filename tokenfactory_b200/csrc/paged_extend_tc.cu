@@ -701,6 +701,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // producers: the slot-id chain of the first key tiles (the request's req_to_token row, then its
+  // entries) is requested before the set-up barrier, so that its two round trips overlap the set-up
+  // and the copies of Q.  Lane l < 16 takes key 64 rank + 16 pw + l (this CTA's K rows and V rows),
+  // lane l >= 16 key 64 (1 - rank) + 16 pw + l - 16 (V rows only): a warp's V rows include its K rows
+  constexpr int kPrefetch = 4;
+  int64_t raw_q[kPrefetch] = {0, 0, 0, 0};
+  const int64_t* r2t = a.req_to_token;
+  int my_key = 0;
+  if (warp >= kPrWarp0 && warp < kIssueWarp) {
+    const int pw = warp - kPrWarp0;
+    int64_t row = a.req_pool_indices[b];
+    if (row < 0 || row >= a.r2t_rows) {
+      if (tid == kPrWarp0 * 32 && rank == 0) record_err(a.err, TF_KERR_REQ_RANGE);
+      row = 0;
+    }
+    r2t = a.req_to_token + row * a.r2t_stride;
+    my_key = lane < 16 ? 64 * (int)rank + 16 * pw + lane : 64 * (1 - (int)rank) + 16 * pw + lane - 16;
+#pragma unroll
+    for (int i = 0; i < kPrefetch; ++i) {
+      int64_t key = (int64_t)i * kPBN + my_key;
+      if (key >= kv_end) key = (int64_t)i * kPBN;  // past the window: repeat the tile's first key
+      if (i < ntiles) raw_q[i] = r2t[key];
+    }
+  }
   if (warp == kIssueWarp) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)), "r"(C::kTmemCols)
@@ -732,27 +756,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       }
       cp_async_arrive_noinc(q_full);
     }
-    int64_t row = a.req_pool_indices[b];
-    if (row < 0 || row >= a.r2t_rows) {
-      if (tid == kPrWarp0 * 32 && rank == 0) record_err(a.err, TF_KERR_REQ_RANGE);
-      row = 0;
-    }
-    const int64_t* r2t = a.req_to_token + row * a.r2t_stride;
     const char* kbuf = (const char*)a.k_buffer + (int64_t)h * a.kv_stride_head * 2;
     const char* vbuf = (const char*)a.v_buffer + (int64_t)h * a.kv_stride_head * 2 + rank * D;
     const int64_t sstride = a.kv_stride_slot * 2;
-    // lane l < 16: key 64 rank + 16 pw + l (this CTA's K rows and V rows); lane l >= 16: key
-    // 64 (1 - rank) + 16 pw + l - 16 (V rows only): a warp's V rows include its K rows
-    const int my_key = lane < 16 ? 64 * (int)rank + 16 * pw + lane : 64 * (1 - (int)rank) + 16 * pw + lane - 16;
     auto raw_of = [&](int tile) -> int64_t {
       int64_t key = (int64_t)tile * kPBN + my_key;
       if (key >= kv_end) key = (int64_t)tile * kPBN;  // past the window: repeat the tile's first key
       return r2t[key];
     };
-    constexpr int kPrefetch = 4;
-    int64_t raw_q[kPrefetch];
-#pragma unroll
-    for (int i = 0; i < kPrefetch; ++i) raw_q[i] = i < ntiles ? raw_of(i) : 0;
     int slot = 0;
     uint32_t phase = 0;
     bool ok = true;
