@@ -99,9 +99,10 @@ _REASONS = {
 
 
 class ClockSampler:
-    """SM clocks and throttle reasons sampled while the timed region runs: NVML read every
-    0.5 ms from a thread (so that even a region of a few milliseconds is covered), with
-    nvidia-smi at 100 ms as the fallback when NVML cannot be loaded.  Reads only."""
+    """SM clocks and throttle reasons sampled while the timed region runs: NVML read back to back
+    from a thread (two calls a sample, about 0.7 ms; the calls release the GIL, so the thread keeps
+    sampling while the main thread waits for the device), with nvidia-smi at 100 ms as the
+    fallback when NVML cannot be loaded.  Reads only."""
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
@@ -109,20 +110,21 @@ class ClockSampler:
         self.lines = []
         self._stop = threading.Event()
         self._thread = None
+        self._max_mhz = 0
 
-    def _nvml_sample(self, handle, nv):
+    def _nvml_sample(self, handle, nv) -> bool:
         try:
-            mx = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
             sm = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
             bits = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
-            self.lines.append(f"{sm}, {mx}, 0, {bits:#x}")
+            self.lines.append(f"{sm}, {self._max_mhz}, 0, {bits:#x}")
+            return True
         except Exception:  # noqa: BLE001 - a failed read is just a missing sample
-            pass
+            return False
 
     def _nvml_loop(self, handle, nv):
         while not self._stop.is_set():
-            self._nvml_sample(handle, nv)
-            time.sleep(0.0005)
+            if not self._nvml_sample(handle, nv):
+                time.sleep(0.001)  # a failing read must not spin on the interpreter lock
 
     def __enter__(self):
         try:
@@ -130,6 +132,7 @@ class ClockSampler:
             nv.nvmlInit()
             idx = torch.cuda._get_nvml_device_index(self.gpu)
             handle = nv.nvmlDeviceGetHandleByIndex(idx)
+            self._max_mhz = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)  # fixed
             self._nvml = (handle, nv)
             self._thread = threading.Thread(target=self._nvml_loop, args=(handle, nv), daemon=True)
             self._thread.start()
